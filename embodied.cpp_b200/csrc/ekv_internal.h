@@ -1,0 +1,61 @@
+// ekv_internal.h -- host-side pool object and the kernel launchers shared by the C-ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <set>
+#include <vector>
+
+#include "../../include/ekv.h"
+#include "ekv_layout.cuh"
+
+struct ekv_pool {
+    ekv_pool_config cfg{};
+    ekv::PoolView view{};
+    void *dev_base = nullptr;
+    size_t bytes_total = 0, bytes_prefix = 0, bytes_suffix = 0;
+    std::set<int32_t> free_blocks;  // lowest index first
+    struct Seq {
+        bool live = false;
+        int32_t n_tokens = 0;
+        std::vector<int32_t> blocks;
+    };
+    std::vector<Seq> seqs;
+    std::set<int32_t> free_seq_ids;
+    std::vector<uint8_t> dirty;    // per sequence: table/length changed since the last sync
+    bool any_dirty = false;
+    int32_t *h_status = nullptr;   // pinned, 4 ints
+};
+
+namespace ekv {
+
+struct AttnArgs {
+    PoolView pool;
+    int32_t layer, n_batch, q_tokens, q_heads, group;
+    float scale_log2;  // scale * log2(e)
+    int32_t mask_flags, chunk_tokens, chunk_stride, window_chunks, q_chunk0;
+    int32_t suffix_len, out_dtype, use_prefix;
+    const int32_t *seq_ids, *prefix_len, *prefix_valid, *span_begin, *span_end;
+    const uint16_t *q;
+    void *out;
+    // key splitting (tensor-core kernel only)
+    int32_t n_splits;
+    float *ws_o;      // [units][128][D] unnormalised partial outputs
+    float *ws_ml;     // [units][128][2] running max (log2 domain) and sum
+};
+
+int launch_append(const PoolView &p, int layer, int n_batch, const int32_t *seq_ids,
+                  const int32_t *dst_pos, const int32_t *n_rows, const int32_t *src_row,
+                  int max_rows, const void *k, const void *v, cudaStream_t s);
+int launch_append_suffix(const PoolView &p, int layer, int n_batch, const int32_t *seq_ids,
+                         int n_rows, const void *k, const void *v, cudaStream_t s);
+int launch_gather(const PoolView &p, int layer, int seq, int pos0, int n_rows, int format,
+                  void *k_out, void *v_out, cudaStream_t s);
+int launch_gather_suffix(const PoolView &p, int layer, int seq, int n_rows, int format,
+                         void *k_out, void *v_out, cudaStream_t s);
+int launch_attention_simt(const AttnArgs &a, cudaStream_t s);
+int launch_attention_tc(const AttnArgs &a, cudaStream_t s);
+size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix);
+
+}  // namespace ekv

@@ -1,0 +1,90 @@
+// ekv_layout.cuh -- device-side layout of the paged KV pool, shared by every kernel.
+//
+// HBM layout (one cudaMalloc per pool, all regions 1024-byte aligned):
+//
+//   prefix arena  [n_layers][n_blocks][2 (K,V)][kv_heads] tiles
+//     bf16 tile : block_tokens x head_dim bf16 stored as [D*2/W chunks][block_tokens rows][W bytes]
+//                 with the tcgen05 shared-memory swizzle already applied (Swizzle<log2(W/16),4,3>,
+//                 W = 128, 64 or 32 bytes). One contiguous copy of a chunk lands in shared
+//                 memory as a canonical K-major operand (K) or MN-major operand (V) tile.
+//     Q8_0 tile : qs int8 [block_tokens][head_dim] followed by fp16 scales
+//                 [block_tokens][head_dim/32]; a gather re-interleaves them into ggml's
+//                 block_q8_0 {d, qs[32]} bytes.
+//   suffix arena  [n_layers][max_seqs][2][kv_heads] tiles of suffix_rows bf16 rows, in the
+//                 same swizzled bf16 tile layout (suffix_rows = suffix_tokens rounded up to 8).
+//   seq table     int32 block_tables[max_seqs][max_blocks_per_seq], int32 seq_lens[max_seqs]
+//   status word   int32[4]: [0] first error code, [1..3] details of that error
+#pragma once
+
+#include <cstdint>
+
+namespace ekv {
+
+struct PoolView {
+    uint8_t *prefix;          // prefix arena
+    uint8_t *suffix;          // suffix arena
+    int32_t *block_tables;    // [max_seqs][max_blocks_per_seq]
+    int32_t *seq_lens;        // [max_seqs]
+    int32_t *status;          // [4]
+    int32_t dtype;            // EKV_DTYPE_BF16 / EKV_DTYPE_Q8_0
+    int32_t block_tokens;
+    int32_t n_blocks;
+    int32_t kv_heads;
+    int32_t head_dim;
+    int32_t n_layers;
+    int32_t max_seqs;
+    int32_t max_blocks_per_seq;
+    int32_t suffix_rows;      // rows per suffix tile (multiple of 8), 0 = none
+    int32_t swz_bytes;        // W: row bytes of one swizzle chunk (128, 64 or 32)
+    int64_t tile_bytes;       // bytes of one (layer, block, kv, head) prefix tile
+    int64_t suffix_tile_bytes;// bytes of one (layer, seq, kv, head) suffix tile
+};
+
+// Error codes written into status[0] by kernels (first error wins).
+enum : int32_t {
+    DEV_ERR_BAD_BLOCK = 1,     // block-table entry outside [0, n_blocks)
+    DEV_ERR_BAD_SEQ = 2,       // sequence id outside [0, max_seqs)
+    DEV_ERR_BAD_POS = 3,       // position outside the sequence's blocks
+    DEV_ERR_TIMEOUT = 4,       // bounded mbarrier wait ran out
+};
+
+__host__ __device__ inline int swizzle_bytes_for(int head_dim) {
+    const int row = head_dim * 2;
+    return (row % 128 == 0) ? 128 : (row % 64 == 0) ? 64 : 32;
+}
+
+// Swizzle<B,4,3> on an offset inside a 1024-byte-aligned frame: the 16-byte unit index
+// (bits 4..4+B) is XORed with bits 7..7+B. mask = W/16 - 1.
+__host__ __device__ inline uint32_t swz(uint32_t off, uint32_t mask) {
+    return off ^ (((off >> 7) & mask) << 4);
+}
+
+// Byte offset of element (row, d) inside a bf16 tile with `rows` rows and chunk width W.
+__host__ __device__ inline uint32_t tile_elem_off(int row, int d, int rows, int W) {
+    const int byte = d * 2;
+    const int chunk = byte / W;
+    const int wb = byte - chunk * W;
+    return (uint32_t)chunk * (uint32_t)(rows * W) + swz((uint32_t)(row * W + wb), (uint32_t)(W / 16 - 1));
+}
+
+__host__ __device__ inline int64_t prefix_tile_index(const PoolView &p, int layer, int block, int kv,
+                                                      int head) {
+    return (((int64_t)layer * p.n_blocks + block) * 2 + kv) * p.kv_heads + head;
+}
+
+__host__ __device__ inline int64_t suffix_tile_index(const PoolView &p, int layer, int seq, int kv,
+                                                      int head) {
+    return (((int64_t)layer * p.max_seqs + seq) * 2 + kv) * p.kv_heads + head;
+}
+
+#ifdef __CUDACC__
+__device__ inline void report_error(int32_t *status, int32_t code, int32_t a, int32_t b, int32_t c) {
+    if (atomicCAS(status, 0, code) == 0) {
+        status[1] = a;
+        status[2] = b;
+        status[3] = c;
+    }
+}
+#endif
+
+}  // namespace ekv

@@ -1,0 +1,241 @@
+"""Python binding of libekv.so, the B200 paged KV-cache + masked-attention library.
+
+A thin ctypes mirror of include/ekv.h for tests, the benchmark and Python callers: the pool
+(`Pool`), sequence/block-table management, append / gather, and attention. Device buffers are
+torch CUDA tensors (passed by data pointer); every call is asynchronous on the given (or
+current) torch stream, like the C-ABI.
+
+There is no fallback: if libekv.so is missing or fails to load, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libekv.so")
+
+OK = 0
+ERR_INVALID_ARG, ERR_CUDA, ERR_POOL_EXHAUSTED, ERR_NO_SEQ = -1, -2, -3, -4
+ERR_RANGE, ERR_UNSUPPORTED, ERR_DEVICE, ERR_TIMEOUT, ERR_ALLOC = -5, -6, -7, -8, -9
+
+DTYPE_F32, DTYPE_F16, DTYPE_Q8_0, DTYPE_BF16 = 0, 1, 8, 30
+GATHER_NATIVE, GATHER_F32 = 0, 1
+MASK_SUFFIX_CAUSAL = 1 << 0
+MASK_SUFFIX_PREFIX_LM = 1 << 1
+MASK_SPAN_ONLY = 1 << 2
+MASK_SPAN_EXCLUDE = 1 << 3
+MASK_BLOCK_CAUSAL = 1 << 4
+ALGO_TC, ALGO_SIMT = 0, 1
+
+# Device-side error codes written into the pool status word by kernels.
+DEV_ERR_BAD_BLOCK, DEV_ERR_BAD_SEQ, DEV_ERR_BAD_POS, DEV_ERR_TIMEOUT = 1, 2, 3, 4
+
+
+class PoolConfig(C.Structure):
+    _fields_ = [("device", C.c_int32), ("dtype", C.c_int32), ("block_tokens", C.c_int32),
+                ("n_blocks", C.c_int32), ("kv_heads", C.c_int32), ("head_dim", C.c_int32),
+                ("n_layers", C.c_int32), ("max_seqs", C.c_int32), ("max_blocks_per_seq", C.c_int32),
+                ("suffix_tokens", C.c_int32)]
+
+
+class PoolInfo(C.Structure):
+    _fields_ = [("bytes_total", C.c_size_t), ("bytes_prefix", C.c_size_t),
+                ("bytes_suffix", C.c_size_t), ("block_bytes", C.c_size_t),
+                ("free_blocks", C.c_int32), ("live_seqs", C.c_int32),
+                ("prefix_base", C.c_void_p), ("suffix_base", C.c_void_p),
+                ("block_tables", C.c_void_p), ("seq_lens", C.c_void_p)]
+
+
+class AttnParams(C.Structure):
+    _fields_ = [("layer", C.c_int32), ("n_batch", C.c_int32), ("q_tokens", C.c_int32),
+                ("q_heads", C.c_int32), ("scale", C.c_float), ("mask_flags", C.c_int32),
+                ("chunk_tokens", C.c_int32), ("chunk_stride", C.c_int32),
+                ("window_chunks", C.c_int32), ("q_chunk0", C.c_int32), ("suffix_len", C.c_int32),
+                ("out_dtype", C.c_int32), ("use_prefix", C.c_int32), ("reserved", C.c_int32),
+                ("seq_ids", C.c_void_p), ("prefix_len", C.c_void_p), ("prefix_valid", C.c_void_p),
+                ("span_begin", C.c_void_p), ("span_end", C.c_void_p)]
+
+
+# Every symbol include/ekv.h declares; tests check that the library exports all of them.
+EXPORTED = [
+    "ekv_pool_create", "ekv_pool_destroy", "ekv_pool_get_info", "ekv_pool_status", "ekv_pool_sync",
+    "ekv_seq_create", "ekv_seq_free", "ekv_seq_resize", "ekv_seq_set_blocks", "ekv_seq_evict_front",
+    "ekv_seq_get", "ekv_append", "ekv_append_suffix", "ekv_gather", "ekv_gather_suffix",
+    "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
+    "ekv_strerror",
+]
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python embodied.cpp_b200/build.py`"
+                          " (there is no CPU fallback)")
+    L = C.CDLL(LIB_PATH)
+    vp, i32, pi32 = C.c_void_p, C.c_int32, C.POINTER(C.c_int32)
+    sig = {
+        "ekv_pool_create": ([C.POINTER(PoolConfig), C.POINTER(vp)], C.c_int),
+        "ekv_pool_destroy": ([vp], C.c_int),
+        "ekv_pool_get_info": ([vp, C.POINTER(PoolInfo)], C.c_int),
+        "ekv_pool_status": ([vp, pi32, vp], C.c_int),
+        "ekv_pool_sync": ([vp, vp], C.c_int),
+        "ekv_seq_create": ([vp, pi32], C.c_int),
+        "ekv_seq_free": ([vp, i32], C.c_int),
+        "ekv_seq_resize": ([vp, i32, i32], C.c_int),
+        "ekv_seq_set_blocks": ([vp, i32, pi32, i32, i32], C.c_int),
+        "ekv_seq_evict_front": ([vp, i32, i32], C.c_int),
+        "ekv_seq_get": ([vp, i32, pi32, pi32, pi32, i32], C.c_int),
+        "ekv_append": ([vp, i32, i32, vp, vp, vp, vp, i32, vp, vp, vp], C.c_int),
+        "ekv_append_suffix": ([vp, i32, i32, vp, i32, vp, vp, vp], C.c_int),
+        "ekv_gather": ([vp, i32, i32, i32, i32, i32, vp, vp, vp], C.c_int),
+        "ekv_gather_suffix": ([vp, i32, i32, i32, i32, vp, vp, vp], C.c_int),
+        "ekv_attention_workspace_size": ([vp, C.POINTER(AttnParams)], C.c_size_t),
+        "ekv_attention": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, vp], C.c_int),
+        "ekv_attention_algo": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, i32, vp], C.c_int),
+        "ekv_version": ([], C.c_char_p),
+        "ekv_strerror": ([C.c_int], C.c_char_p),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    return L
+
+
+lib = _load()
+
+
+class EkvError(RuntimeError):
+    def __init__(self, code, what):
+        super().__init__(f"{what}: {lib.ekv_strerror(code).decode()} ({code})")
+        self.code = code
+
+
+def check(code, what="ekv"):
+    if code != OK:
+        raise EkvError(code, what)
+    return code
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+@dataclass
+class SeqView:
+    n_tokens: int
+    blocks: list
+
+
+class Pool:
+    """A paged KV pool on one device (ekv_pool_create / ekv_pool_destroy)."""
+
+    def __init__(self, *, device=0, dtype=DTYPE_BF16, block_tokens=16, n_blocks=1024, kv_heads=1,
+                 head_dim=256, n_layers=1, max_seqs=64, max_blocks_per_seq=64, suffix_tokens=0):
+        self.cfg = PoolConfig(device, dtype, block_tokens, n_blocks, kv_heads, head_dim, n_layers,
+                              max_seqs, max_blocks_per_seq, suffix_tokens)
+        h = C.c_void_p()
+        check(lib.ekv_pool_create(C.byref(self.cfg), C.byref(h)), "ekv_pool_create")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            check(lib.ekv_pool_destroy(self.h), "ekv_pool_destroy")
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self) -> PoolInfo:
+        i = PoolInfo()
+        check(lib.ekv_pool_get_info(self.h, C.byref(i)), "ekv_pool_get_info")
+        return i
+
+    def status(self, stream=None) -> int:
+        code = C.c_int32()
+        check(lib.ekv_pool_status(self.h, C.byref(code), _stream(stream)), "ekv_pool_status")
+        return code.value
+
+    def sync(self, stream=None):
+        check(lib.ekv_pool_sync(self.h, _stream(stream)), "ekv_pool_sync")
+
+    # ---- sequences ----
+    def seq_create(self) -> int:
+        s = C.c_int32()
+        check(lib.ekv_seq_create(self.h, C.byref(s)), "ekv_seq_create")
+        return s.value
+
+    def seq_free(self, seq):
+        check(lib.ekv_seq_free(self.h, seq), "ekv_seq_free")
+
+    def seq_resize(self, seq, n_tokens):
+        check(lib.ekv_seq_resize(self.h, seq, n_tokens), "ekv_seq_resize")
+
+    def seq_set_blocks(self, seq, blocks, n_tokens):
+        arr = (C.c_int32 * len(blocks))(*blocks)
+        check(lib.ekv_seq_set_blocks(self.h, seq, arr, len(blocks), n_tokens), "ekv_seq_set_blocks")
+
+    def seq_evict_front(self, seq, n_blocks):
+        check(lib.ekv_seq_evict_front(self.h, seq, n_blocks), "ekv_seq_evict_front")
+
+    def seq_get(self, seq) -> SeqView:
+        nt, nb = C.c_int32(), C.c_int32()
+        check(lib.ekv_seq_get(self.h, seq, C.byref(nt), C.byref(nb), None, 0), "ekv_seq_get")
+        arr = (C.c_int32 * max(1, nb.value))()
+        check(lib.ekv_seq_get(self.h, seq, None, None, arr, nb.value), "ekv_seq_get")
+        return SeqView(nt.value, list(arr)[: nb.value])
+
+    # ---- data ----
+    def append(self, layer, seq_ids, dst_pos, n_rows, src_row, max_rows, k, v, stream=None):
+        check(lib.ekv_append(self.h, layer, seq_ids.numel(), _ptr(seq_ids), _ptr(dst_pos),
+                             _ptr(n_rows), _ptr(src_row), max_rows, _ptr(k), _ptr(v),
+                             _stream(stream)), "ekv_append")
+
+    def append_suffix(self, layer, seq_ids, k, v, stream=None):
+        n_rows = k.shape[1]
+        check(lib.ekv_append_suffix(self.h, layer, seq_ids.numel(), _ptr(seq_ids), n_rows, _ptr(k),
+                                    _ptr(v), _stream(stream)), "ekv_append_suffix")
+
+    def gather(self, layer, seq, pos0, n_rows, fmt, k_out, v_out, stream=None):
+        check(lib.ekv_gather(self.h, layer, seq, pos0, n_rows, fmt, _ptr(k_out), _ptr(v_out),
+                             _stream(stream)), "ekv_gather")
+
+    def gather_suffix(self, layer, seq, n_rows, fmt, k_out, v_out, stream=None):
+        check(lib.ekv_gather_suffix(self.h, layer, seq, n_rows, fmt, _ptr(k_out), _ptr(v_out),
+                                    _stream(stream)), "ekv_gather_suffix")
+
+    def attention_params(self, *, layer, seq_ids, q_tokens, q_heads, scale, mask_flags=0,
+                         chunk_tokens=0, chunk_stride=0, window_chunks=0, q_chunk0=0,
+                         suffix_len=0, out_dtype=DTYPE_BF16, use_prefix=True, prefix_len=None,
+                         prefix_valid=None, span_begin=None, span_end=None) -> AttnParams:
+        p = AttnParams(layer, seq_ids.numel(), q_tokens, q_heads, scale, mask_flags, chunk_tokens,
+                       chunk_stride, window_chunks, q_chunk0, suffix_len, out_dtype,
+                       1 if use_prefix else 0, 0, seq_ids.data_ptr(),
+                       None if prefix_len is None else prefix_len.data_ptr(),
+                       None if prefix_valid is None else prefix_valid.data_ptr(),
+                       None if span_begin is None else span_begin.data_ptr(),
+                       None if span_end is None else span_end.data_ptr())
+        p._keep = (seq_ids, prefix_len, prefix_valid, span_begin, span_end)
+        return p
+
+    def workspace_size(self, params: AttnParams) -> int:
+        return lib.ekv_attention_workspace_size(self.h, C.byref(params))
+
+    def attention(self, params: AttnParams, q, out, workspace=None, algo=ALGO_TC, stream=None):
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        check(lib.ekv_attention_algo(self.h, C.byref(params), _ptr(q), _ptr(out), _ptr(workspace),
+                                     ws_bytes, algo, _stream(stream)), "ekv_attention")
+
+
+def version() -> str:
+    return lib.ekv_version().decode()

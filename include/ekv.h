@@ -1,0 +1,201 @@
+/*
+ * ekv.h -- C-ABI of the B200 paged KV-cache + masked-attention library (libekv.so).
+ *
+ * The library is the GPU backend for the denoise-loop attention of Embodied.cpp: action-chunk
+ * (or video-chunk) queries attending over a cached prefix KV. It replaces, in the reference
+ * (paths inside the Embodied.cpp project):
+ *   - the per-step prefix/suffix concat + permute copies        models/pi05.cpp:406-412
+ *   - the attention triple mul_mat(K,Q) / soft_max_ext / mul_mat(V,attn)
+ *                                                              models/pi05.cpp:414-421,
+ *                                                              models/groot_n1.cpp:346-363
+ *   - ggml_flash_attn_ext with a concatenated prefix            models/hy_vla.cpp:1067-1076
+ *   - the slot KV store + device kernels of LingBot-VA          models/lingbot_va.cpp:8740-8997,
+ *                                                              kernels/lingbot/lingbot_flex_attn_cuda.h:13-266
+ *
+ * Conventions (kept from kernels/lingbot/lingbot_flex_attn_cuda.h:13-266): plain C, caller-owned
+ * device buffers, asynchronous launches on the given stream, an int status return
+ * (0 = success, negative = error). Launch-time validation errors return before anything is
+ * enqueued. Errors found by kernels (bad block ids, out-of-range positions, wait budgets) are
+ * written to the pool's device status word and read with ekv_pool_status().
+ *
+ * Threading: one pool per device; calls on one pool are not re-entrant (the caller serialises,
+ * as the reference server's single request loop does, serving/vla-server.cpp:240-523).
+ * Different pools/devices are independent.
+ */
+#ifndef EKV_H
+#define EKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ekv_stream_t; /* same type as cudaStream_t; NULL = legacy stream */
+
+/* ---- status codes ---- */
+#define EKV_OK 0
+#define EKV_ERR_INVALID_ARG (-1)  /* bad pointer, size or configuration                */
+#define EKV_ERR_CUDA (-2)         /* a CUDA runtime call failed                        */
+#define EKV_ERR_POOL_EXHAUSTED (-3)/* not enough free blocks; pool left unchanged       */
+#define EKV_ERR_NO_SEQ (-4)       /* sequence id unknown or not live                   */
+#define EKV_ERR_RANGE (-5)        /* position / length outside the sequence or slot    */
+#define EKV_ERR_UNSUPPORTED (-6)  /* shape or dtype this build does not handle         */
+#define EKV_ERR_DEVICE (-7)       /* a kernel reported a bad index (see ekv_pool_status) */
+#define EKV_ERR_TIMEOUT (-8)      /* a kernel's bounded wait ran out                   */
+#define EKV_ERR_ALLOC (-9)        /* device or host allocation failed                  */
+
+/* ---- dtypes (values follow ggml's enum ggml_type where one exists) ---- */
+#define EKV_DTYPE_F32 0
+#define EKV_DTYPE_F16 1
+#define EKV_DTYPE_Q8_0 8   /* ggml block_q8_0: {fp16 d; int8 qs[32]}, gguf-py quants.py:378-401 */
+#define EKV_DTYPE_BF16 30
+
+/* ---- pool ---- */
+typedef struct ekv_pool_config {
+    int32_t device;             /* CUDA device ordinal                                      */
+    int32_t dtype;              /* paged prefix storage: EKV_DTYPE_BF16 or EKV_DTYPE_Q8_0    */
+    int32_t block_tokens;       /* tokens per block: multiple of 8, at most 256              */
+    int32_t n_blocks;           /* physical blocks per layer                                */
+    int32_t kv_heads;           /* Hkv                                                       */
+    int32_t head_dim;           /* D: multiple of 16 (bf16) or 32 (Q8_0), at most 256        */
+    int32_t n_layers;
+    int32_t max_seqs;           /* sequence slots                                           */
+    int32_t max_blocks_per_seq; /* block-table width                                        */
+    int32_t suffix_tokens;      /* bf16 suffix slot per (sequence, layer); 0 = no slots      */
+} ekv_pool_config;
+
+typedef struct ekv_pool ekv_pool;
+
+typedef struct ekv_pool_info {
+    size_t bytes_total;         /* device bytes owned by the pool                           */
+    size_t bytes_prefix;        /* paged block arena                                        */
+    size_t bytes_suffix;        /* suffix slot arena                                        */
+    size_t block_bytes;         /* bytes of one (layer, block) for K and V of all heads      */
+    int32_t free_blocks;
+    int32_t live_seqs;
+    void *prefix_base;          /* device pointers, for tests and integration               */
+    void *suffix_base;
+    int32_t *block_tables;      /* device int32 [max_seqs][max_blocks_per_seq]               */
+    int32_t *seq_lens;          /* device int32 [max_seqs] token length of each sequence     */
+} ekv_pool_info;
+
+/* Create a pool on cfg->device. Replaces the per-layer cache tensors of the reference
+ * (pi0.5 graph tensors models/pi05.cpp:833-839; LingBotKVCache::init
+ * models/lingbot_va.cpp:8751-8763). Device memory is zeroed. */
+int ekv_pool_create(const ekv_pool_config *cfg, ekv_pool **out);
+int ekv_pool_destroy(ekv_pool *pool);
+int ekv_pool_get_info(const ekv_pool *pool, ekv_pool_info *info);
+/* Read (and clear) the device status word: *code receives EKV_OK or the first kernel error. */
+int ekv_pool_status(ekv_pool *pool, int32_t *code, ekv_stream_t stream);
+/* Upload host-side block tables / lengths changed since the last sync (stream-ordered). */
+int ekv_pool_sync(ekv_pool *pool, ekv_stream_t stream);
+
+/* ---- sequences and block tables ----
+ * Blocks are handed out lowest free index first, the order LingBotKVCache::allocate_slots_into
+ * uses for free slots (models/lingbot_va.cpp:8803-8805, :8826-8829). */
+int ekv_seq_create(ekv_pool *pool, int32_t *seq_id);
+/* Return all blocks of the sequence to the free list (block reuse after request completion). */
+int ekv_seq_free(ekv_pool *pool, int32_t seq_id);
+/* Grow the sequence to n_tokens (allocating blocks); n_tokens below the length truncates and
+ * frees whole trailing blocks. Fails with EKV_ERR_POOL_EXHAUSTED leaving the pool unchanged. */
+int ekv_seq_resize(ekv_pool *pool, int32_t seq_id, int32_t n_tokens);
+/* Install an explicit block table (e.g. a shuffled one); the blocks must be free. */
+int ekv_seq_set_blocks(ekv_pool *pool, int32_t seq_id, const int32_t *blocks, int32_t n_blocks,
+                       int32_t n_tokens);
+/* Drop the oldest n_blocks blocks of the sequence (oldest-chunk eviction of a sliding window,
+ * the role of LingBotKVCache::allocate_slots_into's oldest-id eviction,
+ * models/lingbot_va.cpp:8806-8825). Later tokens move down by n_blocks*block_tokens. */
+int ekv_seq_evict_front(ekv_pool *pool, int32_t seq_id, int32_t n_blocks);
+/* Host view of a sequence: length, block count, and up to `cap` block ids. */
+int ekv_seq_get(const ekv_pool *pool, int32_t seq_id, int32_t *n_tokens, int32_t *n_blocks,
+                int32_t *blocks, int32_t cap);
+
+/* ---- data operations (device pointers, stream-ordered) ---- */
+
+/* Append rows of K and V (bf16 [rows][kv_heads][head_dim]) into the paged prefix of layer
+ * `layer`. For batch element i (device int32 arrays of n_batch entries): sequence seq_ids[i],
+ * destination position dst_pos[i], n_rows[i] rows taken from row src_row[i] of k/v.
+ * max_rows bounds every n_rows[i]. Q8_0 pools quantise on write (gguf-py rule, bit-exact).
+ * Replaces ggml_concat of the prefix (models/pi05.cpp:406-407) and
+ * lingbot_runtime_kv_update_f32 (kernels/lingbot/lingbot_flex_attn_cuda.cu:626-649,900-917). */
+int ekv_append(ekv_pool *pool, int32_t layer, int32_t n_batch, const int32_t *seq_ids,
+               const int32_t *dst_pos, const int32_t *n_rows, const int32_t *src_row,
+               int32_t max_rows, const void *k, const void *v, ekv_stream_t stream);
+
+/* Write n_rows bf16 rows per batch element into the suffix slot of (seq_ids[i], layer):
+ * k/v are [n_batch][n_rows][kv_heads][head_dim]. The suffix is the per-step part of the keys
+ * (the action tokens joined to the prefix by models/pi05.cpp:406-407 every layer-step). */
+int ekv_append_suffix(ekv_pool *pool, int32_t layer, int32_t n_batch, const int32_t *seq_ids,
+                      int32_t n_rows, const void *k, const void *v, ekv_stream_t stream);
+
+#define EKV_GATHER_NATIVE 0   /* bf16 pool: the stored bf16; Q8_0 pool: ggml block_q8_0 bytes */
+#define EKV_GATHER_F32 1      /* values as f32 (dequantised for Q8_0)                          */
+
+/* Copy rows [pos0, pos0+n_rows) of one sequence's paged prefix (layer `layer`) into k_out /
+ * v_out, laid out [n_rows][kv_heads][head_dim] (NATIVE Q8_0: [n_rows][kv_heads][head_dim/32]
+ * blocks of 34 bytes). Replaces LingBotKVCache::compact_valid / lingbot_runtime_kv_gather_f32
+ * (models/lingbot_va.cpp:8974-8996, kernels/lingbot/lingbot_flex_attn_cuda.cu:875-898). */
+int ekv_gather(ekv_pool *pool, int32_t layer, int32_t seq_id, int32_t pos0, int32_t n_rows,
+               int32_t format, void *k_out, void *v_out, ekv_stream_t stream);
+/* Same for the bf16 suffix slot (format NATIVE = bf16, F32 = f32). */
+int ekv_gather_suffix(ekv_pool *pool, int32_t layer, int32_t seq_id, int32_t n_rows,
+                      int32_t format, void *k_out, void *v_out, ekv_stream_t stream);
+
+/* ---- masked attention over the cache ---- */
+#define EKV_MASK_SUFFIX_CAUSAL (1 << 0)    /* models/smolvla.cpp:718-720                    */
+#define EKV_MASK_SUFFIX_PREFIX_LM (1 << 1) /* row 0 sees suffix key 0 only, hy_vla.cpp:2355-2367 */
+#define EKV_MASK_SPAN_ONLY (1 << 2)        /* GR00T image mask, groot_n1.cpp:717            */
+#define EKV_MASK_SPAN_EXCLUDE (1 << 3)     /* GR00T text mask, groot_n1.cpp:716             */
+#define EKV_MASK_BLOCK_CAUSAL (1 << 4)     /* chunked prefix, causal across chunks + window */
+
+typedef struct ekv_attn_params {
+    int32_t layer;
+    int32_t n_batch;        /* B                                                           */
+    int32_t q_tokens;       /* Tq (query tokens per batch element)                         */
+    int32_t q_heads;        /* Hq, a multiple of the pool's kv_heads (MQA / GQA / MHA)       */
+    float scale;            /* softmax scale, 1/sqrt(head_dim) in every reference model      */
+    int32_t mask_flags;     /* EKV_MASK_* bits                                              */
+    int32_t chunk_tokens;   /* BLOCK_CAUSAL: valid tokens per chunk                          */
+    int32_t chunk_stride;   /* BLOCK_CAUSAL: key positions per chunk (>= chunk_tokens)       */
+    int32_t window_chunks;  /* BLOCK_CAUSAL: visible chunks, the query's own included        */
+    int32_t q_chunk0;       /* BLOCK_CAUSAL: chunk index (in key positions) of query token 0 */
+    int32_t suffix_len;     /* suffix-slot keys after the prefix (0 = none)                  */
+    int32_t out_dtype;      /* EKV_DTYPE_BF16 or EKV_DTYPE_F32                               */
+    int32_t use_prefix;     /* 0: attend the suffix only (self-attention layers)             */
+    int32_t reserved;
+    /* device int32 arrays of n_batch entries; NULL selects the default                    */
+    const int32_t *seq_ids;      /* required                                               */
+    const int32_t *prefix_len;   /* prefix keys used; default: the sequence length          */
+    const int32_t *prefix_valid; /* keys >= prefix_valid are padding; default: prefix_len   */
+    const int32_t *span_begin;   /* span for SPAN_ONLY / SPAN_EXCLUDE; default: empty       */
+    const int32_t *span_end;
+} ekv_attn_params;
+
+/* Bytes of workspace that lets ekv_attention split long key ranges across CTAs; 0 means the
+ * call never needs any. */
+size_t ekv_attention_workspace_size(const ekv_pool *pool, const ekv_attn_params *p);
+
+/* out[b][t][h][:] = softmax(scale * q.K^T + mask) V over the prefix keys of seq_ids[b] in
+ * layer p->layer followed by p->suffix_len suffix-slot keys. q is bf16 [B][Tq][Hq][D]; out is
+ * [B][Tq][Hq][D] in p->out_dtype. q head h reads kv head h / (Hq/Hkv), the ggml broadcast of
+ * mul_mat (models/pi05.cpp:414). Rows without a visible key are 0
+ * (models/lingbot_va.cpp:9503-9506). `workspace` may be NULL (no key splitting).
+ * Replaces models/pi05.cpp:410-421 and ggml_flash_attn_ext (models/hy_vla.cpp:1075). */
+int ekv_attention(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
+                  void *workspace, size_t workspace_bytes, ekv_stream_t stream);
+
+#define EKV_ALGO_TC 0     /* tcgen05 tensor-core kernel (default)                           */
+#define EKV_ALGO_SIMT 1   /* one-warp-per-row CUDA-core kernel, kept as a GPU cross-check   */
+int ekv_attention_algo(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
+                       void *workspace, size_t workspace_bytes, int32_t algo,
+                       ekv_stream_t stream);
+
+const char *ekv_version(void);
+const char *ekv_strerror(int code);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EKV_H */

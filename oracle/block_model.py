@@ -1,0 +1,92 @@
+"""Reference model of the pool's block bookkeeping. TEST INFRASTRUCTURE ONLY.
+
+Restates, at block granularity, the slot policy of LingBotKVCache
+(models/lingbot_va.cpp:8793-8831 of Embodied.cpp):
+  * free slots are handed out in ascending index order (`free` is built ascending, :8803-8805,
+    and re-sorted after evictions, :8826; `slots.assign(free.begin(), ...)`, :8829);
+  * when a window is full the oldest entries are evicted first (:8806-8825). In the paged pool
+    each sequence's block table is ordered oldest-first, so oldest-chunk eviction drops blocks
+    from the front of the table;
+  * a request that cannot be satisfied changes nothing and reports failure (:8791-8792,
+    :8827-8828).
+Sequence slots follow the same lowest-free-first rule. Lengths are in tokens.
+"""
+from __future__ import annotations
+
+
+class PoolModel:
+    def __init__(self, n_blocks: int, block_tokens: int, max_seqs: int, max_blocks_per_seq: int):
+        self.bt = block_tokens
+        self.free = set(range(n_blocks))
+        self.n_blocks = n_blocks
+        self.max_bps = max_blocks_per_seq
+        self.free_seqs = set(range(max_seqs))
+        self.seqs: dict[int, dict] = {}
+
+    def _need(self, n_tokens):
+        return (n_tokens + self.bt - 1) // self.bt
+
+    def seq_create(self):
+        if not self.free_seqs:
+            return None
+        s = min(self.free_seqs)
+        self.free_seqs.remove(s)
+        self.seqs[s] = {"n": 0, "blocks": []}
+        return s
+
+    def seq_free(self, s):
+        if s not in self.seqs:
+            return False
+        self.free.update(self.seqs[s]["blocks"])
+        del self.seqs[s]
+        self.free_seqs.add(s)
+        return True
+
+    def seq_resize(self, s, n_tokens):
+        if s not in self.seqs:
+            return "no_seq"
+        q = self.seqs[s]
+        need = self._need(n_tokens)
+        if need > self.max_bps:
+            return "range"
+        have = len(q["blocks"])
+        if need > have:
+            if len(self.free) < need - have:
+                return "exhausted"
+            for _ in range(need - have):
+                b = min(self.free)
+                self.free.remove(b)
+                q["blocks"].append(b)
+        else:
+            self.free.update(q["blocks"][need:])
+            del q["blocks"][need:]
+        q["n"] = n_tokens
+        return "ok"
+
+    def seq_evict_front(self, s, n):
+        if s not in self.seqs:
+            return "no_seq"
+        q = self.seqs[s]
+        if n < 0 or n > len(q["blocks"]):
+            return "range"
+        self.free.update(q["blocks"][:n])
+        del q["blocks"][:n]
+        q["n"] = max(0, q["n"] - n * self.bt)
+        return "ok"
+
+    def seq_set_blocks(self, s, blocks, n_tokens):
+        if s not in self.seqs:
+            return "no_seq"
+        if len(blocks) > self.max_bps or self._need(n_tokens) > len(blocks):
+            return "range"
+        q = self.seqs[s]
+        own = set(q["blocks"])
+        if len(set(blocks)) != len(blocks) or any(b < 0 or b >= self.n_blocks for b in blocks):
+            return "invalid"
+        if any(b not in own and b not in self.free for b in blocks):
+            return "exhausted"
+        self.free.update(q["blocks"])
+        q["blocks"] = list(blocks)
+        self.free.difference_update(blocks)
+        q["n"] = n_tokens
+        return "ok"

@@ -1,0 +1,192 @@
+"""ctypes binding of the CPU oracle (libekv_oracle.so). TEST INFRASTRUCTURE ONLY.
+
+The oracle restates the reference's arithmetic for the denoise-loop attention path on the CPU
+(see ekv_oracle.h for the reference lines). It is the parity checker for tests/, for
+__graft_entry__.smoke(), and the CPU baseline timed by bench.py. The product library
+(embodied.cpp_b200/ekv.py over libekv.so) never imports this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libekv_oracle.so")
+
+MASK_SUFFIX_CAUSAL = 1 << 0
+MASK_SUFFIX_PREFIX_LM = 1 << 1
+MASK_SPAN_ONLY = 1 << 2
+MASK_SPAN_EXCLUDE = 1 << 3
+MASK_BLOCK_CAUSAL = 1 << 4
+
+
+class Seq(C.Structure):
+    _fields_ = [("n_prefix", C.c_int32), ("prefix_valid", C.c_int32),
+                ("span_begin", C.c_int32), ("span_end", C.c_int32), ("n_suffix", C.c_int32)]
+
+
+class Mask(C.Structure):
+    _fields_ = [("flags", C.c_int32), ("chunk_tokens", C.c_int32), ("chunk_stride", C.c_int32),
+                ("window_chunks", C.c_int32), ("q_chunk0", C.c_int32)]
+
+
+class AttnArgs(C.Structure):
+    _fields_ = [("B", C.c_int32), ("Tq", C.c_int32), ("Hq", C.c_int32), ("Hkv", C.c_int32),
+                ("D", C.c_int32), ("Lk_max", C.c_int32), ("scale", C.c_float),
+                ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p),
+                ("dense_mask", C.c_void_p), ("seqs", C.c_void_p), ("mask", Mask),
+                ("out", C.c_void_p)]
+
+
+class CacheArgs(C.Structure):
+    _fields_ = [("B", C.c_int32), ("Tq", C.c_int32), ("Hq", C.c_int32), ("Hkv", C.c_int32),
+                ("D", C.c_int32), ("n_layers", C.c_int32), ("kv_is_q8", C.c_int32),
+                ("max_prefix", C.c_int32), ("n_suffix", C.c_int32), ("scale", C.c_float),
+                ("n_prefix", C.c_void_p), ("prefix_valid", C.c_void_p),
+                ("prefix_k", C.c_void_p), ("prefix_v", C.c_void_p),
+                ("suffix_k", C.c_void_p), ("suffix_v", C.c_void_p),
+                ("q", C.c_void_p), ("n_calls", C.c_int32), ("out", C.c_void_p)]
+
+
+_lib = None
+
+
+def build():
+    """Compile libekv_oracle.so with the committed Makefile (gcc, no fast-math)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH) or (
+                os.path.getmtime(LIB_PATH) < os.path.getmtime(os.path.join(HERE, "ekv_oracle.c"))):
+            build()
+        L = C.CDLL(LIB_PATH)
+        L.ekvo_f32_to_bf16.restype = C.c_uint16
+        L.ekvo_f32_to_bf16.argtypes = [C.c_float]
+        L.ekvo_f32_to_f16.restype = C.c_uint16
+        L.ekvo_f32_to_f16.argtypes = [C.c_float]
+        L.ekvo_f16_to_f32.restype = C.c_float
+        L.ekvo_f16_to_f32.argtypes = [C.c_uint16]
+        L.ekvo_f32_to_bf16_n.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
+        L.ekvo_bf16_to_f32_n.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
+        L.ekvo_quantize_q8_0.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
+        L.ekvo_dequantize_q8_0.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
+        L.ekvo_allowed.restype = C.c_int
+        L.ekvo_allowed.argtypes = [C.POINTER(Mask), C.POINTER(Seq), C.c_int32, C.c_int32]
+        L.ekvo_attention_f32.restype = C.c_int
+        L.ekvo_attention_f32.argtypes = [C.POINTER(AttnArgs), C.c_int]
+        L.ekvo_attention_f64.restype = C.c_int
+        L.ekvo_attention_f64.argtypes = [C.POINTER(AttnArgs), C.c_void_p]
+        L.ekvo_cache_attention_run.restype = C.c_int
+        L.ekvo_cache_attention_run.argtypes = [C.POINTER(CacheArgs), C.c_int]
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+# ---- number formats -------------------------------------------------------------------------
+
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().ekvo_f32_to_bf16_n(_ptr(x), _ptr(out), x.size)
+    return out
+
+
+def bf16_to_f32(h: np.ndarray) -> np.ndarray:
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    out = np.empty(h.shape, dtype=np.float32)
+    lib().ekvo_bf16_to_f32_n(_ptr(h), _ptr(out), h.size)
+    return out
+
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    L = lib()
+    return np.array([L.ekvo_f32_to_f16(float(v)) for v in x], dtype=np.uint16)
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    """x: f32 with last dim a multiple of 32 -> uint8 [..., last/32*34] ggml block_q8_0 bytes."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    assert x.shape[-1] % 32 == 0
+    out = np.empty(x.shape[:-1] + (x.shape[-1] // 32 * 34,), dtype=np.uint8)
+    lib().ekvo_quantize_q8_0(_ptr(x), x.size, _ptr(out))
+    return out
+
+
+def dequantize_q8_0(blocks: np.ndarray) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    assert blocks.shape[-1] % 34 == 0
+    n = blocks.shape[-1] // 34 * 32
+    out = np.empty(blocks.shape[:-1] + (n,), dtype=np.float32)
+    lib().ekvo_dequantize_q8_0(_ptr(blocks), out.size, _ptr(out))
+    return out
+
+
+# ---- masks and attention --------------------------------------------------------------------
+
+def make_mask(flags=0, chunk_tokens=0, chunk_stride=0, window_chunks=0, q_chunk0=0) -> Mask:
+    return Mask(flags, chunk_tokens, chunk_stride, window_chunks, q_chunk0)
+
+
+def make_seqs(n_prefix, prefix_valid=None, span=None, n_suffix=0):
+    """n_prefix etc. are per-request sequences (or scalars broadcast over B)."""
+    n_prefix = np.atleast_1d(np.asarray(n_prefix, dtype=np.int32))
+    B = n_prefix.size
+    pv = n_prefix if prefix_valid is None else np.broadcast_to(np.asarray(prefix_valid, np.int32), (B,))
+    if span is None:
+        sb = np.zeros(B, np.int32)
+        se = np.zeros(B, np.int32)
+    else:
+        sb = np.broadcast_to(np.asarray(span[0], np.int32), (B,))
+        se = np.broadcast_to(np.asarray(span[1], np.int32), (B,))
+    ns = np.broadcast_to(np.asarray(n_suffix, np.int32), (B,))
+    arr = (Seq * B)()
+    for i in range(B):
+        arr[i] = Seq(int(n_prefix[i]), int(pv[i]), int(sb[i]), int(se[i]), int(ns[i]))
+    return arr
+
+
+def allowed_matrix(mask: Mask, seq: Seq, Tq: int, Lk: int) -> np.ndarray:
+    L = lib()
+    out = np.zeros((Tq, Lk), dtype=bool)
+    for q in range(Tq):
+        for k in range(Lk):
+            out[q, k] = bool(L.ekvo_allowed(C.byref(mask), C.byref(seq), q, k))
+    return out
+
+
+def attention(q, k, v, seqs, mask: Mask, scale: float, dense_mask=None, precision="f32",
+              n_threads=0):
+    """q [B,Tq,Hq,D], k/v [B,Lk,Hkv,D] as f32 (prefix keys then suffix keys)."""
+    q = np.ascontiguousarray(q, np.float32)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    B, Tq, Hq, D = q.shape
+    Lk, Hkv = k.shape[1], k.shape[2]
+    dm = None if dense_mask is None else np.ascontiguousarray(dense_mask, np.float32)
+    out = np.zeros(q.shape, np.float32)
+    args = AttnArgs(B, Tq, Hq, Hkv, D, Lk, scale, _ptr(q).value, _ptr(k).value, _ptr(v).value,
+                    None if dm is None else _ptr(dm).value, C.addressof(seqs), mask,
+                    _ptr(out).value)
+    if precision == "f64":
+        out64 = np.zeros(q.shape, np.float64)
+        rc = lib().ekvo_attention_f64(C.byref(args), _ptr(out64))
+        assert rc == 0
+        return out64
+    rc = lib().ekvo_attention_f32(C.byref(args), n_threads or os.cpu_count() or 1)
+    assert rc == 0
+    return out
+
+
+def cache_attention_run(args: CacheArgs, n_threads: int) -> int:
+    return lib().ekvo_cache_attention_run(C.byref(args), n_threads)

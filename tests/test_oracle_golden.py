@@ -1,0 +1,110 @@
+"""Pin the CPU oracle to the golden vectors (gguf-py, numpy, the LingBot smoke test, the
+reference's mask builders). Runs without a GPU."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    return np.load(os.path.join(GOLD, name))
+
+
+def test_q8_0_matches_gguf_bytes():
+    g = load("q8_0_gguf.npz")
+    q = oracle.quantize_q8_0(g["x"])
+    assert q.shape == g["q8_0"].shape
+    np.testing.assert_array_equal(q, g["q8_0"])
+
+
+def test_q8_0_dequant_matches_gguf():
+    g = load("q8_0_gguf.npz")
+    d = oracle.dequantize_q8_0(g["q8_0"])
+    np.testing.assert_array_equal(d.view(np.uint32), g["dequant"].view(np.uint32))
+
+
+def test_bf16_matches_gguf_bits():
+    g = load("bf16_gguf.npz")
+    np.testing.assert_array_equal(oracle.f32_to_bf16(g["x"]), g["bf16"])
+
+
+def test_f16_matches_numpy_bits():
+    g = load("f16_numpy.npz")
+    got = oracle.f32_to_f16_bits(g["x"])
+    np.testing.assert_array_equal(got, g["f16"])
+
+
+def test_lingbot_smoke_known_answer():
+    g = load("lingbot_smoke.npz")
+    S, H, D = g["q"].shape
+    mask = g["mask"].astype(bool)
+    dense = np.where(mask, 0.0, -np.inf).astype(np.float32)[None]
+    seqs = oracle.make_seqs([S], n_suffix=0)
+    out = oracle.attention(g["q"][None], g["k"][None], g["v"][None], seqs, oracle.make_mask(),
+                           float(g["scale"]), dense_mask=dense)
+    assert np.abs(out[0] - g["ref"]).max() < float(g["tol"])
+    out64 = oracle.attention(g["q"][None], g["k"][None], g["v"][None], seqs, oracle.make_mask(),
+                             float(g["scale"]), dense_mask=dense, precision="f64")
+    assert np.abs(out64[0] - g["ref"]).max() < 1e-12
+
+
+def _allowed_from_dense(d):
+    return np.isfinite(d)
+
+
+def test_mask_smolvla_padding_causal():
+    g = load("mask_builders.npz")
+    n_prefix, n_valid, n_suf = (int(x) for x in g["smolvla_meta"])
+    seq = oracle.make_seqs([n_prefix], prefix_valid=n_valid, n_suffix=n_suf)[0]
+    m = oracle.make_mask(oracle.MASK_SUFFIX_CAUSAL)
+    got = oracle.allowed_matrix(m, seq, n_suf, n_prefix + n_suf)
+    np.testing.assert_array_equal(got, _allowed_from_dense(g["smolvla_full"]))
+
+
+def test_mask_hyvla_prefix_lm():
+    g = load("mask_builders.npz")
+    n_pref, n_suf = (int(x) for x in g["hyvla_meta"])
+    seq = oracle.make_seqs([n_pref], n_suffix=n_suf)[0]
+    m = oracle.make_mask(oracle.MASK_SUFFIX_PREFIX_LM)
+    got = oracle.allowed_matrix(m, seq, n_suf, n_pref + n_suf)
+    np.testing.assert_array_equal(got, _allowed_from_dense(g["hyvla_full"]))
+
+
+@pytest.mark.parametrize("kind,flag", [("groot_text", oracle.MASK_SPAN_EXCLUDE),
+                                       ("groot_image", oracle.MASK_SPAN_ONLY)])
+def test_mask_groot_spans(kind, flag):
+    g = load("mask_builders.npz")
+    bb, n_valid, sb, se, seq_q = (int(x) for x in g["groot_meta"])
+    seq = oracle.make_seqs([bb], prefix_valid=n_valid, span=(sb, se), n_suffix=0)[0]
+    got = oracle.allowed_matrix(oracle.make_mask(flag), seq, seq_q, bb)
+    np.testing.assert_array_equal(got, _allowed_from_dense(g[kind]))
+
+
+def test_block_causal_window():
+    # 4 chunks of 3 valid tokens padded to a stride of 4; queries are chunk 3 (q_chunk0=3),
+    # window 2 chunks: keys of chunks 2 and 3 only, padded slots excluded.
+    m = oracle.make_mask(oracle.MASK_BLOCK_CAUSAL, chunk_tokens=3, chunk_stride=4,
+                         window_chunks=2, q_chunk0=3)
+    seq = oracle.make_seqs([16], n_suffix=0)[0]
+    got = oracle.allowed_matrix(m, seq, 3, 16)
+    want = np.zeros((3, 16), bool)
+    want[:, [8, 9, 10, 12, 13, 14]] = True
+    np.testing.assert_array_equal(got, want)
+
+
+def test_f32_vs_f64_pi05_small():
+    rng = np.random.default_rng(0)
+    B, Tq, Hq, Hkv, D, Lp, Ls = 2, 5, 4, 1, 64, 37, 5
+    to_bf = lambda a: oracle.bf16_to_f32(oracle.f32_to_bf16(a))
+    q = to_bf(rng.standard_normal((B, Tq, Hq, D)).astype(np.float32) * 0.5)
+    k = to_bf(rng.standard_normal((B, Lp + Ls, Hkv, D)).astype(np.float32) * 0.5)
+    v = to_bf(rng.standard_normal((B, Lp + Ls, Hkv, D)).astype(np.float32) * 0.5)
+    seqs = oracle.make_seqs([Lp, Lp - 3], prefix_valid=[30, 34], n_suffix=Ls)
+    m = oracle.make_mask()
+    a = oracle.attention(q, k, v, seqs, m, 1 / 8.0)
+    b = oracle.attention(q, k, v, seqs, m, 1 / 8.0, precision="f64")
+    assert np.abs(a - b).max() < 1e-5
