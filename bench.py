@@ -1,0 +1,533 @@
+"""Benchmark of the denoise-loop attention over a paged prefix KV cache (libekv.so on B200).
+
+Default workload (the one the headline metric is quoted on):
+  pi0.5-shaped action-expert attention loop, 18 layers x 10 flow-matching steps, batch 64
+  independent requests per GPU, prefix KV stored as ggml Q8_0 in 16-token blocks with shuffled
+  block tables, prefix lengths uniform 700..816, 50 suffix (action) tokens appended per
+  layer-step as bf16 and attending bidirectionally, 8 query heads over 1 KV head, head_dim 256,
+  scale 1/16, Q/K/V = bf16(N(0,1) * 0.5), fixed seed.
+
+One step = one predict's hot path for the batch: append the prefix K/V of all 18 layers into
+the pool (Q8_0 quantise-on-write), then for each of the 10 x 18 layer-steps append the 50-token
+suffix into its slot and run the masked attention. A query-token is one suffix token (all its
+heads) through one attention call, so a step is 64 * 50 * 180 query-tokens.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config NAME]
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own 64 requests (weak scaling), no
+collective on the data path; timing is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "embodied.cpp_b200"))
+
+METRIC = "denoise-attn query-tok/s"
+
+CONFIGS = {
+    # name: (dtype, batch, prefix lo, prefix hi, text padding, description)
+    "pi05_q8_b64": dict(dtype="q8_0", batch=64, plo=700, phi=816, padded=False,
+                        desc="pi0.5 Q8_0 paged prefix (16-token blocks, shuffled tables), batch 64, "
+                             "prefix U[700,816], 18 layers x 10 steps, 50 suffix tokens, 8q/1kv x 256"),
+    "pi05_bf16_b1": dict(dtype="bf16", batch=1, plo=816, phi=816, padded=True,
+                         desc="pi0.5 bf16 prefix 816 = 768 image + 48 text (valid text U[20,48], rest "
+                              "padding-masked), batch 1, 18 layers x 10 steps, 50 suffix, 8q/1kv x 256"),
+    "serve_q8_b256": dict(dtype="q8_0", batch=256, plo=600, phi=1000, padded=False,
+                          desc="pi0.5 Q8_0 serving sweep, batch 256 per GPU, prefix U[600,1000], "
+                               "18 layers x 10 steps, 50 suffix, 8q/1kv x 256"),
+}
+
+N_LAYERS, N_STEPS, TQ, HQ, HKV, D, BT = 18, 10, 50, 8, 1, 256, 16
+SCALE = 1.0 / 16.0
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return dict(hbm=j["hbm_gbs"], tc=j["bf16_tflops"], tc_sustained=j.get("bf16_tflops_sustained"),
+                    source="measured")
+    return dict(hbm=6650.0, tc=1590.0, tc_sustained=1400.0, source="fallback")
+
+
+# ------------------------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ------------------------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+# workload
+# ------------------------------------------------------------------------------------------
+class Pi05Workload:
+    """Inputs of the pi0.5 denoise loop for `batch` requests, resident in HBM."""
+
+    def __init__(self, cfg: dict, seed: int, device: int):
+        import torch
+        import ekv
+
+        self.torch, self.ekv = torch, ekv
+        self.cfg = cfg
+        self.B = cfg["batch"]
+        self.dtype = ekv.DTYPE_Q8_0 if cfg["dtype"] == "q8_0" else ekv.DTYPE_BF16
+        rng = np.random.default_rng(seed)
+        B = self.B
+        self.plen = rng.integers(cfg["plo"], cfg["phi"] + 1, size=B).astype(np.int32)
+        if cfg["padded"]:
+            # 768 image tokens + 48 text slots, valid text U[20, 48], the rest padding-masked
+            self.pvalid = (768 + rng.integers(20, 49, size=B)).astype(np.int32)
+        else:
+            self.pvalid = self.plen.copy()
+        need = (self.plen + BT - 1) // BT
+        n_blocks = int(need.sum())
+        self.pool = ekv.Pool(device=device, dtype=self.dtype, block_tokens=BT, n_blocks=n_blocks, kv_heads=HKV,
+                             head_dim=D, n_layers=N_LAYERS, max_seqs=B, max_blocks_per_seq=int(need.max()),
+                             suffix_tokens=TQ)
+        perm = rng.permutation(n_blocks)
+        self.seqs, o = [], 0
+        for b in range(B):
+            s = self.pool.seq_create()
+            self.pool.seq_set_blocks(s, [int(x) for x in perm[o:o + need[b]]], int(self.plen[b]))
+            o += int(need[b])
+            self.seqs.append(s)
+        self.pool.sync()
+        dev = f"cuda:{device}"
+        t = lambda a: torch.tensor(np.asarray(a, np.int32), device=dev)
+        self.seq_ids = t(self.seqs)
+        self.zeros = t(np.zeros(B))
+        self.n_rows = t(self.plen)
+        self.src_row = t(np.concatenate([[0], np.cumsum(self.plen)[:-1]]))
+        self.prefix_valid = t(self.pvalid)
+        self.total_rows = int(self.plen.sum())
+        g = torch.Generator(device=dev).manual_seed(seed)
+        rn = lambda *shape: (torch.randn(shape, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        n_calls = N_LAYERS * N_STEPS
+        self.n_calls = n_calls
+        # prefix K/V per layer (packed rows), per-call suffix K/V and Q, per-call output
+        self.pk = rn(N_LAYERS, self.total_rows, HKV, D)
+        self.pv = rn(N_LAYERS, self.total_rows, HKV, D)
+        self.sk = rn(n_calls, B, TQ, HKV, D)
+        self.sv = rn(n_calls, B, TQ, HKV, D)
+        self.q = rn(n_calls, B, TQ, HQ, D)
+        self.out = torch.empty((n_calls, B, TQ, HQ, D), dtype=torch.bfloat16, device=dev)
+        self.params = [self.pool.attention_params(layer=l, seq_ids=self.seq_ids, q_tokens=TQ, q_heads=HQ,
+                                                  scale=SCALE, suffix_len=TQ, out_dtype=ekv.DTYPE_BF16,
+                                                  prefix_valid=self.prefix_valid)
+                       for l in range(N_LAYERS)]
+        ws = max(self.pool.workspace_size(p) for p in self.params)
+        self.ws = torch.empty(ws, dtype=torch.uint8, device=dev) if ws else None
+        # algorithmic work per call (masked / padded keys excluded)
+        lk = (self.pvalid + TQ).astype(np.float64)
+        self.flop_per_call = float((4.0 * TQ * HQ * lk * D).sum())
+        b_kv = 34.0 / 32.0 if self.dtype == ekv.DTYPE_Q8_0 else 2.0
+        self.bytes_per_call = float((TQ * HQ * D * 2 + 2 * HKV * self.pvalid * D * b_kv + 2 * HKV * TQ * D * 2
+                                     + TQ * HQ * D * 2).sum())
+        self.qtok_per_step = B * TQ * n_calls
+
+    def step(self, stream, ev=None, src=None):
+        """Enqueue one step. `ev` = (starts, ends) event lists to bracket each attention call;
+        `src` overrides the input tensors (the end-to-end path's staging buffers)."""
+        pool = self.pool
+        pk, pv, sk, sv, q, out = src if src is not None else (self.pk, self.pv, self.sk, self.sv, self.q, self.out)
+        for l in range(N_LAYERS):
+            pool.append(l, self.seq_ids, self.zeros, self.n_rows, self.src_row, int(self.plen.max()), pk[l], pv[l],
+                        stream=stream)
+        for c in range(self.n_calls):
+            l = c % N_LAYERS
+            pool.append_suffix(l, self.seq_ids, sk[c], sv[c], stream=stream)
+            if ev is not None:
+                ev[0][c].record(stream)
+            pool.attention(self.params[l], q[c], out[c], workspace=self.ws, stream=stream)
+            if ev is not None:
+                ev[1][c].record(stream)
+
+    launches_per_step = N_LAYERS + 2 * N_LAYERS * N_STEPS
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline: the oracle (C restatement of the reference's per-call work), all host cores
+# ------------------------------------------------------------------------------------------
+def cpu_baseline(wl: Pi05Workload, n_req: int, n_layers: int, threads: int):
+    """Times the oracle on the first n_req requests x n_layers layer-calls of denoise step 0,
+    with the same inputs (copied back from the device)."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    import ctypes as C
+
+    B = n_req
+    plen = wl.plen[:B]
+    maxp = int(plen.max())
+    row = HKV * D
+    is_q8 = wl.dtype == wl.ekv.DTYPE_Q8_0
+    rb = row // 32 * 34 if is_q8 else row * 2
+    pk = np.zeros((n_layers, B, maxp, rb), np.uint8)
+    pv = np.zeros_like(pk)
+    src_row = np.concatenate([[0], np.cumsum(wl.plen)[:-1]])
+    for l in range(n_layers):
+        for b in range(B):
+            n = int(plen[b])
+            kb = wl.pk[l, src_row[b]:src_row[b] + n].float().cpu().numpy().reshape(n, row)
+            vb = wl.pv[l, src_row[b]:src_row[b] + n].float().cpu().numpy().reshape(n, row)
+            if is_q8:
+                pk[l, b, :n] = oracle.quantize_q8_0(kb)
+                pv[l, b, :n] = oracle.quantize_q8_0(vb)
+            else:
+                pk[l, b, :n] = oracle.f32_to_bf16(kb).view(np.uint8)
+                pv[l, b, :n] = oracle.f32_to_bf16(vb).view(np.uint8)
+    sk = wl.sk[:n_layers, :B].contiguous().view(torch.int16).cpu().numpy()
+    sv = wl.sv[:n_layers, :B].contiguous().view(torch.int16).cpu().numpy()
+    q = wl.q[:n_layers, :B].contiguous().view(torch.int16).cpu().numpy()
+    out = np.zeros((B, TQ, HQ, D), np.float32)
+    np_ = np.ascontiguousarray(plen, np.int32)
+    nv_ = np.ascontiguousarray(wl.pvalid[:B], np.int32)
+    args = oracle.CacheArgs(B, TQ, HQ, HKV, D, n_layers, 1 if is_q8 else 0, maxp, TQ, SCALE,
+                            np_.ctypes.data, nv_.ctypes.data, pk.ctypes.data, pv.ctypes.data,
+                            sk.ctypes.data, sv.ctypes.data, q.ctypes.data, n_layers, out.ctypes.data)
+    t0 = time.perf_counter()
+    rc = oracle.cache_attention_run(args, threads)
+    dt = time.perf_counter() - t0
+    assert rc == 0
+    qtok = B * TQ * n_layers
+    # parity of the timed sample's last call against the GPU output of the same call
+    got = wl.out[n_layers - 1, :B].float().cpu().numpy()
+    err = float(np.abs(got - out).max())
+    return qtok / dt, dt, qtok, err
+
+
+# ------------------------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference(args, cfg):
+    """The reference arm: the reference's CPU path (the oracle port of it; the ggml CPU backend
+    it restates is not buildable here) on the host cores, bounded sample per step."""
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1234)
+    B = min(cfg["batch"], max(8, threads))
+    n_layers = 2
+    plen = rng.integers(cfg["plo"], cfg["phi"] + 1, size=B).astype(np.int32)
+    pvalid = (768 + rng.integers(20, 49, size=B)).astype(np.int32) if cfg["padded"] else plen.copy()
+    maxp = int(plen.max())
+    row = HKV * D
+    is_q8 = cfg["dtype"] == "q8_0"
+    x = (rng.standard_normal((n_layers, B, maxp, row), dtype=np.float32) * 0.5)
+    xv = (rng.standard_normal((n_layers, B, maxp, row), dtype=np.float32) * 0.5)
+    if is_q8:
+        pk = oracle.quantize_q8_0(oracle.bf16_to_f32(oracle.f32_to_bf16(x)))
+        pv = oracle.quantize_q8_0(oracle.bf16_to_f32(oracle.f32_to_bf16(xv)))
+    else:
+        pk = oracle.f32_to_bf16(x).view(np.uint8)
+        pv = oracle.f32_to_bf16(xv).view(np.uint8)
+    sk = oracle.f32_to_bf16(rng.standard_normal((n_layers, B, TQ, HKV, D), dtype=np.float32) * 0.5)
+    sv = oracle.f32_to_bf16(rng.standard_normal((n_layers, B, TQ, HKV, D), dtype=np.float32) * 0.5)
+    q = oracle.f32_to_bf16(rng.standard_normal((n_layers, B, TQ, HQ, D), dtype=np.float32) * 0.5)
+    out = np.zeros((B, TQ, HQ, D), np.float32)
+    args_c = oracle.CacheArgs(B, TQ, HQ, HKV, D, n_layers, 1 if is_q8 else 0, maxp, TQ, SCALE,
+                              plen.ctypes.data, pvalid.ctypes.data, pk.ctypes.data, pv.ctypes.data,
+                              sk.ctypes.data, sv.ctypes.data, q.ctypes.data, n_layers, out.ctypes.data)
+    for _ in range(args.warmup):
+        oracle.cache_attention_run(args_c, threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.cache_attention_run(args_c, threads)
+        times.append(time.perf_counter() - t0)
+    qtok = B * TQ * n_layers
+    tot = sum(times)
+    value = qtok * len(times) / tot
+    sample = f"{B} requests x {n_layers} layer-calls of one denoise step per timed step"
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "query-tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": args.config, "description": cfg["desc"]},
+            "cpu_baseline": {"value": value, "unit": "query-tok/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "query-tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ekv", choices=["ekv", "reference"])
+    ap.add_argument("--config", default="pi05_q8_b64", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=0, help="override the requests per GPU (profiling cases)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["batch"] = args.batch
+    if args.impl == "reference":
+        run_reference(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    wl = Pi05Workload(cfg, seed=1234 + rank, device=local)
+    stream = torch.cuda.current_stream()
+    n_ev = wl.n_calls * args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+
+    for _ in range(args.warmup):
+        wl.step(stream)
+    torch.cuda.synchronize()
+    if wl.pool.status() != 0:
+        raise RuntimeError("device status word set during warm-up")
+
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    clocks = Clocks(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(args.steps):
+        sl = slice(k * wl.n_calls, (k + 1) * wl.n_calls)
+        wl.step(stream, ev=(starts[sl], ends[sl]))
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = t_start.elapsed_time(t_end)
+    if world > 1:
+        tt = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_per_step = ms / args.steps
+    value = world * wl.qtok_per_step * args.steps / (ms / 1e3)
+    attn_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    attn_avg_s = statistics.mean(attn_ms) / 1e3
+    status = wl.pool.status()
+
+    peaks = load_peaks()
+    flop_t = wl.flop_per_call / (peaks["tc"] * 1e12)
+    byte_t = wl.bytes_per_call / (peaks["hbm"] * 1e9)
+    bound = "tensor" if flop_t >= byte_t else "hbm"
+    if bound == "tensor":
+        achieved = wl.flop_per_call / attn_avg_s / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["tc"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["tc"]}
+    else:
+        achieved = wl.bytes_per_call / attn_avg_s / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm"]}
+    roof["traffic"] = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            roof["traffic"] = json.load(f).get(args.config)
+    roof["peak_source"] = peaks["source"] + " (burst bf16 figure)"
+    roof["kernel"] = "attn_tc_kernel<256,Q8>" if wl.dtype == wl.ekv.DTYPE_Q8_0 else "attn_tc_kernel<256,bf16>"
+    roof["avg_launch_us"] = attn_avg_s * 1e6
+    roof["algorithmic_per_launch"] = {"flop": wl.flop_per_call, "bytes": wl.bytes_per_call}
+
+    # ---- end to end through the C-ABI with host buffers (pinned), copies inside the timing ----
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(wl, args, world, barrier)
+
+    line = {"metric": METRIC, "value": value, "unit": "query-tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16/bf16 MMA, f32 accumulate (Q8_0 cache)" if wl.dtype == wl.ekv.DTYPE_Q8_0
+            else "bf16 MMA, f32 accumulate",
+            "data": "synthetic", "config": {"workload": args.config, "description": cfg["desc"],
+                                            "batch_per_gpu": wl.B, "layers": N_LAYERS, "denoise_steps": N_STEPS,
+                                            "suffix_tokens": TQ, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                                            "block_tokens": BT, "parallelism": f"request-sharded x{world}",
+                                            "l2": "inputs > L2 (per step ~%.1f GB of distinct Q/KV/O)" %
+                                                  ((wl.q.numel() * 2 * 2 + wl.sk.numel() * 4 + wl.pk.numel() * 4) / 1e9)},
+            "roofline": roof, "clocks": clk, "gpu_launches": wl.launches_per_step * args.steps,
+            "device_status": status}
+    if e2e is not None:
+        line["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, dt, qtok, err = cpu_baseline(wl, n_req=min(wl.B, 16), n_layers=N_LAYERS, threads=threads)
+        line["cpu_baseline"] = {"value": v, "unit": "query-tok/s", "cores": threads, "kind": "port",
+                                "sample": f"{min(wl.B, 16)} requests x {N_LAYERS} layer-calls (denoise step 0), "
+                                          f"{qtok} query-tokens in {dt:.2f} s",
+                                "max_abs_err_vs_gpu": err}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(wl, args, world, barrier):
+    """Same metric through the C-ABI with host buffers: every step copies its inputs from
+    pinned host memory (prefix K/V of all layers, per-call suffix K/V and Q) and reads every
+    call's output back, on separate copy streams overlapped with compute per layer-call."""
+    import torch
+    dev = wl.q.device
+    hp = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h_pk, h_pv, h_sk, h_sv, h_q, h_out = hp(wl.pk), hp(wl.pv), hp(wl.sk), hp(wl.sv), hp(wl.q), hp(wl.out)
+    h_pk.copy_(wl.pk)
+    h_pv.copy_(wl.pv)
+    h_sk.copy_(wl.sk)
+    h_sv.copy_(wl.sv)
+    h_q.copy_(wl.q)
+    # device staging: two slots per per-call tensor
+    d_pk, d_pv = torch.empty_like(wl.pk), torch.empty_like(wl.pv)
+    slot = lambda t: torch.empty((2,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
+    d_sk, d_sv, d_q, d_out = slot(wl.sk), slot(wl.sv), slot(wl.q), slot(wl.out)
+    s_c = torch.cuda.current_stream()
+    s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    N = wl.n_calls
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    h2d_bytes = (wl.pk.numel() + wl.pv.numel() + wl.sk.numel() + wl.sv.numel() + wl.q.numel()) * 2
+    d2h_bytes = wl.out.numel() * 2
+
+    def one_step():
+        with torch.cuda.stream(s_h2d):
+            d_pk.copy_(h_pk, non_blocking=True)
+            d_pv.copy_(h_pv, non_blocking=True)
+        pre = torch.cuda.Event()
+        pre.record(s_h2d)
+        s_c.wait_event(pre)
+        for l in range(N_LAYERS):
+            wl.pool.append(l, wl.seq_ids, wl.zeros, wl.n_rows, wl.src_row, int(wl.plen.max()), d_pk[l], d_pv[l],
+                           stream=s_c)
+
+        def stage(c):
+            i = c & 1
+            with torch.cuda.stream(s_h2d):
+                s_h2d.wait_event(ev_done[i])  # slot free once call c-2 finished reading it
+                d_sk[i].copy_(h_sk[c], non_blocking=True)
+                d_sv[i].copy_(h_sv[c], non_blocking=True)
+                d_q[i].copy_(h_q[c], non_blocking=True)
+                ev_in[i].record(s_h2d)
+
+        stage(0)
+        for c in range(N):
+            i = c & 1
+            if c + 1 < N:
+                stage(c + 1)
+            s_c.wait_event(ev_in[i])
+            s_c.wait_event(ev_out[i])  # output slot drained (call c-2)
+            l = c % N_LAYERS
+            wl.pool.append_suffix(l, wl.seq_ids, d_sk[i], d_sv[i], stream=s_c)
+            wl.pool.attention(wl.params[l], d_q[i], d_out[i], workspace=wl.ws, stream=s_c)
+            ev_done[i].record(s_c)
+            with torch.cuda.stream(s_d2h):
+                s_d2h.wait_event(ev_done[i])
+                h_out[c].copy_(d_out[i], non_blocking=True)
+                ev_out[i].record(s_d2h)
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_step()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([dt], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dt = float(tt.item())
+    barrier()
+    # the host buffers received the same outputs the device-resident run produced
+    ok = bool(torch.equal(h_out[-1].to(dev), wl.out[-1]))
+    return {"value": world * wl.qtok_per_step * args.steps / dt, "unit": "query-tok/s",
+            "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
+            "ms_per_step": 1e3 * dt / args.steps, "outputs_match_device_run": ok,
+            "timing": "host wall clock around K steps, synchronised on both sides"}
+
+
+if __name__ == "__main__":
+    main()

@@ -22,7 +22,7 @@ struct KeySrc {
 
 __device__ __forceinline__ float load_elem(const PoolView &p, const KeySrc &s, int d) {
     if (!s.q8) {
-        const uint16_t h = *(const uint16_t *)(s.tile + tile_elem_off(s.row, d, s.rows, p.swz_bytes));
+        const uint16_t h = *(const uint16_t *)(s.tile + tile_elem_off(s.row, d, p.head_dim, p.swz_bytes));
         return bf16_bits_to_f32(h);
     }
     const int8_t q = *(const int8_t *)(s.tile + (int64_t)s.row * p.head_dim + d);

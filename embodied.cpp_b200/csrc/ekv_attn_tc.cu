@@ -6,23 +6,31 @@
 //
 // Work unit (one CTA): 128 query rows that share one KV head (rows = (token, head-in-group),
 // so for MQA all 8 heads of 16 tokens share the K/V tiles) x a range of key tiles.
-//   warps 0-3  softmax: each thread owns one query row = one TMEM lane; reads S from TMEM,
-//              applies the mask, online max/sum in the exp2 domain, writes P (bf16/f16) to
-//              shared memory, rescales O in TMEM when the running max grows by > 2^8, and
-//              finally normalises O and stores it.
-//   warp 4     TMEM allocation + single-thread tcgen05.mma issue: S = Q K^T (M=128, N=BN,
-//              K=head_dim) into a double-buffered TMEM S, O += P V (M=128, N=head_dim, K=BN)
-//              into TMEM O; tcgen05.commit signals the mbarriers.
-//   warps 5+   producers: bf16 pools copy K/V block chunks with cp.async.bulk straight from the
-//              pool (tiles are stored pre-swizzled, so one contiguous copy per (block, chunk)
-//              lands as a canonical SW128/64/32 operand); Q8_0 pools load int8 + fp16 scales
-//              with 16-byte vector loads and dequantise in registers (exact int8 -> f16 via the
-//              0x6400 magic, one f16 multiply by the scale) into the same swizzled layout.
-// Q8_0 pools run the MMA in f16 (Q and the bf16 suffix converted exactly for normal values),
-// bf16 pools in bf16. Accumulation is f32 throughout.
+//
+// Tensor memory (512 columns): two S buffers of BN f32 columns (P, 16-bit, is written back
+// over the first BN/2 columns of its own S buffer), O (head_dim f32 columns) and Q (head_dim/2
+// columns of packed 16-bit pairs). Both MMAs take A from tensor memory:
+//   S = Q K^T   (M=128, N=BN, K=head_dim; A = Q in TMEM, B = K tile in shared memory)
+//   O += P V    (M=128, N=head_dim, K=BN; A = P in TMEM, B = V tile, MN-major)
+// so shared memory holds only K/V operand stages (and, for Q8_0, a raw staging ring).
+//
+// Warp roles:
+//   warps 0-3  softmax: thread = query row = TMEM lane. Reads S in 32-column halves, masks
+//              (closed-form key ranges), online max/sum in the exp2 domain, writes P into TMEM,
+//              rescales O in TMEM only when the running max grows by more than 2^8 (exact after
+//              the final division); epilogue O/l -> bf16/f32 (or split partials).
+//   warp 4     TMEM allocation; one thread issues tcgen05.mma, polling the K-ready and P-ready
+//              barriers so whichever of S(j+1) / PV(j) is ready goes first.
+//   warp 5     copy engine feeder: bf16 pools -> one cp.async.bulk per (block, swizzle chunk)
+//              straight into a K/V stage (pool tiles are stored pre-swizzled); Q8_0 pools ->
+//              bulk copies of the int8 and fp16-scale planes into a raw staging ring.
+//   warps 6-9  (Q8_0) dequantise raw -> f16 operand in shared memory: exact int8 -> f16 via the
+//              0x6400 magic, one f16 multiply by the scale; the bf16 suffix is converted to f16.
+// Q8_0 pools run the MMA in f16, bf16 pools in bf16; accumulation is f32.
 //
 // Every mbarrier wait is bounded (clock64 budget); on expiry the kernel records
-// DEV_ERR_TIMEOUT in the pool status word, raises a CTA-local abort flag and unwinds.
+// DEV_ERR_TIMEOUT in the pool status word, raises a CTA-local abort flag and unwinds, waiting
+// for its own in-flight copies and MMAs before releasing tensor memory.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -37,9 +45,30 @@ namespace {
 
 using namespace sm100;
 
+#ifdef EKV_TRACE
+__device__ unsigned long long *g_trace = nullptr;
+__device__ __forceinline__ void trace_at(int slot) {
+    if (g_trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        g_trace[slot] = t;
+    }
+}
+#define TRACE(slot) trace_at(slot)
+__device__ __forceinline__ void trace_clock(int slot) {
+    if (g_trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_trace[slot] = (unsigned long long)clock64();
+}
+#define TRACE_CLK(slot) trace_clock(slot)
+#else
+#define TRACE(slot) ((void)0)
+#define TRACE_CLK(slot) ((void)0)
+#endif
+
+
 constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (~2-3 s) before giving up
 constexpr int kBM = 128;
 constexpr int kMaxSplits = 8;
+constexpr int kDq = 128;  // dequantising threads (Q8_0)
 
 template <int D, bool Q8>
 struct TcCfg {
@@ -47,27 +76,52 @@ struct TcCfg {
     static constexpr int BN = D > 128 ? 64 : 128;
     static constexpr int W = (D * 2) % 128 == 0 ? 128 : ((D * 2) % 64 == 0 ? 64 : 32);
     static constexpr uint32_t LAYOUT = W == 128 ? 2u : (W == 64 ? 4u : 6u);
-    static constexpr int Q_BYTES = BM * D * 2;
+    static constexpr uint32_t SBO = (D * 2 / W) * 8 * W;  // bytes between 8-row groups (= 16 * D)
+    static constexpr int NSTAGE = Q8 ? 2 : 3;  // K/V operand stages
+    static constexpr int NRAW = Q8 ? 2 : 0;    // raw Q8_0 staging stages
     static constexpr int KV_BYTES = BN * D * 2;
-    static constexpr int P_BYTES = BM * BN * 2;
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = OFF_Q + Q_BYTES;
-    static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
-    static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
-    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-    static constexpr int SMEM = OFF_BAR + 256 + 1024;  // barriers/flags + 1 KB alignment slack
+    static constexpr int RAW_QS = BN * D;         // int8 of K (or V) for one tile
+    static constexpr int RAW_SC = BN * (D / 16);  // fp16 scales of K (or V): BN rows x D/32 x 2 B
+    static constexpr int RAW_BYTES = 2 * (RAW_QS + RAW_SC);
+    static constexpr int OFF_K = 0;
+    static constexpr int OFF_V = NSTAGE * KV_BYTES;
+    static constexpr int OFF_RAW = 2 * NSTAGE * KV_BYTES;
+    static constexpr int OFF_BAR = OFF_RAW + NRAW * RAW_BYTES;
+    static constexpr int OFF_TBL = OFF_BAR + 256;
+    // tile base pointers of the split's block-table entries (whatever fits, at most 512)
+    static constexpr int TBL_ROOM = (232448 - 1024 - OFF_TBL) / 8;
+    static constexpr int TBL = TBL_ROOM > 512 ? 512 : TBL_ROOM;
+    static constexpr int SMEM = OFF_TBL + TBL * 8 + 1024;  // + 1 KB alignment slack
+    static constexpr int QSTR = D * 2 + 16;               // Q staging row stride (bank-conflict free)
     static constexpr int MMA_WARP = 4;
-    static constexpr int PROD_WARP0 = 5;
-    static constexpr int N_PROD = Q8 ? 128 : 32;
-    static constexpr int THREADS = 160 + N_PROD;
+    static constexpr int TMA_WARP = 5;
+    static constexpr int DQ_WARP0 = 6;
+    static constexpr int THREADS = Q8 ? 192 + kDq : 192;
     static constexpr int TMEM_COLS = 512;
+    static constexpr int S_COL = 0;
     static constexpr int O_COL = 2 * BN;
-    static_assert(O_COL + D <= TMEM_COLS, "TMEM budget");
+    static constexpr int Q_COL = 512 - D / 2;
+    static_assert(O_COL + D <= Q_COL, "TMEM budget");
+    static_assert(Q_COL % 8 == 0, "TMEM alignment");
     static_assert(SMEM <= 232448, "shared-memory budget");
+    static_assert(TBL >= 64, "block-table cache");
+    static_assert(BM * QSTR <= 2 * NSTAGE * KV_BYTES, "Q staging fits in the K/V stages");
+    static constexpr int OSTR = D * 4 + 16;  // epilogue staging row stride (f32 worst case)
+    static_assert(BM * OSTR <= OFF_BAR, "epilogue staging fits below the barriers");
     static_assert(D % 16 == 0, "head_dim must be a multiple of 16");
 };
 
-enum { BAR_KV_FULL = 0, BAR_KV_EMPTY = 2, BAR_S_FULL = 4, BAR_P_FULL = 6, BAR_P_EMPTY = 8, BAR_DONE = 10, N_BARS = 11 };
+enum {
+    BAR_OP_FULL = 0,     // [3] K/V operand stage filled
+    BAR_OP_EMPTY = 3,    // [3] K/V operand stage consumed (P.V done)
+    BAR_RAW_FULL = 6,    // [2] raw Q8_0 stage landed
+    BAR_RAW_EMPTY = 8,   // [2] raw Q8_0 stage read
+    BAR_S_FULL = 10,     // [2] S(j) in TMEM
+    BAR_P_FULL = 12,     // [2] P(j) in TMEM
+    BAR_P_EMPTY = 14,    // [2] P.V(j) done (P consumed, O updated)
+    BAR_DONE = 16,
+    N_BARS = 17
+};
 
 // Key-tile schedule of one CTA, computed identically by every thread.
 struct Plan {
@@ -78,6 +132,8 @@ struct Plan {
     int np_tiles;   // prefix tiles
     int ns_tiles;   // suffix tiles
     int j0, j1;     // this split's tile range [j0, j1)
+    int tbl_lo;     // first block-table index cached in shared memory
+    int tbl_n;      // entries cached (table indices [tbl_lo, tbl_lo + tbl_n))
 };
 
 template <int BN>
@@ -120,106 +176,260 @@ __device__ __forceinline__ Plan make_plan(const AttnArgs &a, int n_qtiles) {
     const int per = (n + n_splits - 1) / n_splits;
     pl.j0 = min(n, pl.split * per);
     pl.j1 = min(n, pl.j0 + per);
+    // prefix keys this split reads: tiles [j0, min(j1, np_tiles)), clipped to the sequence
+    pl.tbl_lo = 0;
+    pl.tbl_n = 0;
+    const int pj1 = min(pl.j1, pl.np_tiles);
+    if (pl.j0 < pj1) {
+        const int k_lo = pl.kbeg + pl.j0 * BN;
+        const int k_hi = min(pl.kbeg + pj1 * BN, pl.sk.n_prefix);
+        if (k_hi > k_lo) {
+            const int bt = a.pool.block_tokens;
+            pl.tbl_lo = k_lo / bt;
+            pl.tbl_n = (k_hi + bt - 1) / bt - pl.tbl_lo;
+        }
+    }
     (void)n_qtiles;
     return pl;
 }
 
-// ---- Q tile: bf16 [B][Tq][Hq][D] rows -> swizzled K-major A operand (f16 for Q8_0 pools) ----
+
+// Bits of the keys [lo, hi) inside the 32-key word starting at key w0.
+__device__ __forceinline__ uint32_t range_bits(int lo, int hi, int w0) {
+    const int a = max(lo - w0, 0), b = min(hi - w0, 32);
+    if (b <= a) return 0u;
+    const uint32_t upto_b = b >= 32 ? 0xffffffffu : ((1u << b) - 1u);
+    const uint32_t below_a = (1u << a) - 1u;  // a < 32 here
+    return upto_b & ~below_a;
+}
+
+// Visibility of keys [w0, w0+32) for query token t, from key ranges (no per-key loop):
+// the predicate of prefix_allowed / suffix_allowed in closed form.
+__device__ __forceinline__ uint32_t vis_word(const MaskDesc &m, bool suffix, int w0, int t, int prefix_valid,
+                                             int span_b, int span_e, int suffix_len) {
+    if (suffix) {
+        int hi = suffix_len;
+        if (m.flags & EKV_MASK_SUFFIX_CAUSAL) hi = min(hi, t + 1);
+        if ((m.flags & EKV_MASK_SUFFIX_PREFIX_LM) && t == 0) hi = min(hi, 1);
+        return range_bits(0, hi, w0);
+    }
+    uint32_t bits = range_bits(0, prefix_valid, w0);
+    if (m.flags & EKV_MASK_SPAN_ONLY) bits &= range_bits(span_b, span_e, w0);
+    if (m.flags & EKV_MASK_SPAN_EXCLUDE) bits &= ~range_bits(span_b, span_e, w0);
+    if (m.flags & EKV_MASK_BLOCK_CAUSAL) {
+        const int qc = m.q_chunk0 + t / m.chunk_tokens;
+        const int kc_lo = max(qc - m.window_chunks + 1, max(w0, 0) / m.chunk_stride);
+        const int kc_hi = min(qc, (w0 + 31) / m.chunk_stride);
+        uint32_t win = 0u;
+        for (int kc = kc_lo; kc <= kc_hi; ++kc)
+            win |= range_bits(kc * m.chunk_stride, kc * m.chunk_stride + m.chunk_tokens, w0);
+        bits &= win;
+    }
+    return bits;
+}
+
+
+// Table index of key k, and the key's row inside its block (shift/mask for power-of-two blocks).
+__device__ __forceinline__ int block_index(const PoolView &p, int k, int &rib) {
+    if (p.bt_shift >= 0) {
+        rib = k & (p.block_tokens - 1);
+        return k >> p.bt_shift;
+    }
+    const int idx = k / p.block_tokens;
+    rib = k - idx * p.block_tokens;
+    return idx;
+}
+
+// K tile base (head g, this layer) of block-table entry `idx`: shared-memory copy when cached,
+// otherwise from the global table; nullptr for an invalid entry (reported by lookup_block).
+template <int TBL>
+__device__ __forceinline__ const uint8_t *ptr_of(const AttnArgs &a, const Plan &pl, const uint8_t *const *sPtr,
+                                                 int idx) {
+    const int i = idx - pl.tbl_lo;
+    if (pl.tbl_n <= TBL && i >= 0 && i < pl.tbl_n) return sPtr[i];
+    const int blk = lookup_block(a.pool, pl.sk.seq, idx);
+    return blk < 0 ? nullptr
+                   : a.pool.prefix + prefix_tile_index(a.pool, a.layer, blk, 0, pl.g) * a.pool.tile_bytes;
+}
+
+// ---- Q: bf16 [B][Tq][Hq][D] rows -> shared staging (all threads, every load in flight before
+// the first store) -> TMEM Q columns (softmax warps, one row per thread; f16 for Q8_0 pools) ----
 template <int D, bool Q8>
-__device__ __forceinline__ void load_q_tile(const AttnArgs &a, const Plan &pl, uint8_t *sQ) {
-    using C = TcCfg<D, Q8>;
-    constexpr int UNITS_PER_ROW = D / 8;
-    for (int u = threadIdx.x; u < kBM * UNITS_PER_ROW; u += C::THREADS) {
-        const int r = u / UNITS_PER_ROW;
-        const int d0 = (u - r * UNITS_PER_ROW) * 8;
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (r < pl.rows_valid) {
+struct QStage {
+    static constexpr int UPR = D / 8;  // 16-byte units per row
+    static constexpr int UNITS = kBM * UPR;
+    static constexpr int ITERS = (UNITS + TcCfg<D, Q8>::THREADS - 1) / TcCfg<D, Q8>::THREADS;
+    uint4 val[ITERS];
+};
+
+template <int D, bool Q8>
+__device__ __forceinline__ void stage_q_load(const AttnArgs &a, const Plan &pl, QStage<D, Q8> &qs) {
+    using Q = QStage<D, Q8>;
+#pragma unroll
+    for (int i = 0; i < Q::ITERS; ++i) {
+        const int u = threadIdx.x + i * TcCfg<D, Q8>::THREADS;
+        const int r = u / Q::UPR;
+        qs.val[i] = make_uint4(0, 0, 0, 0);
+        if (u < Q::UNITS && r < pl.rows_valid) {
+            const int d0 = (u - r * Q::UPR) * 8;
             const int qr = pl.qrow0 + r;
             const int t = qr / a.group;
             const int h = pl.g * a.group + (qr - t * a.group);
-            val = *(const uint4 *)(a.q + (((int64_t)pl.b * a.q_tokens + t) * a.q_heads + h) * D + d0);
-            if (Q8) {
-                uint32_t w[4] = {val.x, val.y, val.z, val.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const __half2 h2 = __floats2half2_rn(__uint_as_float(w[i] << 16),
-                                                         __uint_as_float(w[i] & 0xffff0000u));
-                    w[i] = *(const uint32_t *)&h2;
-                }
-                val = make_uint4(w[0], w[1], w[2], w[3]);
-            }
+            qs.val[i] = __ldg((const uint4 *)(a.q + (((int64_t)pl.b * a.q_tokens + t) * a.q_heads + h) * D + d0));
         }
-        *(uint4 *)(sQ + tile_elem_off(r, d0, kBM, C::W)) = val;
     }
 }
 
-// ---- bf16 producer: one warp; zero-fills missing rows, lane 0 issues the bulk copies ----
+template <int D, bool Q8>
+__device__ __forceinline__ void stage_q_store(const QStage<D, Q8> &qs, uint8_t *stg) {
+    using Q = QStage<D, Q8>;
+#pragma unroll
+    for (int i = 0; i < Q::ITERS; ++i) {
+        const int u = threadIdx.x + i * TcCfg<D, Q8>::THREADS;
+        if (u >= Q::UNITS) break;
+        const int r = u / Q::UPR;
+        *(uint4 *)(stg + r * TcCfg<D, Q8>::QSTR + (u - r * Q::UPR) * 16) = qs.val[i];
+    }
+}
+
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
+    const __half2 h2 = __floats2half2_rn(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    return *(const uint32_t *)&h2;
+}
+
+template <int D, bool Q8>
+__device__ __forceinline__ void q_to_tmem(const uint8_t *stg, int r, uint32_t taddr) {
+    using C = TcCfg<D, Q8>;
+#pragma unroll 1
+    for (int c = 0; c < D / 16; ++c) {  // 16 elements = 8 columns per store
+        const uint4 a0 = *(const uint4 *)(stg + r * C::QSTR + c * 32);
+        const uint4 a1 = *(const uint4 *)(stg + r * C::QSTR + c * 32 + 16);
+        uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        if (Q8) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
+        }
+        tmem_st8(taddr + (uint32_t)(c * 8), w);
+    }
+}
+
+// ---- bf16 feeder: one warp, one lane per segment (a block, or the suffix rows of the tile).
+// Source and destination are runs of whole 8-row groups, i.e. one contiguous copy each for K
+// and V; rows without a source are zero-filled by the whole warp ----
 template <int D>
-__device__ __forceinline__ void produce_bf16_tile(const AttnArgs &a, const Plan &pl, int j, uint8_t *sK,
-                                                  uint8_t *sV, uint32_t bar_full, int lane) {
+__device__ __forceinline__ void produce_bf16_tile(const AttnArgs &a, const Plan &pl, const uint8_t *const *sPtr,
+                                                  int j, uint8_t *sK, uint8_t *sV, uint32_t bar_full, int lane) {
     using C = TcCfg<D, false>;
-    constexpr int BN = C::BN, W = C::W, NCH = D * 2 / W;
+    constexpr int BN = C::BN, RB = D * 2;
     const PoolView &p = a.pool;
     const bool suffix = j >= pl.np_tiles;
-    // Segments of the tile: [row0, row0+len) of the tile come from one block (or the suffix
-    // tile); src == nullptr means zero-fill.
-    uint32_t total = 0;
-    // pass 0: zero-fill (all lanes) and byte count; pass 1: lane 0 issues copies
-    for (int pass = 0; pass < 2; ++pass) {
-        if (pass == 1) {
-            fence_proxy_async();
-            __syncwarp();
-            if (lane != 0) break;
-            if (total) mbar_arrive_expect_tx(bar_full, total);
-            else mbar_arrive(bar_full);
+    const int seg = suffix ? BN : min(p.block_tokens, BN);
+    const int n_seg = BN / seg;
+    const uint8_t *src = nullptr;
+    uint32_t bytes = 0;
+    const uint32_t dst = (uint32_t)lane * seg * RB;
+    int64_t v_off = 0;
+    if (lane < n_seg) {
+        if (suffix) {
+            const int s0 = (j - pl.np_tiles) * BN;
+            if (s0 < p.suffix_rows) {
+                bytes = (uint32_t)min(BN, p.suffix_rows - s0) * RB;
+                src = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 0, pl.g) * p.suffix_tile_bytes + (int64_t)s0 * RB;
+                v_off = (int64_t)p.kv_heads * p.suffix_tile_bytes;
+            }
+        } else {
+            const int k = pl.kbeg + j * BN + lane * seg;
+            int rib;
+            const int idx = block_index(p, k, rib);
+            if (k < pl.sk.n_prefix) {
+                src = ptr_of<C::TBL>(a, pl, sPtr, idx);
+                if (src) {
+                    src += (int64_t)rib * RB;
+                    bytes = (uint32_t)seg * RB;
+                    v_off = (int64_t)p.kv_heads * p.tile_bytes;
+                }
+            }
         }
-        int row = 0;
-        while (row < BN) {
-            const uint8_t *srcK = nullptr, *srcV = nullptr;
-            int len, src_rows = 0, src_row0 = 0;
-            if (suffix) {
-                const int s0 = (j - pl.np_tiles) * BN + row;
-                len = BN - row;
-                if (s0 < p.suffix_rows) {
-                    len = min(len, p.suffix_rows - s0);
-                    srcK = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 0, pl.g) * p.suffix_tile_bytes;
-                    srcV = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 1, pl.g) * p.suffix_tile_bytes;
-                    src_rows = p.suffix_rows;
-                    src_row0 = s0;
-                }
-            } else {
-                const int k = pl.kbeg + j * BN + row;
-                const int rib = k % p.block_tokens;
-                len = min(BN - row, p.block_tokens - rib);
-                if (k < pl.sk.n_prefix) {
-                    const int blk = lookup_block(p, pl.sk.seq, k / p.block_tokens);
-                    if (blk >= 0) {
-                        srcK = p.prefix + prefix_tile_index(p, a.layer, blk, 0, pl.g) * p.tile_bytes;
-                        srcV = p.prefix + prefix_tile_index(p, a.layer, blk, 1, pl.g) * p.tile_bytes;
-                        src_rows = p.block_tokens;
-                        src_row0 = rib;
-                    }
-                }
+    }
+    const uint32_t zlo = dst + bytes, zhi = lane < n_seg ? dst + (uint32_t)seg * RB : zlo;
+    const uint32_t need_zero = __ballot_sync(0xffffffffu, zhi > zlo);
+    const uint32_t total = __reduce_add_sync(0xffffffffu, src ? 2 * bytes : 0u);
+    if (need_zero) {
+        for (uint32_t m = need_zero; m; m &= m - 1) {
+            const int s = __ffs(m) - 1;
+            const uint32_t z0 = __shfl_sync(0xffffffffu, zlo, s), z1 = __shfl_sync(0xffffffffu, zhi, s);
+            for (uint32_t o = z0 + lane * 16; o < z1; o += 32 * 16) {
+                *(uint4 *)(sK + o) = make_uint4(0, 0, 0, 0);
+                *(uint4 *)(sV + o) = make_uint4(0, 0, 0, 0);
             }
-            for (int c = 0; c < NCH; ++c) {
-                const uint32_t dst_off = (uint32_t)c * (BN * W) + (uint32_t)row * W;
-                const uint32_t bytes = (uint32_t)len * W;
-                if (srcK) {
-                    if (pass == 0) {
-                        total += 2 * bytes;
-                    } else {
-                        const int64_t so = (int64_t)c * src_rows * W + (int64_t)src_row0 * W;
-                        bulk_g2s(smem_addr(sK + dst_off), srcK + so, bytes, bar_full);
-                        bulk_g2s(smem_addr(sV + dst_off), srcV + so, bytes, bar_full);
-                    }
-                } else if (pass == 0) {
-                    for (uint32_t o = lane * 16; o < bytes; o += 32 * 16) {
-                        *(uint4 *)(sK + dst_off + o) = make_uint4(0, 0, 0, 0);
-                        *(uint4 *)(sV + dst_off + o) = make_uint4(0, 0, 0, 0);
-                    }
-                }
-            }
-            row += len;
+        }
+        fence_proxy_async();
+        __syncwarp();
+    }
+    if (lane == 0) {
+        if (total) mbar_arrive_expect_tx(bar_full, total);
+        else mbar_arrive(bar_full);
+    }
+    __syncwarp();
+    if (src) {
+        bulk_g2s(smem_addr(sK + dst), src, bytes, bar_full);
+        bulk_g2s(smem_addr(sV + dst), src + v_off, bytes, bar_full);
+    }
+}
+
+// ---- Q8_0 feeder: the raw stage holds, per segment of vbt = min(block_tokens, BN) rows, a K part
+// then a V part, each [qs vbt x D][fp16 scales vbt x D/32] -- exactly the pool's Q8_0 tile, so a
+// whole block whose K and V tiles are adjacent (one KV head) is ONE copy; otherwise one per tile,
+// or one per plane for a partial block. One lane per segment. ----
+template <int D>
+__device__ __forceinline__ void produce_q8_raw(const AttnArgs &a, const Plan &pl, const uint8_t *const *sPtr, int j,
+                                               uint8_t *raw, uint32_t bar_full, int lane) {
+    using C = TcCfg<D, true>;
+    constexpr int BN = C::BN, SCB = D / 16;  // scale bytes per row
+    const PoolView &p = a.pool;
+    const int bt = p.block_tokens;
+    const int vbt = min(bt, BN), n_seg = BN / vbt;
+    const uint32_t vtile = (uint32_t)vbt * (D + SCB);
+    const uint32_t part = 2 * vtile;
+    const uint8_t *tk = nullptr;
+    int rib = 0;
+    if (lane < n_seg) {
+        const int k = pl.kbeg + j * BN + lane * vbt;
+        const int idx = block_index(p, k, rib);
+        if (k < pl.sk.n_prefix) tk = ptr_of<C::TBL>(a, pl, sPtr, idx);
+    }
+    const uint32_t segmask = n_seg >= 32 ? 0xffffffffu : ((1u << n_seg) - 1u);
+    const uint32_t valid = __ballot_sync(0xffffffffu, tk != nullptr) & segmask;
+    const uint32_t missing = ~valid & segmask;
+    if (missing) {
+        for (uint32_t m = missing; m; m &= m - 1) {
+            uint8_t *z = raw + (__ffs(m) - 1) * part;
+            for (uint32_t o = lane * 16; o < part; o += 32 * 16) *(uint4 *)(z + o) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async();
+        __syncwarp();
+    }
+    if (lane == 0) {
+        if (valid) mbar_arrive_expect_tx(bar_full, (uint32_t)__popc(valid) * part);
+        else mbar_arrive(bar_full);
+    }
+    __syncwarp();
+    if (!tk) return;
+    const int64_t v_off = (int64_t)p.kv_heads * p.tile_bytes;  // V tile of the same head
+    uint8_t *dst = raw + lane * part;
+    if (vbt == bt) {
+        if (p.kv_heads == 1) {
+            bulk_g2s(smem_addr(dst), tk, part, bar_full);  // K tile + V tile, contiguous
+        } else {
+            bulk_g2s(smem_addr(dst), tk, vtile, bar_full);
+            bulk_g2s(smem_addr(dst + vtile), tk + v_off, vtile, bar_full);
+        }
+    } else {  // rows [rib, rib + BN) of a larger block: qs and scale planes separately
+        for (int kv = 0; kv < 2; ++kv) {
+            const uint8_t *sk = tk + kv * v_off;
+            uint8_t *d = dst + kv * vtile;
+            bulk_g2s(smem_addr(d), sk + (int64_t)rib * D, (uint32_t)BN * D, bar_full);
+            bulk_g2s(smem_addr(d + BN * D), sk + (int64_t)bt * D + (int64_t)rib * SCB, (uint32_t)BN * SCB, bar_full);
         }
     }
 }
@@ -244,7 +454,7 @@ __device__ __forceinline__ void dequant16(const uint4 q, uint32_t dbits, uint4 &
     hi = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
-__device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {
+[[maybe_unused]] __device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {
     uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -254,95 +464,80 @@ __device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <int D>
-struct Q8Raw {
-    static constexpr int BN = TcCfg<D, true>::BN;
-    static constexpr int PU = BN * (D / 16) / 128;  // prefix units (16 int8) per thread
-    static constexpr int SU = BN * (D / 8) / 128;   // suffix units (8 bf16) per thread
-    static constexpr int NU = PU > SU ? PU : SU;
-    uint4 k[NU], v[NU];
-    uint32_t dk[PU], dv[PU];
-};
 
+// raw stage -> f16 K/V operand stage (128 threads; every raw load before the first store).
+// Thread t always converts the same 16-column segment (t % (D/16)) of rows r0 + i*RS, so its
+// operand offsets are one base plus a constant stride per i.
 template <int D>
-__device__ __forceinline__ void q8_load_tile(const AttnArgs &a, const Plan &pl, int j, int ptid, Q8Raw<D> &raw) {
-    constexpr int BN = TcCfg<D, true>::BN;
-    const PoolView &p = a.pool;
-    if (j >= pl.np_tiles) {
-        const int s_base = (j - pl.np_tiles) * BN;
-        const uint8_t *tk = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 0, pl.g) * p.suffix_tile_bytes;
-        const uint8_t *tv = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 1, pl.g) * p.suffix_tile_bytes;
+__device__ __forceinline__ void dequant_tile(const uint8_t *raw, uint8_t *sK, uint8_t *sV, int vbt_shift, int dtid) {
+    using C = TcCfg<D, true>;
+    constexpr int BN = C::BN, W = C::W, UPR = D / 16, RS = kDq / UPR, PER = BN / RS, SCB = D / 16;
+    static_assert(kDq % UPR == 0 && RS % 8 == 0 && BN % RS == 0, "dequant thread mapping");
+    const int seg = dtid % UPR, r0 = dtid / UPR;
+    const int vbt = 1 << vbt_shift;
+    const uint32_t vtile = (uint32_t)vbt * (D + SCB);
+    uint4 qk[PER], qv[PER];
+    uint32_t dk[PER], dv[PER];
 #pragma unroll
-        for (int i = 0; i < Q8Raw<D>::SU; ++i) {
-            const int u = ptid + i * 128;
-            const int row = u / (D / 8);
-            const int d0 = (u - row * (D / 8)) * 8;
-            const int s = s_base + row;
-            if (s < p.suffix_rows) {
-                const uint32_t off = tile_elem_off(s, d0, p.suffix_rows, p.swz_bytes);
-                raw.k[i] = __ldg((const uint4 *)(tk + off));
-                raw.v[i] = __ldg((const uint4 *)(tv + off));
-            } else {
-                raw.k[i] = raw.v[i] = make_uint4(0, 0, 0, 0);
-            }
-        }
-        return;
+    for (int i = 0; i < PER; ++i) {
+        const int row = r0 + i * RS;
+        const int s = row >> vbt_shift, rib = row & (vbt - 1);
+        const uint8_t *kt = raw + s * 2 * vtile;
+        const uint32_t qo = rib * D + seg * 16, so = vbt * D + rib * SCB + (seg >> 1) * 2;
+        qk[i] = *(const uint4 *)(kt + qo);
+        dk[i] = *(const uint16_t *)(kt + so);
+        qv[i] = *(const uint4 *)(kt + vtile + qo);
+        dv[i] = *(const uint16_t *)(kt + vtile + so);
     }
-    const int groups = D / 32;
+    const uint32_t off_lo = tile_elem_off(r0, seg * 16, D, W), off_hi = tile_elem_off(r0, seg * 16 + 8, D, W);
+    constexpr uint32_t STEP = (RS / 8) * C::SBO;
 #pragma unroll
-    for (int i = 0; i < Q8Raw<D>::PU; ++i) {
-        const int u = ptid + i * 128;
-        const int row = u / (D / 16);
-        const int seg = u - row * (D / 16);
-        const int k = pl.kbeg + j * BN + row;
-        raw.k[i] = raw.v[i] = make_uint4(0, 0, 0, 0);
-        raw.dk[i] = raw.dv[i] = 0;
-        if (k < pl.sk.n_prefix) {
-            const int blk = lookup_block(p, pl.sk.seq, k / p.block_tokens);
-            if (blk >= 0) {
-                const int rib = k % p.block_tokens;
-                const uint8_t *tk = p.prefix + prefix_tile_index(p, a.layer, blk, 0, pl.g) * p.tile_bytes;
-                const uint8_t *tv = p.prefix + prefix_tile_index(p, a.layer, blk, 1, pl.g) * p.tile_bytes;
-                const int64_t qo = (int64_t)rib * D + seg * 16;
-                const int64_t so = (int64_t)p.block_tokens * D + ((int64_t)rib * groups + seg / 2) * 2;
-                raw.k[i] = __ldg((const uint4 *)(tk + qo));
-                raw.v[i] = __ldg((const uint4 *)(tv + qo));
-                raw.dk[i] = __ldg((const uint16_t *)(tk + so));
-                raw.dv[i] = __ldg((const uint16_t *)(tv + so));
-            }
-        }
+    for (int i = 0; i < PER; ++i) {
+        uint4 lo, hi;
+        dequant16(qk[i], dk[i], lo, hi);
+        *(uint4 *)(sK + off_lo + i * STEP) = lo;
+        *(uint4 *)(sK + off_hi + i * STEP) = hi;
+        dequant16(qv[i], dv[i], lo, hi);
+        *(uint4 *)(sV + off_lo + i * STEP) = lo;
+        *(uint4 *)(sV + off_hi + i * STEP) = hi;
     }
 }
 
+// bf16 suffix slot -> f16 K/V operand stage (Q8_0 pools), 4 units in flight per thread
 template <int D>
-__device__ __forceinline__ void q8_store_tile(const Plan &pl, int j, int ptid, const Q8Raw<D> &raw, uint8_t *sK,
-                                              uint8_t *sV) {
+__device__ __forceinline__ void convert_suffix_tile(const AttnArgs &a, const Plan &pl, int j, uint8_t *sK, uint8_t *sV,
+                                                    int dtid) {
     using C = TcCfg<D, true>;
-    constexpr int BN = C::BN, W = C::W;
-    if (j >= pl.np_tiles) {
+    constexpr int BN = C::BN, W = C::W, UPR = D / 8, UNITS = BN * UPR;
+    const PoolView &p = a.pool;
+    const int s_base = (j - pl.np_tiles) * BN;
+    const uint8_t *tk = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 0, pl.g) * p.suffix_tile_bytes;
+    const uint8_t *tv = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 1, pl.g) * p.suffix_tile_bytes;
+#pragma unroll 1
+    for (int u0 = 0; u0 < UNITS; u0 += 4 * kDq) {
+        uint4 kk[4], vv[4];
 #pragma unroll
-        for (int i = 0; i < Q8Raw<D>::SU; ++i) {
-            const int u = ptid + i * 128;
-            const int row = u / (D / 8);
-            const int d0 = (u - row * (D / 8)) * 8;
-            const uint32_t off = tile_elem_off(row, d0, BN, W);
-            *(uint4 *)(sK + off) = bf16x8_to_f16x8(raw.k[i]);
-            *(uint4 *)(sV + off) = bf16x8_to_f16x8(raw.v[i]);
+        for (int i = 0; i < 4; ++i) {
+            const int u = u0 + dtid + i * kDq;
+            const int row = u / UPR, d0 = (u - row * UPR) * 8, srow = s_base + row;
+            kk[i] = vv[i] = make_uint4(0, 0, 0, 0);
+            if (u < UNITS && srow < p.suffix_rows) {
+                const uint32_t off = tile_elem_off(srow, d0, D, W);
+                kk[i] = __ldg((const uint4 *)(tk + off));
+                vv[i] = __ldg((const uint4 *)(tv + off));
+            }
         }
-        return;
-    }
 #pragma unroll
-    for (int i = 0; i < Q8Raw<D>::PU; ++i) {
-        const int u = ptid + i * 128;
-        const int row = u / (D / 16);
-        const int d0 = (u - row * (D / 16)) * 16;
-        uint4 lo, hi;
-        dequant16(raw.k[i], raw.dk[i], lo, hi);
-        *(uint4 *)(sK + tile_elem_off(row, d0, BN, W)) = lo;
-        *(uint4 *)(sK + tile_elem_off(row, d0 + 8, BN, W)) = hi;
-        dequant16(raw.v[i], raw.dv[i], lo, hi);
-        *(uint4 *)(sV + tile_elem_off(row, d0, BN, W)) = lo;
-        *(uint4 *)(sV + tile_elem_off(row, d0 + 8, BN, W)) = hi;
+        for (int i = 0; i < 4; ++i) {
+            const int u = u0 + dtid + i * kDq;
+            if (u >= UNITS) break;
+            const int row = u / UPR, d0 = (u - row * UPR) * 8;
+            const uint32_t off = tile_elem_off(row, d0, D, W);
+            *(uint4 *)(sK + off) = make_uint4(bf16x2_to_f16x2(kk[i].x), bf16x2_to_f16x2(kk[i].y),
+                                              bf16x2_to_f16x2(kk[i].z), bf16x2_to_f16x2(kk[i].w));
+            *(uint4 *)(sV + off) = make_uint4(bf16x2_to_f16x2(vv[i].x), bf16x2_to_f16x2(vv[i].y),
+                                              bf16x2_to_f16x2(vv[i].z), bf16x2_to_f16x2(vv[i].w));
+        }
     }
 }
 
@@ -354,27 +549,36 @@ __device__ __forceinline__ void fail_timeout(const AttnArgs &a, volatile int *ab
 template <int D, bool Q8>
 __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const AttnArgs a, int n_qtiles) {
     using C = TcCfg<D, Q8>;
-    constexpr int BN = C::BN, W = C::W;
+    constexpr int BN = C::BN, W = C::W, NS = C::NSTAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *sQ = smem + C::OFF_Q;
     uint8_t *sK = smem + C::OFF_K;
     uint8_t *sV = smem + C::OFF_V;
-    uint8_t *sP = smem + C::OFF_P;
+    uint8_t *sRaw = smem + C::OFF_RAW;
     uint64_t *bars = (uint64_t *)(smem + C::OFF_BAR);
     uint32_t *tmem_holder = (uint32_t *)(bars + N_BARS);
     volatile int *abort = (volatile int *)(bars + N_BARS + 1);
+    const uint8_t **sPtr = (const uint8_t **)(smem + C::OFF_TBL);
     const uint32_t bar0 = smem_addr(bars);
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) {
+        TRACE(0);
+        TRACE_CLK(20);
+    }
     const Plan pl = make_plan<BN>(a, n_qtiles);
+    if (threadIdx.x == 0) TRACE(1);
     if (threadIdx.x == 0 && !pl.sk.ok) report_error(a.pool.status, DEV_ERR_BAD_SEQ, pl.b, a.seq_ids[pl.b], 3);
 
     if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(bar(BAR_OP_FULL + s), Q8 ? kDq : 1);
+            mbar_init(bar(BAR_OP_EMPTY + s), 1);
+        }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(bar(BAR_KV_FULL + s), Q8 ? 128 : 1);
-            mbar_init(bar(BAR_KV_EMPTY + s), 1);
+            mbar_init(bar(BAR_RAW_FULL + s), 1);
+            mbar_init(bar(BAR_RAW_EMPTY + s), kDq);
             mbar_init(bar(BAR_S_FULL + s), 1);
             mbar_init(bar(BAR_P_FULL + s), 128);
             mbar_init(bar(BAR_P_EMPTY + s), 1);
@@ -384,133 +588,223 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
         mbar_init_fence();
     }
     if (warp == C::MMA_WARP) tmem_alloc(smem_addr(tmem_holder), C::TMEM_COLS);
-    load_q_tile<D, Q8>(a, pl, sQ);
-    fence_proxy_async();
+    QStage<D, Q8> qstage;
+    stage_q_load<D, Q8>(a, pl, qstage);  // Q loads in flight while the table is read
+    // tile base pointers of the split's block-table entries, validated once, in shared memory
+    if (pl.tbl_n <= C::TBL)
+        for (int i = threadIdx.x; i < pl.tbl_n; i += C::THREADS) {
+            const int blk = lookup_block(a.pool, pl.sk.seq, pl.tbl_lo + i);
+            sPtr[i] = blk < 0 ? nullptr
+                              : a.pool.prefix + prefix_tile_index(a.pool, a.layer, blk, 0, pl.g) * a.pool.tile_bytes;
+        }
+    stage_q_store<D, Q8>(qstage, smem + C::OFF_K);
+    if (threadIdx.x == 0) TRACE(2);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    const uint32_t lane_base = ((uint32_t)((warp & 3) * 32)) << 16;
+    if (warp < 4) {
+        q_to_tmem<D, Q8>(smem + C::OFF_K, threadIdx.x, tmem + lane_base + C::Q_COL);
+        tmem_wait_st();
+    }
+    fence_proxy_async();  // staging reads (generic) before the copy engine refills the stages
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) TRACE(3);
     const int n = pl.j1 - pl.j0;
 
     if (warp == C::MMA_WARP) {
-        if (lane == 0 && n > 0) {
+        if (n > 0) {
+            // The whole warp runs the schedule (warp-uniform descriptors and decisions); lane 0
+            // issues the tcgen05 instructions.
             const uint32_t idS = idesc_f16(!Q8, false, BN);
             const uint32_t idO = idesc_f16(!Q8, true, D);
-            const uint32_t q_addr = smem_addr(sQ), k_addr = smem_addr(sK), v_addr = smem_addr(sV),
-                           p_addr = smem_addr(sP);
+            const uint32_t k_addr = smem_addr(sK), v_addr = smem_addr(sV);
             bool ok = true;
             auto issue_s = [&](int jj) {
-                const int st = jj & 1;
-                if (!mbar_wait(bar(BAR_KV_FULL + st), (jj >> 1) & 1, abort, kWaitBudget)) return false;
+                const int st = jj % NS, sb = jj & 1;
+                if (jj < 50 && lane == 0) TRACE(400 + jj);
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + (uint32_t)(st * BN);
+                const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)(sb * BN);
+                const uint64_t bd0 = sdesc(k_addr + st * C::KV_BYTES, 16, C::SBO, C::LAYOUT);
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t byte = (uint32_t)kk * 32u;
-                    const uint32_t chunk = byte / W, within = byte % W;
-                    const uint64_t ad = sdesc(q_addr + chunk * (kBM * W) + within, 16, 8 * W, C::LAYOUT);
-                    const uint64_t bd =
-                        sdesc(k_addr + st * C::KV_BYTES + chunk * (BN * W) + within, 16, 8 * W, C::LAYOUT);
-                    mma_ss(d_tmem, ad, bd, idS, kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        constexpr int KPC = W / 32;  // K-steps per swizzle chunk
+                        const uint32_t off = (uint32_t)(kk / KPC) * (8 * W) + (uint32_t)(kk % KPC) * 32u;
+                        mma_ts(d_tmem, tmem + C::Q_COL + (uint32_t)(kk * 8), bd0 + (off >> 4), idS, kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(bar(BAR_S_FULL + sb));
                 }
-                mma_commit(bar(BAR_S_FULL + st));
-                return true;
+                __syncwarp();
+                if (jj < 50 && lane == 0) TRACE(200 + jj);
             };
-            ok = issue_s(0);
-            for (int jj = 0; ok && jj < n; ++jj) {
-                if (jj + 1 < n && !(ok = issue_s(jj + 1))) break;
-                const int st = jj & 1;
-                if (!(ok = mbar_wait(bar(BAR_P_FULL + st), (jj >> 1) & 1, abort, kWaitBudget))) break;
+            auto issue_pv = [&](int jj) {
+                const int st = jj % NS, sb = jj & 1;
                 tc_fence_after();
+                const uint64_t bd0 = sdesc(v_addr + st * C::KV_BYTES, 8 * W, C::SBO, C::LAYOUT);
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint32_t byte = (uint32_t)kk * 32u;
-                    const uint64_t ad = sdesc(p_addr + st * C::P_BYTES + (byte / 128) * (kBM * 128) + byte % 128, 16,
-                                              1024, 2u);
-                    const uint64_t bd = sdesc(v_addr + st * C::KV_BYTES + (uint32_t)kk * 16u * W, BN * W, 8 * W,
-                                              C::LAYOUT);
-                    mma_ss(tmem + C::O_COL, ad, bd, idO, (jj > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < BN / 16; ++kk)
+                        mma_ts(tmem + C::O_COL, tmem + C::S_COL + (uint32_t)(sb * BN + kk * 8),
+                               bd0 + ((uint32_t)kk * 2u * C::SBO >> 4), idO, (jj > 0 || kk > 0) ? 1u : 0u);
+                    mma_commit(bar(BAR_OP_EMPTY + st));
+                    mma_commit(bar(BAR_P_EMPTY + sb));
                 }
-                mma_commit(bar(BAR_KV_EMPTY + st));
-                mma_commit(bar(BAR_P_EMPTY + st));
+                __syncwarp();
+                if (jj < 50 && lane == 0) TRACE(250 + jj);
+            };
+            // S(j) needs its K stage and its S buffer (P(j-2) consumed: P.V(j-2) issued, and the
+            // tensor core executes in issue order); P.V(j) needs P(j).
+            int next_s = 0, next_pv = 0;
+            long long t_prog = clock64();
+            while (next_pv < n) {
+                int act = 0;
+                if (lane == 0) {
+                    if (next_s < n && next_s <= next_pv + 1 &&
+                        mbar_test_wait(bar(BAR_OP_FULL + next_s % NS), (next_s / NS) & 1))
+                        act = 1;
+                    else if (next_pv < next_s &&
+                             mbar_test_wait(bar(BAR_P_FULL + (next_pv & 1)), (next_pv >> 1) & 1))
+                        act = 2;
+                }
+                act = __shfl_sync(0xffffffffu, act, 0);
+                if (act == 1) {
+                    issue_s(next_s++);
+                    t_prog = clock64();
+                } else if (act == 2) {
+                    issue_pv(next_pv++);
+                    t_prog = clock64();
+                } else if (__shfl_sync(0xffffffffu, (*abort || clock64() - t_prog > kWaitBudget) ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
             }
-            if (!ok) fail_timeout(a, abort, 1);
-            // Every MMA this thread issued must have finished before TMEM is released.
-            mma_commit(bar(BAR_DONE));
-            mbar_wait(bar(BAR_DONE), 0, abort, kWaitBudget);
+            if (lane == 0) {
+                if (!ok) fail_timeout(a, abort, 1);
+                // Every MMA this warp issued must have finished before TMEM is released.
+                mma_commit(bar(BAR_DONE));
+                mbar_wait(bar(BAR_DONE), 0, abort, kWaitBudget);
+            }
+            __syncwarp();
         }
-    } else if (warp >= C::PROD_WARP0) {
-        const int ptid = threadIdx.x - C::PROD_WARP0 * 32;
+    } else if (warp == C::TMA_WARP) {
+        // copy-engine feeder
+        int issued = 0;
+        for (int jj = 0; jj < n; ++jj) {
+            const int j = pl.j0 + jj;
+            if constexpr (Q8) {
+                if (j >= pl.np_tiles) break;  // suffix tiles are converted by the dequant warps
+                const int r = jj % C::NRAW;
+                if (jj >= C::NRAW &&
+                    !mbar_wait(bar(BAR_RAW_EMPTY + r), ((jj - C::NRAW) / C::NRAW) & 1, abort, kWaitBudget)) {
+                    fail_timeout(a, abort, 2);
+                    break;
+                }
+                if (lane == 0 && jj < 50) TRACE(450 + jj);
+                produce_q8_raw<D>(a, pl, (const uint8_t *const *)sPtr, j, sRaw + r * C::RAW_BYTES, bar(BAR_RAW_FULL + r), lane);
+            } else {
+                const int st = jj % NS;
+                if (jj >= NS && !mbar_wait(bar(BAR_OP_EMPTY + st), ((jj - NS) / NS) & 1, abort, kWaitBudget)) {
+                    fail_timeout(a, abort, 2);
+                    break;
+                }
+                if (lane == 0 && jj < 50) TRACE(450 + jj);
+                produce_bf16_tile<D>(a, pl, (const uint8_t *const *)sPtr, j, sK + st * C::KV_BYTES, sV + st * C::KV_BYTES,
+                                     bar(BAR_OP_FULL + st), lane);
+            }
+            issued = jj + 1;
+            if (lane == 0 && jj < 50) TRACE(150 + jj);
+        }
+        // Do not leave the CTA with bulk copies still writing shared memory.
+        if (lane == 0 && *abort) {
+            constexpr int depth = Q8 ? C::NRAW : NS;
+            for (int jj = max(0, issued - depth); jj < issued; ++jj) {
+                const uint32_t b = Q8 ? bar(BAR_RAW_FULL + jj % depth) : bar(BAR_OP_FULL + jj % depth);
+                mbar_wait(b, (jj / depth) & 1, abort, kWaitBudget / 4);
+            }
+        }
+    } else if (warp >= C::DQ_WARP0) {
         if constexpr (Q8) {
-            Q8Raw<D> raw;
+            const int dtid = threadIdx.x - C::DQ_WARP0 * 32;
+            const int vbt = min(a.pool.block_tokens, BN);
+            const int vbt_shift = 31 - __clz(vbt);  // power of two: checked by the launcher
             for (int jj = 0; jj < n; ++jj) {
-                const int st = jj & 1;
-                q8_load_tile<D>(a, pl, pl.j0 + jj, ptid, raw);
-                if (jj >= 2 && !mbar_wait(bar(BAR_KV_EMPTY + st), ((jj - 2) >> 1) & 1, abort, kWaitBudget)) {
-                    fail_timeout(a, abort, 2);
+                const int j = pl.j0 + jj, st = jj % NS;
+                const bool prefix = j < pl.np_tiles;
+                if (prefix && !mbar_wait(bar(BAR_RAW_FULL + jj % C::NRAW), (jj / C::NRAW) & 1, abort, kWaitBudget)) {
+                    fail_timeout(a, abort, 5);
                     break;
                 }
-                q8_store_tile<D>(pl, pl.j0 + jj, ptid, raw, sK + st * C::KV_BYTES, sV + st * C::KV_BYTES);
+                if (dtid == 0 && jj < 50) TRACE(500 + jj);
+                if (jj >= NS && !mbar_wait(bar(BAR_OP_EMPTY + st), ((jj - NS) / NS) & 1, abort, kWaitBudget)) {
+                    fail_timeout(a, abort, 6);
+                    break;
+                }
+                if (dtid == 0 && jj < 50) TRACE(550 + jj);
+                if (prefix) {
+                    dequant_tile<D>(sRaw + (jj % C::NRAW) * C::RAW_BYTES, sK + st * C::KV_BYTES,
+                                    sV + st * C::KV_BYTES, vbt_shift, dtid);
+                    if (dtid == 0 && jj < 50) TRACE(800 + jj);
+                    fence_proxy_async();
+                    mbar_arrive(bar(BAR_RAW_EMPTY + jj % C::NRAW));
+                } else {
+                    convert_suffix_tile<D>(a, pl, j, sK + st * C::KV_BYTES, sV + st * C::KV_BYTES, dtid);
+                }
                 fence_proxy_async();
-                mbar_arrive(bar(BAR_KV_FULL + st));
-            }
-        } else {
-            for (int jj = 0; jj < n; ++jj) {
-                const int st = jj & 1;
-                if (jj >= 2 && !mbar_wait(bar(BAR_KV_EMPTY + st), ((jj - 2) >> 1) & 1, abort, kWaitBudget)) {
-                    fail_timeout(a, abort, 2);
-                    break;
-                }
-                produce_bf16_tile<D>(a, pl, pl.j0 + jj, sK + st * C::KV_BYTES, sV + st * C::KV_BYTES,
-                                     bar(BAR_KV_FULL + st), lane);
-            }
-            // Do not leave the CTA with bulk copies still writing shared memory.
-            if (lane == 0 && n > 0 && *abort) {
-                for (int jj = max(0, n - 2); jj < n; ++jj)
-                    mbar_wait(bar(BAR_KV_FULL + (jj & 1)), (jj >> 1) & 1, abort, kWaitBudget / 4);
+                mbar_arrive(bar(BAR_OP_FULL + st));
+                if (dtid == 0 && jj < 50) TRACE(100 + jj);
             }
         }
-    } else {
+    } else if (warp < 4) {
         // ---- softmax / epilogue: thread = query row = TMEM lane ----
         const int r = threadIdx.x;
         const bool row_ok = r < pl.rows_valid;
         const int qr = pl.qrow0 + r;
         const int t = qr / a.group;
-        const uint32_t lane_base = ((uint32_t)(warp * 32)) << 16;
         const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
         const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
         const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
         float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int jj = 0; jj < n; ++jj) {
-            const int st = jj & 1;
+            const int sb = jj & 1;
             const int j = pl.j0 + jj;
-            if (!(ok = mbar_wait(bar(BAR_S_FULL + st), (jj >> 1) & 1, abort, kWaitBudget))) break;
+            if (!(ok = mbar_wait(bar(BAR_S_FULL + sb), (jj >> 1) & 1, abort, kWaitBudget))) break;
             tc_fence_after();
-            float x[BN];
-#pragma unroll
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                uint32_t rr[32];
-                tmem_load32(tmem + lane_base + (uint32_t)(st * BN + c0), rr);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) x[c0 + i] = __uint_as_float(rr[i]);
-            }
-            // mask + scale (exp2 domain)
+            if (r == 0 && jj < 50) TRACE(300 + jj);
             const bool suffix = j >= pl.np_tiles;
             const int key0 = suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN;
             const bool all_vis = row_ok && (suffix ? (suffix_simple && key0 + BN <= a.suffix_len)
                                                    : (prefix_simple && key0 + BN <= pl.sk.prefix_valid));
-            float m_tile = -INFINITY;
+            uint32_t vis_bits[BN / 32];
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                bool vis = all_vis;
-                if (!all_vis && row_ok) {
-                    vis = suffix ? suffix_allowed(m, t, key0 + c, a.suffix_len)
-                                 : prefix_allowed(m, t, key0 + c, pl.sk.prefix_valid, pl.sk.span_b, pl.sk.span_e);
+            for (int w = 0; w < BN / 32; ++w)
+                vis_bits[w] = all_vis ? 0xffffffffu
+                                      : (row_ok ? vis_word(m, suffix, key0 + 32 * w, t, pl.sk.prefix_valid, pl.sk.span_b,
+                                                           pl.sk.span_e, a.suffix_len)
+                                                : 0u);
+            // the S row is read in 32-column halves twice (max, then exponentials): only 32
+            // scores are live at a time; P (16-bit) goes back over the consumed S columns.
+            // The max is taken on raw scores and scaled once (scale > 0).
+            const uint32_t s_col = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
+            float s_max = -INFINITY;
+#pragma unroll
+            for (int h32 = 0; h32 < BN / 32; ++h32) {
+                uint32_t rr[32];
+                tmem_load32(s_col + h32 * 32, rr);
+                if (all_vis) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) s_max = fmaxf(s_max, __uint_as_float(rr[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if ((vis_bits[h32] >> i) & 1u) s_max = fmaxf(s_max, __uint_as_float(rr[i]));
                 }
-                x[c] = vis ? x[c] * a.scale_log2 : -INFINITY;
-                m_tile = fmaxf(m_tile, x[c]);
             }
+            const float m_tile = s_max * a.scale_log2;
             float alpha = 1.0f;
             bool rescale = false;
             if (m_tile > m_used) {
@@ -523,20 +817,12 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                     rescale = true;
                 }
             }
-            float psum = 0.0f;
-#pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                const float pv = (x[c] == -INFINITY) ? 0.0f : ex2(x[c] - m_used);
-                x[c] = pv;
-                psum += pv;
-            }
-            l += psum;
             if (__any_sync(0xffffffffu, rescale)) {
                 // O may only be touched once the previous P.V has landed in TMEM.
                 if (!(ok = mbar_wait(bar(BAR_P_EMPTY + ((jj - 1) & 1)), ((jj - 1) >> 1) & 1, abort, kWaitBudget)))
                     break;
                 tc_fence_after();
-#pragma unroll
+#pragma unroll 1
                 for (int c0 = 0; c0 < D; c0 += 16) {
                     uint32_t rr[16];
                     tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), rr);
@@ -546,29 +832,40 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                 }
                 tmem_wait_st();
             }
-            if (jj >= 2 && !(ok = mbar_wait(bar(BAR_P_EMPTY + st), ((jj - 2) >> 1) & 1, abort, kWaitBudget))) break;
-            uint8_t *pbuf = sP + st * C::P_BYTES;
+            float psum = 0.0f;
+            const float neg_m = -m_used;
+            const bool any_vis = m_used != -INFINITY;
 #pragma unroll
-            for (int c8 = 0; c8 < BN / 8; ++c8) {
-                uint32_t w[4];
+            for (int h32 = 0; h32 < BN / 32; ++h32) {
+                uint32_t rr[32];
+                tmem_load32(s_col + h32 * 32, rr);
+                uint32_t pw[16];
+                const uint32_t vb = all_vis ? 0xffffffffu : (any_vis ? vis_bits[h32] : 0u);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float lo = x[c8 * 8 + 2 * i], hi = x[c8 * 8 + 2 * i + 1];
+                for (int i = 0; i < 16; ++i) {
+                    float pr[2];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int c = 2 * i + e;
+                        const float x = ex2(fmaf(__uint_as_float(rr[c]), a.scale_log2, neg_m));
+                        pr[e] = ((vb >> c) & 1u) ? x : 0.0f;
+                        psum += pr[e];
+                    }
                     if (Q8) {
-                        const __half2 h2 = __floats2half2_rn(lo, hi);
-                        w[i] = *(const uint32_t *)&h2;
+                        const __half2 h2 = __floats2half2_rn(pr[0], pr[1]);
+                        pw[i] = *(const uint32_t *)&h2;
                     } else {
-                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
-                        w[i] = *(const uint32_t *)&b2;
+                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(pr[0], pr[1]);
+                        pw[i] = *(const uint32_t *)&b2;
                     }
                 }
-                const uint32_t byte = (uint32_t)c8 * 16u;
-                const uint32_t off = (byte / 128) * (kBM * 128) + swz((uint32_t)r * 128u + byte % 128, 7u);
-                *(uint4 *)(pbuf + off) = make_uint4(w[0], w[1], w[2], w[3]);
+                tmem_st16(s_col + h32 * 16, pw);
             }
-            fence_proxy_async();
+            l += psum;
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(BAR_P_FULL + st));
+            mbar_arrive(bar(BAR_P_FULL + sb));
+            if (r == 0 && jj < 50) TRACE(350 + jj);
         }
         if (!ok) fail_timeout(a, abort, 3);
         if (ok && n > 0) {
@@ -577,13 +874,14 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
             tc_fence_after();
         }
         // ---- epilogue ----
+        if (r == 0) TRACE(10);
         const bool have_o = ok && n > 0;
         const int h = pl.g * a.group + (qr - t * a.group);
         if (a.n_splits > 1) {
             const int64_t unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
             float *wo = a.ws_o + (unit * kBM + r) * D;
             float *wml = a.ws_ml + (unit * kBM + r) * 2;
-#pragma unroll
+#pragma unroll 1
             for (int c0 = 0; c0 < D; c0 += 16) {
                 uint32_t rr[16];
                 if (have_o) {
@@ -604,45 +902,68 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                 wml[1] = have_o ? l : 0.0f;
             }
         } else {
+            // O/l (bf16 or f32) -> shared staging row r -> each warp writes whole rows with
+            // consecutive 16-byte lanes (the K/V stages are idle once the last P.V has landed).
             const float inv = (have_o && l > 0.0f) ? 1.0f / l : 0.0f;
-            const int64_t obase = (((int64_t)pl.b * a.q_tokens + t) * a.q_heads + h) * D;
-#pragma unroll
-            for (int c0 = 0; c0 < D; c0 += 16) {
-                uint32_t rr[16];
+            const bool f32 = a.out_dtype == EKV_DTYPE_F32;
+            uint8_t *orow = smem + C::OFF_K + r * C::OSTR;
+            constexpr int EC = (D % 32 == 0) ? 32 : 16;  // columns per TMEM load
+#pragma unroll 2
+            for (int c0 = 0; c0 < D; c0 += EC) {
+                uint32_t rr[32];
                 if (have_o) {
-                    tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), rr);
+                    if constexpr (EC == 32) {
+                        tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), rr);
+                    } else {
+                        uint32_t (&r16)[16] = *reinterpret_cast<uint32_t (*)[16]>(rr);
+                        tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), r16);
+                    }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) rr[i] = 0u;
+                    for (int i = 0; i < EC; ++i) rr[i] = 0u;
                 }
-                if (!row_ok) continue;
-                if (a.out_dtype == EKV_DTYPE_F32) {
-                    float *o = (float *)a.out + obase + c0;
+                if (f32) {
 #pragma unroll
-                    for (int i = 0; i < 16; i += 4)
-                        *(float4 *)(o + i) =
+                    for (int i = 0; i < EC; i += 4)
+                        *(float4 *)(orow + (c0 + i) * 4) =
                             make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
                                         __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
                 } else {
-                    uint32_t w[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(rr[2 * i]) * inv,
-                                                                        __uint_as_float(rr[2 * i + 1]) * inv);
-                        w[i] = *(const uint32_t *)&b2;
+                    for (int i0 = 0; i0 < EC; i0 += 8) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(rr[i0 + 2 * i]) * inv,
+                                                                            __uint_as_float(rr[i0 + 2 * i + 1]) * inv);
+                            w[i] = *(const uint32_t *)&b2;
+                        }
+                        *(uint4 *)(orow + (c0 + i0) * 2) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
-                    uint4 *o = (uint4 *)((uint16_t *)a.out + obase + c0);
-                    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
                 }
             }
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 softmax warps only
+            const int row_bytes = D * (f32 ? 4 : 2);
+            for (int rw = warp; rw < pl.rows_valid; rw += 4) {
+                const int qrw = pl.qrow0 + rw;
+                const int tw = qrw / a.group;
+                const int hw = pl.g * a.group + (qrw - tw * a.group);
+                uint8_t *dst = (uint8_t *)a.out + ((((int64_t)pl.b * a.q_tokens + tw) * a.q_heads + hw) * D) * (f32 ? 4 : 2);
+                const uint8_t *srow = smem + C::OFF_K + rw * C::OSTR;
+                for (int o = lane * 16; o < row_bytes; o += 32 * 16) *(uint4 *)(dst + o) = *(const uint4 *)(srow + o);
+            }
         }
+    }
+    if (threadIdx.x == 0) {
+        TRACE(11);
+        TRACE_CLK(21);
     }
     __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (warp == C::MMA_WARP) tmem_dealloc(tmem, C::TMEM_COLS);
+    if (threadIdx.x == 0) TRACE(12);
 }
 
 // Combine the per-split partial outputs: O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
@@ -714,6 +1035,8 @@ int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
             return EKV_ERR_CUDA;
         attr_done[dev] = 1;
     }
+    const int bt = a.pool.block_tokens;
+    if (C::BN % bt != 0 && bt % C::BN != 0) return EKV_ERR_UNSUPPORTED;  // blocks must tile key tiles
     const int n_qtiles = (a.q_tokens * a.group + kBM - 1) / kBM;
     const int64_t units = (int64_t)a.n_batch * a.pool.kv_heads * n_qtiles;
     if (a.n_splits == 0) {
@@ -753,6 +1076,14 @@ int dispatch(const AttnArgs &a, cudaStream_t s, size_t ws) {
 }
 
 }  // namespace
+
+#ifdef EKV_TRACE
+}  // namespace ekv
+extern "C" int ekv_debug_set_trace(unsigned long long *buf) {
+    return cudaMemcpyToSymbol(ekv::g_trace, &buf, sizeof(buf)) == cudaSuccess ? 0 : -2;
+}
+namespace ekv {
+#endif
 
 size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix) {
     if (prm.q_heads <= 0 || p.kv_heads <= 0 || prm.q_heads % p.kv_heads) return 0;

@@ -55,7 +55,7 @@ __global__ void append_bf16_kernel(PoolView p, int layer, const int32_t *__restr
     const int64_t src = (((int64_t)src_row[b] + r) * p.kv_heads + h) * p.head_dim + d0;
     const uint4 val = (kv ? v : k)[src / 8];
     uint8_t *tile = p.prefix + prefix_tile_index(p, layer, blk, kv, h) * p.tile_bytes;
-    *(uint4 *)(tile + tile_elem_off(rib, d0, p.block_tokens, p.swz_bytes)) = val;
+    *(uint4 *)(tile + tile_elem_off(rib, d0, p.head_dim, p.swz_bytes)) = val;
 }
 
 // Q8_0 append: one thread quantises one 32-element group of one (row, kv, head).
@@ -135,7 +135,7 @@ __global__ void append_suffix_kernel(PoolView p, int layer, const int32_t *__res
     const int64_t src = (((int64_t)b * n_rows + r) * p.kv_heads + h) * p.head_dim + d0;
     const uint4 val = (kv ? v : k)[src / 8];
     uint8_t *tile = p.suffix + suffix_tile_index(p, layer, seq, kv, h) * p.suffix_tile_bytes;
-    *(uint4 *)(tile + tile_elem_off(r, d0, p.suffix_rows, p.swz_bytes)) = val;
+    *(uint4 *)(tile + tile_elem_off(r, d0, p.head_dim, p.swz_bytes)) = val;
 }
 
 // Gather of bf16 tiles (prefix or suffix) back to [rows][kv_heads][head_dim].
@@ -155,13 +155,13 @@ __global__ void gather_bf16_kernel(PoolView p, int layer, int seq, int pos0, int
     uint32_t off;
     if (from_suffix) {
         tile = p.suffix + suffix_tile_index(p, layer, seq, kv, h) * p.suffix_tile_bytes;
-        off = tile_elem_off(r, d0, p.suffix_rows, p.swz_bytes);
+        off = tile_elem_off(r, d0, p.head_dim, p.swz_bytes);
     } else {
         const int pos = pos0 + r;
         const int blk = lookup_block(p, seq, pos / p.block_tokens);
         if (blk < 0) return;
         tile = p.prefix + prefix_tile_index(p, layer, blk, kv, h) * p.tile_bytes;
-        off = tile_elem_off(pos % p.block_tokens, d0, p.block_tokens, p.swz_bytes);
+        off = tile_elem_off(pos % p.block_tokens, d0, p.head_dim, p.swz_bytes);
     }
     const uint4 val = *(const uint4 *)(tile + off);
     const int64_t dst = ((int64_t)r * p.kv_heads + h) * p.head_dim + d0;

@@ -88,6 +88,9 @@ int ekv_pool_create(const ekv_pool_config *cfg, ekv_pool **out) {
     v.max_blocks_per_seq = c.max_blocks_per_seq;
     v.suffix_rows = (c.suffix_tokens + 7) / 8 * 8;
     v.swz_bytes = ekv::swizzle_bytes_for(c.head_dim);
+    v.bt_shift = -1;
+    for (int sh = 0; sh < 16; ++sh)
+        if ((1 << sh) == c.block_tokens) v.bt_shift = sh;
     v.tile_bytes = c.dtype == EKV_DTYPE_BF16
                        ? (int64_t)c.block_tokens * c.head_dim * 2
                        : (int64_t)c.block_tokens * c.head_dim + (int64_t)c.block_tokens * (c.head_dim / 32) * 2;

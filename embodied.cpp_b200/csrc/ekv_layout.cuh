@@ -3,9 +3,9 @@
 // HBM layout (one cudaMalloc per pool, all regions 1024-byte aligned):
 //
 //   prefix arena  [n_layers][n_blocks][2 (K,V)][kv_heads] tiles
-//     bf16 tile : block_tokens x head_dim bf16 stored as [D*2/W chunks][block_tokens rows][W bytes]
+//     bf16 tile : block_tokens x head_dim bf16 stored as [rows/8][D*2/W chunks][8 rows][W bytes]
 //                 with the tcgen05 shared-memory swizzle already applied (Swizzle<log2(W/16),4,3>,
-//                 W = 128, 64 or 32 bytes). One contiguous copy of a chunk lands in shared
+//                 W = 128, 64 or 32 bytes). One contiguous copy of a block lands in shared
 //                 memory as a canonical K-major operand (K) or MN-major operand (V) tile.
 //     Q8_0 tile : qs int8 [block_tokens][head_dim] followed by fp16 scales
 //                 [block_tokens][head_dim/32]; a gather re-interleaves them into ggml's
@@ -36,6 +36,7 @@ struct PoolView {
     int32_t max_blocks_per_seq;
     int32_t suffix_rows;      // rows per suffix tile (multiple of 8), 0 = none
     int32_t swz_bytes;        // W: row bytes of one swizzle chunk (128, 64 or 32)
+    int32_t bt_shift;         // log2(block_tokens) when it is a power of two, else -1
     int64_t tile_bytes;       // bytes of one (layer, block, kv, head) prefix tile
     int64_t suffix_tile_bytes;// bytes of one (layer, seq, kv, head) suffix tile
 };
@@ -59,12 +60,18 @@ __host__ __device__ inline uint32_t swz(uint32_t off, uint32_t mask) {
     return off ^ (((off >> 7) & mask) << 4);
 }
 
-// Byte offset of element (row, d) inside a bf16 tile with `rows` rows and chunk width W.
-__host__ __device__ inline uint32_t tile_elem_off(int row, int d, int rows, int W) {
+// Byte offset of element (row, d) inside a bf16 tile of head_dim D and swizzle chunk width W.
+// Row-group-major: [row / 8][chunk = 2d / W][row % 8][W bytes], swizzled inside each 8 x W atom.
+// The rows of one block (or any run of whole 8-row groups) are one contiguous byte range, and
+// in shared memory the tile is a canonical tcgen05 operand: K-major with 8-row groups at
+// SBO = (2D/W) * 8W bytes (K), or MN-major with D-chunks at LBO = 8W and the same SBO (V).
+__host__ __device__ inline uint32_t tile_elem_off(int row, int d, int D, int W) {
+    const int nch = D * 2 / W;
     const int byte = d * 2;
     const int chunk = byte / W;
     const int wb = byte - chunk * W;
-    return (uint32_t)chunk * (uint32_t)(rows * W) + swz((uint32_t)(row * W + wb), (uint32_t)(W / 16 - 1));
+    return (uint32_t)((row >> 3) * nch + chunk) * (uint32_t)(8 * W) +
+           swz((uint32_t)((row & 7) * W + wb), (uint32_t)(W / 16 - 1));
 }
 
 __host__ __device__ inline int64_t prefix_tile_index(const PoolView &p, int layer, int block, int kv,

@@ -14,7 +14,8 @@ import os
 from dataclasses import dataclass
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libekv.so")
+# EKV_LIB_PATH selects another build of the same library (e.g. a tracing build).
+LIB_PATH = os.environ.get("EKV_LIB_PATH") or os.path.join(HERE, "libekv.so")
 
 OK = 0
 ERR_INVALID_ARG, ERR_CUDA, ERR_POOL_EXHAUSTED, ERR_NO_SEQ = -1, -2, -3, -4
