@@ -25,7 +25,7 @@ __device__ __forceinline__ float load_elem(const PoolView &p, const KeySrc &s, i
         const uint16_t h = *(const uint16_t *)(s.tile + tile_elem_off(s.row, d, p.head_dim, p.swz_bytes));
         return bf16_bits_to_f32(h);
     }
-    const int8_t q = *(const int8_t *)(s.tile + (int64_t)s.row * p.head_dim + d);
+    const int8_t q = *(const int8_t *)(s.tile + q8_qs_off(s.row, d, p.head_dim));
     const uint16_t db = *((const uint16_t *)(s.tile + (int64_t)p.block_tokens * p.head_dim) +
                           s.row * (p.head_dim / 32) + d / 32);
     return (float)q * f16_bits_to_f32(db);

@@ -68,7 +68,7 @@ __device__ __forceinline__ void trace_clock(int slot) {
 constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (~2-3 s) before giving up
 constexpr int kBM = 128;
 constexpr int kMaxSplits = 8;
-constexpr int kDq = 128;  // dequantising threads (Q8_0)
+constexpr int kDq = 256;  // dequantising threads (Q8_0): 8 warps, two per SM sub-partition
 
 template <int D, bool Q8>
 struct TcCfg {
@@ -465,15 +465,18 @@ __device__ __forceinline__ void dequant16(const uint4 q, uint32_t dbits, uint4 &
 }
 
 
-// raw stage -> f16 K/V operand stage (128 threads; every raw load before the first store).
-// Thread t always converts the same 16-column segment (t % (D/16)) of rows r0 + i*RS, so its
-// operand offsets are one base plus a constant stride per i.
+// raw stage -> f16 K/V operand stage (kDq threads; every raw load before the first store).
+// Thread mapping: 8 consecutive threads take 8 consecutive rows of one 16-column segment, so
+// both the swizzled int8 loads and the swizzled operand stores of a thread-phase hit 8 distinct
+// bank groups; each thread keeps one segment and one row-in-group, so its operand offsets are
+// one base plus a constant stride per unit.
 template <int D>
 __device__ __forceinline__ void dequant_tile(const uint8_t *raw, uint8_t *sK, uint8_t *sV, int vbt_shift, int dtid) {
     using C = TcCfg<D, true>;
     constexpr int BN = C::BN, W = C::W, UPR = D / 16, RS = kDq / UPR, PER = BN / RS, SCB = D / 16;
-    static_assert(kDq % UPR == 0 && RS % 8 == 0 && BN % RS == 0, "dequant thread mapping");
-    const int seg = dtid % UPR, r0 = dtid / UPR;
+    static_assert(kDq % (8 * UPR) == 0 && BN % RS == 0, "dequant thread mapping");
+    const int rlow = dtid & 7, seg = (dtid >> 3) % UPR, rhigh = (dtid >> 3) / UPR;
+    const int r0 = rhigh * 8 + rlow;
     const int vbt = 1 << vbt_shift;
     const uint32_t vtile = (uint32_t)vbt * (D + SCB);
     uint4 qk[PER], qv[PER];
@@ -483,7 +486,7 @@ __device__ __forceinline__ void dequant_tile(const uint8_t *raw, uint8_t *sK, ui
         const int row = r0 + i * RS;
         const int s = row >> vbt_shift, rib = row & (vbt - 1);
         const uint8_t *kt = raw + s * 2 * vtile;
-        const uint32_t qo = rib * D + seg * 16, so = vbt * D + rib * SCB + (seg >> 1) * 2;
+        const uint32_t qo = q8_qs_off(rib, seg * 16, D), so = vbt * D + rib * SCB + (seg >> 1) * 2;
         qk[i] = *(const uint4 *)(kt + qo);
         dk[i] = *(const uint16_t *)(kt + so);
         qv[i] = *(const uint4 *)(kt + vtile + qo);
@@ -876,7 +879,6 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
         // ---- epilogue ----
         if (r == 0) TRACE(10);
         const bool have_o = ok && n > 0;
-        const int h = pl.g * a.group + (qr - t * a.group);
         if (a.n_splits > 1) {
             const int64_t unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
             float *wo = a.ws_o + (unit * kBM + r) * D;

@@ -106,9 +106,8 @@ __global__ void append_q8_kernel(PoolView p, int layer, const int32_t *__restric
         qw[j] = word;
     }
     uint8_t *tile = p.prefix + prefix_tile_index(p, layer, blk, kv, h) * p.tile_bytes;
-    uint4 *qdst = (uint4 *)(tile + (int64_t)rib * p.head_dim + g * 32);
-    qdst[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
-    qdst[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
+    *(uint4 *)(tile + q8_qs_off(rib, g * 32, p.head_dim)) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+    *(uint4 *)(tile + q8_qs_off(rib, g * 32 + 16, p.head_dim)) = make_uint4(qw[4], qw[5], qw[6], qw[7]);
     uint16_t *sdst = (uint16_t *)(tile + (int64_t)p.block_tokens * p.head_dim) + rib * groups + g;
     *sdst = __half_as_ushort(__float2half_rn(d));
 }
@@ -199,9 +198,9 @@ __global__ void gather_q8_kernel(PoolView p, int layer, int seq, int pos0, int n
     if (blk < 0) return;
     const int rib = pos % p.block_tokens;
     const uint8_t *tile = p.prefix + prefix_tile_index(p, layer, blk, kv, h) * p.tile_bytes;
-    const uint4 *qs = (const uint4 *)(tile + (int64_t)rib * p.head_dim + g * 32);
     const uint16_t dbits = *((const uint16_t *)(tile + (int64_t)p.block_tokens * p.head_dim) + rib * groups + g);
-    const uint4 q0 = qs[0], q1 = qs[1];
+    const uint4 q0 = *(const uint4 *)(tile + q8_qs_off(rib, g * 32, p.head_dim));
+    const uint4 q1 = *(const uint4 *)(tile + q8_qs_off(rib, g * 32 + 16, p.head_dim));
     const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const int64_t blk_out = ((int64_t)r * p.kv_heads + h) * groups + g;
     if (!as_f32) {

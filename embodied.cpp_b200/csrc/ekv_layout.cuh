@@ -7,9 +7,9 @@
 //                 with the tcgen05 shared-memory swizzle already applied (Swizzle<log2(W/16),4,3>,
 //                 W = 128, 64 or 32 bytes). One contiguous copy of a block lands in shared
 //                 memory as a canonical K-major operand (K) or MN-major operand (V) tile.
-//     Q8_0 tile : qs int8 [block_tokens][head_dim] followed by fp16 scales
-//                 [block_tokens][head_dim/32]; a gather re-interleaves them into ggml's
-//                 block_q8_0 {d, qs[32]} bytes.
+//     Q8_0 tile : qs int8 [block_tokens][head_dim] (16-byte units XOR-swizzled by row, see
+//                 q8_qs_off) followed by fp16 scales [block_tokens][head_dim/32]; a gather
+//                 re-interleaves them into ggml's block_q8_0 {d, qs[32]} bytes.
 //   suffix arena  [n_layers][max_seqs][2][kv_heads] tiles of suffix_rows bf16 rows, in the
 //                 same swizzled bf16 tile layout (suffix_rows = suffix_tokens rounded up to 8).
 //   seq table     int32 block_tables[max_seqs][max_blocks_per_seq], int32 seq_lens[max_seqs]
@@ -72,6 +72,15 @@ __host__ __device__ inline uint32_t tile_elem_off(int row, int d, int D, int W) 
     const int wb = byte - chunk * W;
     return (uint32_t)((row >> 3) * nch + chunk) * (uint32_t)(8 * W) +
            swz((uint32_t)((row & 7) * W + wb), (uint32_t)(W / 16 - 1));
+}
+
+// Byte offset of int8 element (row, d) in the qs plane of a Q8_0 tile: rows of D bytes whose
+// 16-byte units are XOR-swizzled by the row (unit ^ (row & m), m = min(D/16, 8) - 1), so that
+// 8 consecutive rows of one 16-byte column fall in 8 different shared-memory bank groups.
+__host__ __device__ inline uint32_t q8_qs_off(int row, int d, int D) {
+    const int units = D / 16;
+    const int m = (units < 8 ? units : 8) - 1;
+    return (uint32_t)(row * D + (((d >> 4) ^ (row & m)) << 4) + (d & 15));
 }
 
 __host__ __device__ inline int64_t prefix_tile_index(const PoolView &p, int layer, int block, int kv,
