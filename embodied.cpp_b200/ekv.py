@@ -65,8 +65,9 @@ EXPORTED = [
     "ekv_seq_create", "ekv_seq_free", "ekv_seq_resize", "ekv_seq_set_blocks", "ekv_seq_evict_front",
     "ekv_seq_get", "ekv_append", "ekv_append_suffix", "ekv_gather", "ekv_gather_suffix",
     "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
-    "ekv_strerror",
+    "ekv_strerror", "ekv_attention_noalloc",
 ]
+NOALLOC_SCRATCH_BYTES = 16 << 20  # EKV_NOALLOC_SCRATCH_BYTES
 
 
 def _load():
@@ -94,6 +95,7 @@ def _load():
         "ekv_attention_workspace_size": ([vp, C.POINTER(AttnParams)], C.c_size_t),
         "ekv_attention": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, vp], C.c_int),
         "ekv_attention_algo": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, i32, vp], C.c_int),
+        "ekv_attention_noalloc": ([vp, C.POINTER(AttnParams), vp, vp, vp], C.c_int),
         "ekv_version": ([], C.c_char_p),
         "ekv_strerror": ([C.c_int], C.c_char_p),
     }

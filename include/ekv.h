@@ -186,6 +186,19 @@ size_t ekv_attention_workspace_size(const ekv_pool *pool, const ekv_attn_params 
 int ekv_attention(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                   void *workspace, size_t workspace_bytes, ekv_stream_t stream);
 
+/* Attention without any device allocation, for callers that cannot call cudaMalloc where
+ * attention runs (a controller or server that reserves its device memory at start-up and
+ * forbids allocation on the control path, or a plugin host such as a ggml backend op callback
+ * that has nowhere to put a workspace). It has no counterpart in the reference. The key-split
+ * scratch lives in a fixed EKV_NOALLOC_SCRATCH_BYTES device array that every GPU loading the
+ * library reserves until the process exits; a call whose ekv_attention_workspace_size exceeds
+ * it returns EKV_ERR_RANGE. The first call on a device looks up the array's device address
+ * (once per device); make that first call before any stream capture. All calls on a device
+ * share the array: calls that overlap on the GPU race. Results equal ekv_attention's. */
+#define EKV_NOALLOC_SCRATCH_BYTES (16u << 20)
+int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
+                          ekv_stream_t stream);
+
 #define EKV_ALGO_TC 0     /* tcgen05 tensor-core kernel (default)                           */
 #define EKV_ALGO_SIMT 1   /* one-warp-per-row CUDA-core kernel, kept as a GPU cross-check   */
 int ekv_attention_algo(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
