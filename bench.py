@@ -309,7 +309,7 @@ def run_reference(args, cfg):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "query-tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": args.config, "description": cfg["desc"]},
+            "data": "synthetic", "config": {"workload": args.workload, "description": cfg["desc"]},
             "cpu_baseline": {"value": value, "unit": "query-tok/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "query-tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -329,8 +329,10 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = dict(CONFIGS[args.config])
+    args.workload = args.config
     if args.batch:
         cfg["batch"] = args.batch
+        args.workload = f"{args.config}@batch{args.batch}"  # a profiling case, not the headline config
     if args.impl == "reference":
         run_reference(args, cfg)
         return
@@ -404,7 +406,7 @@ def main():
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
-            roof["traffic"] = json.load(f).get(args.config)
+            roof["traffic"] = json.load(f).get(args.workload)
     roof["peak_source"] = peaks["source"] + " (burst bf16 figure)"
     roof["kernel"] = "attn_tc_kernel<256,Q8>" if wl.dtype == wl.ekv.DTYPE_Q8_0 else "attn_tc_kernel<256,bf16>"
     roof["avg_launch_us"] = attn_avg_s * 1e6
@@ -419,7 +421,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16/bf16 MMA, f32 accumulate (Q8_0 cache)" if wl.dtype == wl.ekv.DTYPE_Q8_0
             else "bf16 MMA, f32 accumulate",
-            "data": "synthetic", "config": {"workload": args.config, "description": cfg["desc"],
+            "data": "synthetic", "config": {"workload": args.workload, "description": cfg["desc"],
                                             "batch_per_gpu": wl.B, "layers": N_LAYERS, "denoise_steps": N_STEPS,
                                             "suffix_tokens": TQ, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
                                             "block_tokens": BT, "parallelism": f"request-sharded x{world}",
