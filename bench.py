@@ -33,6 +33,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "embodied.cpp_b200"))
 
+import dispatch  # noqa: E402  (request assignment, scatter/gather, max over ranks)
+
 METRIC = "denoise-attn query-tok/s"
 
 CONFIGS = {
@@ -122,22 +124,22 @@ class Clocks:
 class Pi05Workload:
     """Inputs of the pi0.5 denoise loop for `batch` requests, resident in HBM."""
 
-    def __init__(self, cfg: dict, seed: int, device: int):
+    def __init__(self, cfg: dict, reqs, device: int):
+        """`reqs`: this rank's request descriptors (dispatch.RequestDesc), already assigned."""
         import torch
         import ekv
 
         self.torch, self.ekv = torch, ekv
         self.cfg = cfg
-        self.B = cfg["batch"]
+        self.B = len(reqs)
+        self.req_ids = [r.req_id for r in reqs]
         self.dtype = ekv.DTYPE_Q8_0 if cfg["dtype"] == "q8_0" else ekv.DTYPE_BF16
+        seed = reqs[0].seed
         rng = np.random.default_rng(seed)
         B = self.B
-        self.plen = rng.integers(cfg["plo"], cfg["phi"] + 1, size=B).astype(np.int32)
-        if cfg["padded"]:
-            # 768 image tokens + 48 text slots, valid text U[20, 48], the rest padding-masked
-            self.pvalid = (768 + rng.integers(20, 49, size=B)).astype(np.int32)
-        else:
-            self.pvalid = self.plen.copy()
+        self.plen = np.array([r.prefix_len for r in reqs], np.int32)
+        # pi0.5 bf16: 768 image tokens + 48 text slots, valid text U[20, 48], the rest padding-masked
+        self.pvalid = np.array([r.prefix_valid for r in reqs], np.int32)
         need = (self.plen + BT - 1) // BT
         n_blocks = int(need.sum())
         self.pool = ekv.Pool(device=device, dtype=self.dtype, block_tokens=BT, n_blocks=n_blocks, kv_heads=HKV,
@@ -275,8 +277,9 @@ def run_reference(args, cfg):
     rng = np.random.default_rng(1234)
     B = min(cfg["batch"], max(8, threads))
     n_layers = 2
-    plen = rng.integers(cfg["plo"], cfg["phi"] + 1, size=B).astype(np.int32)
-    pvalid = (768 + rng.integers(20, 49, size=B)).astype(np.int32) if cfg["padded"] else plen.copy()
+    reqs = dispatch.make_requests(B, cfg["plo"], cfg["phi"], seed=1234, padded=cfg["padded"])
+    plen = np.array([r.prefix_len for r in reqs], np.int32)  # the GPU arm's first B requests
+    pvalid = np.array([r.prefix_valid for r in reqs], np.int32)
     maxp = int(plen.max())
     row = HKV * D
     is_q8 = cfg["dtype"] == "q8_0"
@@ -351,7 +354,11 @@ def main():
         if world > 1:
             dist.barrier()
 
-    wl = Pi05Workload(cfg, seed=1234 + rank, device=local)
+    # rank 0 draws the whole job's request table and scatters each rank its (length-balanced) share
+    table = dispatch.make_requests(cfg["batch"] * world, cfg["plo"], cfg["phi"], seed=1234,
+                                   padded=cfg["padded"]) if rank == 0 else None
+    mine = dispatch.scatter_requests(table, world, rank, "balanced")
+    wl = Pi05Workload(cfg, mine, device=local)
     stream = torch.cuda.current_stream()
     n_ev = wl.n_calls * args.steps
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
@@ -379,11 +386,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
-    ms = t_start.elapsed_time(t_end)
-    if world > 1:
-        tt = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+    ms = dispatch.max_over_ranks(t_start.elapsed_time(t_end), device=f"cuda:{local}")
     ms_per_step = ms / args.steps
     value = world * wl.qtok_per_step * args.steps / (ms / 1e3)
     attn_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
@@ -516,12 +519,7 @@ def run_e2e(wl, args, world, barrier):
     for _ in range(args.steps):
         one_step()
     torch.cuda.synchronize()
-    dt = time.perf_counter() - t0
-    if world > 1:
-        import torch.distributed as dist
-        tt = torch.tensor([dt], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        dt = float(tt.item())
+    dt = dispatch.max_over_ranks(time.perf_counter() - t0, device=dev)
     barrier()
     # the host buffers received the same outputs the device-resident run produced
     ok = bool(torch.equal(h_out[-1].to(dev), wl.out[-1]))
