@@ -544,6 +544,55 @@ __device__ __forceinline__ void convert_suffix_tile(const AttnArgs &a, const Pla
     }
 }
 
+// One pass over a tile's S row (thread = row): per 32-column chunk, the masked chunk maximum is
+// checked against the running maximum; while no visible score exceeds it by more than 2^8
+// (raw-score threshold `thr`), P = 2^(s * scale_log2 - m_used) is written straight back over the
+// consumed S columns and the running sum is not rescaled. Returns false (warp-uniform) as soon as
+// any row of the warp needs a new maximum; the caller then redoes the tile on the two-pass path,
+// which rewrites every P column of the tile. Maxima and sums use four independent accumulators.
+template <int BN, bool MASKED, bool F16P>
+__device__ __forceinline__ bool softmax_tile_1pass(uint32_t s_col, const uint32_t (&vis_bits)[BN / 32],
+                                                   float scale_log2, float m_used, float thr, float &l) {
+    const float neg_m = -m_used;
+    float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int h32 = 0; h32 < BN / 32; ++h32) {
+        uint32_t rr[32];
+        tmem_load32(s_col + h32 * 32, rr);
+        const uint32_t vb = MASKED ? vis_bits[h32] : 0xffffffffu;
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float v = __uint_as_float(rr[i]);
+            mx[i & 3] = fmaxf(mx[i & 3], (!MASKED || ((vb >> i) & 1u)) ? v : -INFINITY);
+        }
+        const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        if (__any_sync(0xffffffffu, cm > thr)) return false;
+        uint32_t pw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float pr[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int c = 2 * i + e;
+                const float x = ex2(fmaf(__uint_as_float(rr[c]), scale_log2, neg_m));
+                pr[e] = (!MASKED || ((vb >> c) & 1u)) ? x : 0.0f;
+                ps[c & 3] += pr[e];
+            }
+            if (F16P) {
+                const __half2 h2 = __floats2half2_rn(pr[0], pr[1]);
+                pw[i] = *(const uint32_t *)&h2;
+            } else {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(pr[0], pr[1]);
+                pw[i] = *(const uint32_t *)&b2;
+            }
+        }
+        tmem_st16(s_col + h32 * 16, pw);
+    }
+    l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+    return true;
+}
+
 __device__ __forceinline__ void fail_timeout(const AttnArgs &a, volatile int *abort, int where) {
     *abort = 1;
     report_error(a.pool.status, DEV_ERR_TIMEOUT, where, blockIdx.x, blockIdx.z);
@@ -771,6 +820,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
         const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
         const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
         float m_used = -INFINITY, l = 0.0f;
+        const float inv_scale_log2 = 1.0f / a.scale_log2;
         bool ok = true;
         for (int jj = 0; jj < n; ++jj) {
             const int sb = jj & 1;
@@ -780,8 +830,11 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
             if (r == 0 && jj < 50) TRACE(300 + jj);
             const bool suffix = j >= pl.np_tiles;
             const int key0 = suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN;
-            const bool all_vis = row_ok && (suffix ? (suffix_simple && key0 + BN <= a.suffix_len)
-                                                   : (prefix_simple && key0 + BN <= pl.sk.prefix_valid));
+            // every key of the tile visible to every row (uniform over the CTA): rows past
+            // rows_valid score zero queries and are never written, so they take that path too
+            const bool tile_vis = suffix ? (suffix_simple && key0 + BN <= a.suffix_len)
+                                         : (prefix_simple && key0 + BN <= pl.sk.prefix_valid);
+            const bool all_vis = row_ok && tile_vis;
             uint32_t vis_bits[BN / 32];
 #pragma unroll
             for (int w = 0; w < BN / 32; ++w)
@@ -789,10 +842,15 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                                       : (row_ok ? vis_word(m, suffix, key0 + 32 * w, t, pl.sk.prefix_valid, pl.sk.span_b,
                                                            pl.sk.span_e, a.suffix_len)
                                                 : 0u);
-            // the S row is read in 32-column halves twice (max, then exponentials): only 32
-            // scores are live at a time; P (16-bit) goes back over the consumed S columns.
-            // The max is taken on raw scores and scaled once (scale > 0).
             const uint32_t s_col = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
+            // common case: one pass, no new maximum (see softmax_tile_1pass)
+            const float thr = (m_used + 8.0f) * inv_scale_log2;
+            const bool one_pass = tile_vis ? softmax_tile_1pass<BN, false, Q8>(s_col, vis_bits, a.scale_log2, m_used, thr, l)
+                                           : softmax_tile_1pass<BN, true, Q8>(s_col, vis_bits, a.scale_log2, m_used, thr, l);
+            if (!one_pass) {
+            // two passes: the S row is read in 32-column halves twice (max, then exponentials):
+            // only 32 scores are live at a time; P (16-bit) goes back over the consumed S columns.
+            // The max is taken on raw scores and scaled once (scale > 0).
             float s_max = -INFINITY;
 #pragma unroll
             for (int h32 = 0; h32 < BN / 32; ++h32) {
@@ -865,6 +923,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                 tmem_st16(s_col + h32 * 16, pw);
             }
             l += psum;
+            }  // two-pass path
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(BAR_P_FULL + sb));
