@@ -87,16 +87,20 @@ struct TcCfg {
     static constexpr int OFF_V = NSTAGE * KV_BYTES;
     static constexpr int OFF_RAW = 2 * NSTAGE * KV_BYTES;
     static constexpr int OFF_BAR = OFF_RAW + NRAW * RAW_BYTES;
-    static constexpr int OFF_TBL = OFF_BAR + 256;
+    static constexpr int OFF_XCH = OFF_BAR + 256;  // softmax pair exchange: row maxima [2][2][128], sums [2][128]
+    static constexpr int OFF_TBL = OFF_XCH + 6 * kBM * 4;
     // tile base pointers of the split's block-table entries (whatever fits, at most 512)
     static constexpr int TBL_ROOM = (232448 - 1024 - OFF_TBL) / 8;
     static constexpr int TBL = TBL_ROOM > 512 ? 512 : TBL_ROOM;
     static constexpr int SMEM = OFF_TBL + TBL * 8 + 1024;  // + 1 KB alignment slack
     static constexpr int QSTR = D * 2 + 16;               // Q staging row stride (bank-conflict free)
-    static constexpr int MMA_WARP = 4;
-    static constexpr int TMA_WARP = 5;
-    static constexpr int DQ_WARP0 = 6;
-    static constexpr int THREADS = Q8 ? 192 + kDq : 192;
+    // BN = 64: two softmax warps per TMEM lane quarter, each owning half of the tile's columns
+    static constexpr bool SPLIT = BN == 64;
+    static constexpr int SMW = SPLIT ? 8 : 4;  // softmax warps
+    static constexpr int MMA_WARP = SMW;
+    static constexpr int TMA_WARP = SMW + 1;
+    static constexpr int DQ_WARP0 = SMW + 2;
+    static constexpr int THREADS = (SMW + 2) * 32 + (Q8 ? kDq : 0);
     static constexpr int TMEM_COLS = 512;
     static constexpr int S_COL = 0;
     static constexpr int O_COL = 2 * BN;
@@ -111,17 +115,26 @@ struct TcCfg {
     static_assert(D % 16 == 0, "head_dim must be a multiple of 16");
 };
 
+// K and V operand stages are separate rings: a K stage is free again once S(j) has been
+// computed, long before P.V(j) releases the V stage.
 enum {
-    BAR_OP_FULL = 0,     // [3] K/V operand stage filled
-    BAR_OP_EMPTY = 3,    // [3] K/V operand stage consumed (P.V done)
-    BAR_RAW_FULL = 6,    // [2] raw Q8_0 stage landed
-    BAR_RAW_EMPTY = 8,   // [2] raw Q8_0 stage read
-    BAR_S_FULL = 10,     // [2] S(j) in TMEM
-    BAR_P_FULL = 12,     // [2] P(j) in TMEM
-    BAR_P_EMPTY = 14,    // [2] P.V(j) done (P consumed, O updated)
-    BAR_DONE = 16,
-    N_BARS = 17
+    BAR_K_FULL = 0,      // [3] K operand stage filled
+    BAR_K_EMPTY = 3,     // [3] K operand stage consumed (S done)
+    BAR_V_FULL = 6,      // [3] V operand stage filled
+    BAR_V_EMPTY = 9,     // [3] V operand stage consumed (P.V done)
+    BAR_RAW_FULL = 12,   // [2] raw Q8_0 stage landed
+    BAR_RAW_EMPTY = 14,  // [2] raw Q8_0 stage read
+    BAR_P_FULL = 16,     // [2] P(j) in TMEM
+    BAR_DONE = 18,
+    BAR_XCH = 19,        // [4] softmax pair exchange (one per TMEM lane quarter; SPLIT only)
+    N_BARS = 23
 };
+// One commit per MMA group: "S(j) done" is the completion of K stage j % NS and "P.V(j) done"
+// that of V stage j % NS. A waiter for S(j) or P.V(j - 1) in the softmax cannot be overtaken by a
+// later phase of the same barrier: S(j + NS) needs P(j + NS - 2) and P.V(j - 1 + NS) needs
+// P(j - 1 + NS), both produced by the softmax after tile j.
+__device__ __forceinline__ uint32_t s_done_parity(int j, int ns) { return (uint32_t)(j / ns) & 1u; }
+static_assert(N_BARS * 8 + 16 <= 256, "barrier block");
 
 // Key-tile schedule of one CTA, computed identically by every thread.
 struct Plan {
@@ -298,10 +311,10 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
 }
 
 template <int D, bool Q8>
-__device__ __forceinline__ void q_to_tmem(const uint8_t *stg, int r, uint32_t taddr) {
+__device__ __forceinline__ void q_to_tmem(const uint8_t *stg, int r, uint32_t taddr, int c_lo, int c_hi) {
     using C = TcCfg<D, Q8>;
 #pragma unroll 1
-    for (int c = 0; c < D / 16; ++c) {  // 16 elements = 8 columns per store
+    for (int c = c_lo; c < c_hi; ++c) {  // 16 elements = 8 columns per store
         const uint4 a0 = *(const uint4 *)(stg + r * C::QSTR + c * 32);
         const uint4 a1 = *(const uint4 *)(stg + r * C::QSTR + c * 32 + 16);
         uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
@@ -314,11 +327,12 @@ __device__ __forceinline__ void q_to_tmem(const uint8_t *stg, int r, uint32_t ta
 }
 
 // ---- bf16 feeder: one warp, one lane per segment (a block, or the suffix rows of the tile).
-// Source and destination are runs of whole 8-row groups, i.e. one contiguous copy each for K
-// and V; rows without a source are zero-filled by the whole warp ----
+// Copies the K (kv = 0) or V (kv = 1) rows of tile j into one operand stage: source and
+// destination are runs of whole 8-row groups, one contiguous copy per segment; rows without a
+// source are zero-filled by the whole warp ----
 template <int D>
-__device__ __forceinline__ void produce_bf16_tile(const AttnArgs &a, const Plan &pl, const uint8_t *const *sPtr,
-                                                  int j, uint8_t *sK, uint8_t *sV, uint32_t bar_full, int lane) {
+__device__ __forceinline__ void produce_bf16_part(const AttnArgs &a, const Plan &pl, const uint8_t *const *sPtr,
+                                                  int j, int kv, uint8_t *sDst, uint32_t bar_full, int lane) {
     using C = TcCfg<D, false>;
     constexpr int BN = C::BN, RB = D * 2;
     const PoolView &p = a.pool;
@@ -328,14 +342,13 @@ __device__ __forceinline__ void produce_bf16_tile(const AttnArgs &a, const Plan 
     const uint8_t *src = nullptr;
     uint32_t bytes = 0;
     const uint32_t dst = (uint32_t)lane * seg * RB;
-    int64_t v_off = 0;
     if (lane < n_seg) {
         if (suffix) {
             const int s0 = (j - pl.np_tiles) * BN;
             if (s0 < p.suffix_rows) {
                 bytes = (uint32_t)min(BN, p.suffix_rows - s0) * RB;
-                src = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 0, pl.g) * p.suffix_tile_bytes + (int64_t)s0 * RB;
-                v_off = (int64_t)p.kv_heads * p.suffix_tile_bytes;
+                src = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, kv, pl.g) * p.suffix_tile_bytes +
+                      (int64_t)s0 * RB;
             }
         } else {
             const int k = pl.kbeg + j * BN + lane * seg;
@@ -344,24 +357,20 @@ __device__ __forceinline__ void produce_bf16_tile(const AttnArgs &a, const Plan 
             if (k < pl.sk.n_prefix) {
                 src = ptr_of<C::TBL>(a, pl, sPtr, idx);
                 if (src) {
-                    src += (int64_t)rib * RB;
+                    src += (int64_t)kv * p.kv_heads * p.tile_bytes + (int64_t)rib * RB;
                     bytes = (uint32_t)seg * RB;
-                    v_off = (int64_t)p.kv_heads * p.tile_bytes;
                 }
             }
         }
     }
     const uint32_t zlo = dst + bytes, zhi = lane < n_seg ? dst + (uint32_t)seg * RB : zlo;
     const uint32_t need_zero = __ballot_sync(0xffffffffu, zhi > zlo);
-    const uint32_t total = __reduce_add_sync(0xffffffffu, src ? 2 * bytes : 0u);
+    const uint32_t total = __reduce_add_sync(0xffffffffu, src ? bytes : 0u);
     if (need_zero) {
         for (uint32_t m = need_zero; m; m &= m - 1) {
             const int s = __ffs(m) - 1;
             const uint32_t z0 = __shfl_sync(0xffffffffu, zlo, s), z1 = __shfl_sync(0xffffffffu, zhi, s);
-            for (uint32_t o = z0 + lane * 16; o < z1; o += 32 * 16) {
-                *(uint4 *)(sK + o) = make_uint4(0, 0, 0, 0);
-                *(uint4 *)(sV + o) = make_uint4(0, 0, 0, 0);
-            }
+            for (uint32_t o = z0 + lane * 16; o < z1; o += 32 * 16) *(uint4 *)(sDst + o) = make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async();
         __syncwarp();
@@ -371,10 +380,7 @@ __device__ __forceinline__ void produce_bf16_tile(const AttnArgs &a, const Plan 
         else mbar_arrive(bar_full);
     }
     __syncwarp();
-    if (src) {
-        bulk_g2s(smem_addr(sK + dst), src, bytes, bar_full);
-        bulk_g2s(smem_addr(sV + dst), src + v_off, bytes, bar_full);
-    }
+    if (src) bulk_g2s(smem_addr(sDst + dst), src, bytes, bar_full);
 }
 
 // ---- Q8_0 feeder: the raw stage holds, per segment of vbt = min(block_tokens, BN) rows, a K part
@@ -465,13 +471,13 @@ __device__ __forceinline__ void dequant16(const uint4 q, uint32_t dbits, uint4 &
 }
 
 
-// raw stage -> f16 K/V operand stage (kDq threads; every raw load before the first store).
-// Thread mapping: 8 consecutive threads take 8 consecutive rows of one 16-column segment, so
-// both the swizzled int8 loads and the swizzled operand stores of a thread-phase hit 8 distinct
-// bank groups; each thread keeps one segment and one row-in-group, so its operand offsets are
-// one base plus a constant stride per unit.
+// raw stage -> the K (kv = 0) or V (kv = 1) f16 operand stage (kDq threads; every raw load before the
+// first store). Thread mapping: 8 consecutive threads take 8 consecutive rows of one 16-column
+// segment, so both the swizzled int8 loads and the swizzled operand stores of a thread-phase hit 8
+// distinct bank groups; each thread keeps one segment and one row-in-group, so its operand offsets
+// are one base plus a constant stride per unit.
 template <int D>
-__device__ __forceinline__ void dequant_tile(const uint8_t *raw, uint8_t *sK, uint8_t *sV, int vbt_shift, int dtid) {
+__device__ __forceinline__ void dequant_part(const uint8_t *raw, int kv, uint8_t *sDst, int vbt_shift, int dtid) {
     using C = TcCfg<D, true>;
     constexpr int BN = C::BN, W = C::W, UPR = D / 16, RS = kDq / UPR, PER = BN / RS, SCB = D / 16;
     static_assert(kDq % (8 * UPR) == 0 && BN % RS == 0, "dequant thread mapping");
@@ -479,67 +485,54 @@ __device__ __forceinline__ void dequant_tile(const uint8_t *raw, uint8_t *sK, ui
     const int r0 = rhigh * 8 + rlow;
     const int vbt = 1 << vbt_shift;
     const uint32_t vtile = (uint32_t)vbt * (D + SCB);
-    uint4 qk[PER], qv[PER];
-    uint32_t dk[PER], dv[PER];
+    uint4 q[PER];
+    uint32_t d[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         const int row = r0 + i * RS;
         const int s = row >> vbt_shift, rib = row & (vbt - 1);
-        const uint8_t *kt = raw + s * 2 * vtile;
-        const uint32_t qo = q8_qs_off(rib, seg * 16, D), so = vbt * D + rib * SCB + (seg >> 1) * 2;
-        qk[i] = *(const uint4 *)(kt + qo);
-        dk[i] = *(const uint16_t *)(kt + so);
-        qv[i] = *(const uint4 *)(kt + vtile + qo);
-        dv[i] = *(const uint16_t *)(kt + vtile + so);
+        const uint8_t *t = raw + s * 2 * vtile + kv * vtile;
+        q[i] = *(const uint4 *)(t + q8_qs_off(rib, seg * 16, D));
+        d[i] = *(const uint16_t *)(t + vbt * D + rib * SCB + (seg >> 1) * 2);
     }
     const uint32_t off_lo = tile_elem_off(r0, seg * 16, D, W), off_hi = tile_elem_off(r0, seg * 16 + 8, D, W);
     constexpr uint32_t STEP = (RS / 8) * C::SBO;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         uint4 lo, hi;
-        dequant16(qk[i], dk[i], lo, hi);
-        *(uint4 *)(sK + off_lo + i * STEP) = lo;
-        *(uint4 *)(sK + off_hi + i * STEP) = hi;
-        dequant16(qv[i], dv[i], lo, hi);
-        *(uint4 *)(sV + off_lo + i * STEP) = lo;
-        *(uint4 *)(sV + off_hi + i * STEP) = hi;
+        dequant16(q[i], d[i], lo, hi);
+        *(uint4 *)(sDst + off_lo + i * STEP) = lo;
+        *(uint4 *)(sDst + off_hi + i * STEP) = hi;
     }
 }
 
-// bf16 suffix slot -> f16 K/V operand stage (Q8_0 pools), 4 units in flight per thread
+// bf16 suffix slot -> the K or V f16 operand stage (Q8_0 pools), 4 units in flight per thread
 template <int D>
-__device__ __forceinline__ void convert_suffix_tile(const AttnArgs &a, const Plan &pl, int j, uint8_t *sK, uint8_t *sV,
+__device__ __forceinline__ void convert_suffix_part(const AttnArgs &a, const Plan &pl, int j, int kv, uint8_t *sDst,
                                                     int dtid) {
     using C = TcCfg<D, true>;
     constexpr int BN = C::BN, W = C::W, UPR = D / 8, UNITS = BN * UPR;
     const PoolView &p = a.pool;
     const int s_base = (j - pl.np_tiles) * BN;
-    const uint8_t *tk = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 0, pl.g) * p.suffix_tile_bytes;
-    const uint8_t *tv = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, 1, pl.g) * p.suffix_tile_bytes;
+    const uint8_t *src = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, kv, pl.g) * p.suffix_tile_bytes;
 #pragma unroll 1
     for (int u0 = 0; u0 < UNITS; u0 += 4 * kDq) {
-        uint4 kk[4], vv[4];
+        uint4 v[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int u = u0 + dtid + i * kDq;
             const int row = u / UPR, d0 = (u - row * UPR) * 8, srow = s_base + row;
-            kk[i] = vv[i] = make_uint4(0, 0, 0, 0);
-            if (u < UNITS && srow < p.suffix_rows) {
-                const uint32_t off = tile_elem_off(srow, d0, D, W);
-                kk[i] = __ldg((const uint4 *)(tk + off));
-                vv[i] = __ldg((const uint4 *)(tv + off));
-            }
+            v[i] = make_uint4(0, 0, 0, 0);
+            if (u < UNITS && srow < p.suffix_rows) v[i] = __ldg((const uint4 *)(src + tile_elem_off(srow, d0, D, W)));
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int u = u0 + dtid + i * kDq;
             if (u >= UNITS) break;
             const int row = u / UPR, d0 = (u - row * UPR) * 8;
-            const uint32_t off = tile_elem_off(row, d0, D, W);
-            *(uint4 *)(sK + off) = make_uint4(bf16x2_to_f16x2(kk[i].x), bf16x2_to_f16x2(kk[i].y),
-                                              bf16x2_to_f16x2(kk[i].z), bf16x2_to_f16x2(kk[i].w));
-            *(uint4 *)(sV + off) = make_uint4(bf16x2_to_f16x2(vv[i].x), bf16x2_to_f16x2(vv[i].y),
-                                              bf16x2_to_f16x2(vv[i].z), bf16x2_to_f16x2(vv[i].w));
+            *(uint4 *)(sDst + tile_elem_off(row, d0, D, W)) =
+                make_uint4(bf16x2_to_f16x2(v[i].x), bf16x2_to_f16x2(v[i].y), bf16x2_to_f16x2(v[i].z),
+                           bf16x2_to_f16x2(v[i].w));
         }
     }
 }
@@ -598,6 +591,224 @@ __device__ __forceinline__ void fail_timeout(const AttnArgs &a, volatile int *ab
     report_error(a.pool.status, DEV_ERR_TIMEOUT, where, blockIdx.x, blockIdx.z);
 }
 
+// Bounded wait on this warp's pair-exchange barrier (both warps of a TMEM lane quarter arrive
+// once per use, lane 0 after a warp sync, so the lanes' shared-memory writes are released).
+__device__ __forceinline__ bool pair_sync(uint32_t xbar, int use, volatile int *abort) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(xbar);
+    return mbar_wait(xbar, (uint32_t)use & 1u, abort, kWaitBudget);
+}
+
+// ---- softmax / epilogue with two warps per TMEM lane quarter (BN = 64): warp w owns query row
+// (w & 3) * 32 + lane and S columns [h * 32, h * 32 + 32) of every tile, h = w >> 2. Per tile the
+// two warps swap their masked chunk maxima through shared memory; P for the 32 keys goes back as
+// 16 packed columns [h * 16, h * 16 + 16) of the tile's S buffer (both warps have read S by then).
+// The O rescale and the epilogue split O's columns the same way. ----
+template <int D, bool Q8>
+__device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan &pl, uint8_t *smem, uint32_t bar0,
+                                                   volatile int *abort, uint32_t tmem, uint32_t lane_base, int n,
+                                                   int n_qtiles) {
+    using C = TcCfg<D, Q8>;
+    constexpr int BN = C::BN, DH = D / 2;
+    static_assert(BN == 64, "split softmax: 32 columns per warp");
+    auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int h = warp >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const bool row_ok = r < pl.rows_valid;
+    const int t = (pl.qrow0 + r) / a.group;
+    const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
+    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
+    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
+    float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][2 half][128 rows]
+    float *xl = xmax + 4 * kBM;                   // [2 half][128 rows]
+    const uint32_t xbar = bar(BAR_XCH + quarter);
+    int uses = 0;
+    float m_used = -INFINITY, l = 0.0f;
+    const float inv_scale_log2 = 1.0f / a.scale_log2;
+    bool ok = true;
+    for (int jj = 0; jj < n; ++jj) {
+        const int sb = jj & 1;
+        const int j = pl.j0 + jj;
+        if (!(ok = mbar_wait(bar(BAR_K_EMPTY + jj % C::NSTAGE), s_done_parity(jj, C::NSTAGE), abort, kWaitBudget))) break;
+        tc_fence_after();
+        if (r == 0 && h == 0 && jj < 50) TRACE(300 + jj);
+        const bool suffix = j >= pl.np_tiles;
+        const int key0 = (suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN) + h * 32;  // this warp's 32 keys
+        // all 32 keys visible to every row (uniform over the CTA; rows past rows_valid score zero
+        // queries and are never written)
+        const bool all_vis = suffix ? (suffix_simple && key0 + 32 <= a.suffix_len)
+                                    : (prefix_simple && key0 + 32 <= pl.sk.prefix_valid);
+        const uint32_t vb = all_vis ? 0xffffffffu
+                                    : (row_ok ? vis_word(m, suffix, key0, t, pl.sk.prefix_valid, pl.sk.span_b,
+                                                         pl.sk.span_e, a.suffix_len)
+                                              : 0u);
+        const uint32_t s_buf = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
+        uint32_t rr[32];
+        tmem_load32(s_buf + h * 32, rr);
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (all_vis) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(rr[i]));
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], ((vb >> i) & 1u) ? __uint_as_float(rr[i]) : -INFINITY);
+        }
+        const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        xmax[((jj & 1) * 2 + h) * kBM + r] = cm;
+        if (!(ok = pair_sync(xbar, uses++, abort))) break;
+        const float rmax = fmaxf(cm, xmax[((jj & 1) * 2 + (h ^ 1)) * kBM + r]);  // raw scores (scale > 0)
+        // a new maximum more than 2^8 above the one in use: rescale l and O (both warps of the pair
+        // see the same row maxima, so they take this branch together)
+        if (__any_sync(0xffffffffu, rmax > (m_used + 8.0f) * inv_scale_log2)) {
+            const float m_tile = rmax * a.scale_log2;
+            float alpha = 1.0f;
+            bool rescale = false;
+            if (m_tile > m_used) {
+                if (m_used == -INFINITY) {
+                    m_used = m_tile;
+                } else if (m_tile > m_used + 8.0f) {
+                    alpha = ex2(m_used - m_tile);
+                    m_used = m_tile;
+                    l *= alpha;
+                    rescale = true;
+                }
+            }
+            if (__any_sync(0xffffffffu, rescale)) {
+                // O may only be touched once the previous P.V has landed in TMEM.
+                if (!(ok = mbar_wait(bar(BAR_V_EMPTY + (jj - 1) % C::NSTAGE), s_done_parity(jj - 1, C::NSTAGE), abort, kWaitBudget)))
+                    break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 16) {
+                    uint32_t o16[16];
+                    tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), o16);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
+                    tmem_st16(tmem + lane_base + (uint32_t)(C::O_COL + c0), o16);
+                }
+                tmem_wait_st();
+            }
+        }
+        // P = 2^(s * scale_log2 - m_used), masked keys 0
+        const float neg_m = -m_used;
+        const uint32_t pv_bits = (m_used != -INFINITY) ? vb : 0u;
+        float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        uint32_t pw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float pr[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int c = 2 * i + e;
+                const float x = ex2(fmaf(__uint_as_float(rr[c]), a.scale_log2, neg_m));
+                pr[e] = ((pv_bits >> c) & 1u) ? x : 0.0f;
+                ps[c & 3] += pr[e];
+            }
+            if (Q8) {
+                const __half2 h2 = __floats2half2_rn(pr[0], pr[1]);
+                pw[i] = *(const uint32_t *)&h2;
+            } else {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(pr[0], pr[1]);
+                pw[i] = *(const uint32_t *)&b2;
+            }
+        }
+        tmem_st16(s_buf + h * 16, pw);
+        l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(BAR_P_FULL + sb));
+        if (r == 0 && h == 0 && jj < 50) TRACE(350 + jj);
+    }
+    if (!ok) fail_timeout(a, abort, 3);
+    if (ok && n > 0) {
+        ok = mbar_wait(bar(BAR_V_EMPTY + (n - 1) % C::NSTAGE), s_done_parity(n - 1, C::NSTAGE), abort, kWaitBudget);
+        if (!ok) fail_timeout(a, abort, 4);
+        tc_fence_after();
+    }
+    // ---- epilogue: row sum over both halves, then this warp's D/2 columns of O ----
+    if (r == 0 && h == 0) TRACE(10);
+    xl[h * kBM + r] = l;
+    if (ok && !pair_sync(xbar, uses++, abort)) {
+        ok = false;
+        fail_timeout(a, abort, 7);
+    }
+    const float l_row = ok ? xl[r] + xl[kBM + r] : 0.0f;  // same order in both warps
+    const bool have_o = ok && n > 0;
+    const bool row_ok2 = row_ok;
+    if (a.n_splits > 1) {
+        const int64_t unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
+        float *wo = a.ws_o + (unit * kBM + r) * D;
+#pragma unroll 1
+        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 16) {
+            uint32_t o16[16];
+            if (have_o) {
+                tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), o16);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o16[i] = 0u;
+            }
+            if (row_ok2) {
+#pragma unroll
+                for (int i = 0; i < 16; i += 4)
+                    *(float4 *)(wo + c0 + i) = make_float4(__uint_as_float(o16[i]), __uint_as_float(o16[i + 1]),
+                                                           __uint_as_float(o16[i + 2]), __uint_as_float(o16[i + 3]));
+            }
+        }
+        if (row_ok2 && h == 0) {
+            float *wml = a.ws_ml + (unit * kBM + r) * 2;
+            wml[0] = have_o ? m_used : -INFINITY;
+            wml[1] = have_o ? l_row : 0.0f;
+        }
+    } else {
+        // O/l (bf16 or f32) -> shared staging row r -> the softmax warps write whole rows with
+        // consecutive 16-byte lanes (the K/V stages are idle once the last P.V has landed)
+        const float inv = (have_o && l_row > 0.0f) ? 1.0f / l_row : 0.0f;
+        const bool f32 = a.out_dtype == EKV_DTYPE_F32;
+        uint8_t *orow = smem + C::OFF_K + r * C::OSTR;
+#pragma unroll 1
+        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
+            uint32_t o32[32];
+            if (have_o) {
+                tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o32[i] = 0u;
+            }
+            if (f32) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                    *(float4 *)(orow + (c0 + i) * 4) =
+                        make_float4(__uint_as_float(o32[i]) * inv, __uint_as_float(o32[i + 1]) * inv,
+                                    __uint_as_float(o32[i + 2]) * inv, __uint_as_float(o32[i + 3]) * inv);
+            } else {
+#pragma unroll
+                for (int i0 = 0; i0 < 32; i0 += 8) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o32[i0 + 2 * i]) * inv,
+                                                                        __uint_as_float(o32[i0 + 2 * i + 1]) * inv);
+                        w[i] = *(const uint32_t *)&b2;
+                    }
+                    *(uint4 *)(orow + (c0 + i0) * 2) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(C::SMW * 32) : "memory");  // the softmax warps only
+        const int row_bytes = D * (f32 ? 4 : 2);
+        for (int rw = warp; rw < pl.rows_valid; rw += C::SMW) {
+            const int qrw = pl.qrow0 + rw;
+            const int tw = qrw / a.group;
+            const int hw = pl.g * a.group + (qrw - tw * a.group);
+            uint8_t *dst = (uint8_t *)a.out + ((((int64_t)pl.b * a.q_tokens + tw) * a.q_heads + hw) * D) * (f32 ? 4 : 2);
+            const uint8_t *srow = smem + C::OFF_K + rw * C::OSTR;
+            for (int o = lane * 16; o < row_bytes; o += 32 * 16) *(uint4 *)(dst + o) = *(const uint4 *)(srow + o);
+        }
+    }
+}
+
 template <int D, bool Q8>
 __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const AttnArgs a, int n_qtiles) {
     using C = TcCfg<D, Q8>;
@@ -625,17 +836,18 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
-            mbar_init(bar(BAR_OP_FULL + s), Q8 ? kDq : 1);
-            mbar_init(bar(BAR_OP_EMPTY + s), 1);
+            mbar_init(bar(BAR_K_FULL + s), Q8 ? kDq / 32 : 1);
+            mbar_init(bar(BAR_K_EMPTY + s), 1);
+            mbar_init(bar(BAR_V_FULL + s), Q8 ? kDq / 32 : 1);
+            mbar_init(bar(BAR_V_EMPTY + s), 1);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(bar(BAR_RAW_FULL + s), 1);
-            mbar_init(bar(BAR_RAW_EMPTY + s), kDq);
-            mbar_init(bar(BAR_S_FULL + s), 1);
-            mbar_init(bar(BAR_P_FULL + s), 128);
-            mbar_init(bar(BAR_P_EMPTY + s), 1);
+            mbar_init(bar(BAR_RAW_EMPTY + s), kDq / 32);
+            mbar_init(bar(BAR_P_FULL + s), C::SMW);
         }
         mbar_init(bar(BAR_DONE), 1);
+        for (int q = 0; q < 4; ++q) mbar_init(bar(BAR_XCH + q), 2);
         *abort = 0;
         mbar_init_fence();
     }
@@ -656,8 +868,11 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     const uint32_t lane_base = ((uint32_t)((warp & 3) * 32)) << 16;
-    if (warp < 4) {
-        q_to_tmem<D, Q8>(smem + C::OFF_K, threadIdx.x, tmem + lane_base + C::Q_COL);
+    if (warp < C::SMW) {
+        // row (warp & 3) * 32 + lane; with SPLIT the two warps of a lane quarter take half the columns each
+        const int h = C::SPLIT ? warp >> 2 : 0, nh = C::SPLIT ? 2 : 1;
+        q_to_tmem<D, Q8>(smem + C::OFF_K, (warp & 3) * 32 + lane, tmem + lane_base + C::Q_COL, h * (D / 16) / nh,
+                         (h + 1) * (D / 16) / nh);
         tmem_wait_st();
     }
     fence_proxy_async();  // staging reads (generic) before the copy engine refills the stages
@@ -668,86 +883,63 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
     const int n = pl.j1 - pl.j0;
 
     if (warp == C::MMA_WARP) {
-        if (n > 0) {
-            // The whole warp runs the schedule (warp-uniform descriptors and decisions); lane 0
-            // issues the tcgen05 instructions.
+        // One thread issues everything, in the fixed order S(0), [S(j+1), P.V(j)] for j = 0..n-1.
+        // tcgen05.mma issue returns about when the previous MMA starts executing, so every cycle
+        // this thread spends elsewhere is an idle tensor pipe: straight-line waits (which return at
+        // once when the operand is ready), one commit per group. S(j+1) reuses the S buffer of
+        // P(j-1), whose P.V was issued before it (the tensor core executes in issue order).
+        if (n > 0 && lane == 0) {
             const uint32_t idS = idesc_f16(!Q8, false, BN);
             const uint32_t idO = idesc_f16(!Q8, true, D);
             const uint32_t k_addr = smem_addr(sK), v_addr = smem_addr(sV);
             bool ok = true;
             auto issue_s = [&](int jj) {
                 const int st = jj % NS, sb = jj & 1;
-                if (jj < 50 && lane == 0) TRACE(400 + jj);
+                if (!mbar_wait(bar(BAR_K_FULL + st), (jj / NS) & 1, abort, kWaitBudget)) return false;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)(sb * BN);
                 const uint64_t bd0 = sdesc(k_addr + st * C::KV_BYTES, 16, C::SBO, C::LAYOUT);
-                if (lane == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; ++kk) {
-                        constexpr int KPC = W / 32;  // K-steps per swizzle chunk
-                        const uint32_t off = (uint32_t)(kk / KPC) * (8 * W) + (uint32_t)(kk % KPC) * 32u;
-                        mma_ts(d_tmem, tmem + C::Q_COL + (uint32_t)(kk * 8), bd0 + (off >> 4), idS, kk > 0 ? 1u : 0u);
-                    }
-                    mma_commit(bar(BAR_S_FULL + sb));
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    constexpr int KPC = W / 32;  // K-steps per swizzle chunk
+                    const uint32_t off = (uint32_t)(kk / KPC) * (8 * W) + (uint32_t)(kk % KPC) * 32u;
+                    mma_ts(d_tmem, tmem + C::Q_COL + (uint32_t)(kk * 8), bd0 + (off >> 4), idS, kk > 0 ? 1u : 0u);
                 }
-                __syncwarp();
-                if (jj < 50 && lane == 0) TRACE(200 + jj);
+                mma_commit(bar(BAR_K_EMPTY + st));  // S(j) done: K stage free, S(j) readable
+                if (jj < 50) TRACE(200 + jj);
+                return true;
             };
             auto issue_pv = [&](int jj) {
                 const int st = jj % NS, sb = jj & 1;
+                if (!mbar_wait(bar(BAR_P_FULL + sb), (jj >> 1) & 1, abort, kWaitBudget)) return false;
+                if (!mbar_wait(bar(BAR_V_FULL + st), (jj / NS) & 1, abort, kWaitBudget)) return false;
                 tc_fence_after();
                 const uint64_t bd0 = sdesc(v_addr + st * C::KV_BYTES, 8 * W, C::SBO, C::LAYOUT);
-                if (lane == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < BN / 16; ++kk)
-                        mma_ts(tmem + C::O_COL, tmem + C::S_COL + (uint32_t)(sb * BN + kk * 8),
-                               bd0 + ((uint32_t)kk * 2u * C::SBO >> 4), idO, (jj > 0 || kk > 0) ? 1u : 0u);
-                    mma_commit(bar(BAR_OP_EMPTY + st));
-                    mma_commit(bar(BAR_P_EMPTY + sb));
-                }
-                __syncwarp();
-                if (jj < 50 && lane == 0) TRACE(250 + jj);
+                for (int kk = 0; kk < BN / 16; ++kk)
+                    mma_ts(tmem + C::O_COL, tmem + C::S_COL + (uint32_t)(sb * BN + kk * 8),
+                           bd0 + ((uint32_t)kk * 2u * C::SBO >> 4), idO, (jj > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(bar(BAR_V_EMPTY + st));  // P.V(j) done: V stage free, P(j) consumed
+                if (jj < 50) TRACE(250 + jj);
+                return true;
             };
-            // S(j) needs its K stage and its S buffer (P(j-2) consumed: P.V(j-2) issued, and the
-            // tensor core executes in issue order); P.V(j) needs P(j).
-            int next_s = 0, next_pv = 0;
-            long long t_prog = clock64();
-            while (next_pv < n) {
-                int act = 0;
-                if (lane == 0) {
-                    if (next_s < n && next_s <= next_pv + 1 &&
-                        mbar_test_wait(bar(BAR_OP_FULL + next_s % NS), (next_s / NS) & 1))
-                        act = 1;
-                    else if (next_pv < next_s &&
-                             mbar_test_wait(bar(BAR_P_FULL + (next_pv & 1)), (next_pv >> 1) & 1))
-                        act = 2;
-                }
-                act = __shfl_sync(0xffffffffu, act, 0);
-                if (act == 1) {
-                    issue_s(next_s++);
-                    t_prog = clock64();
-                } else if (act == 2) {
-                    issue_pv(next_pv++);
-                    t_prog = clock64();
-                } else if (__shfl_sync(0xffffffffu, (*abort || clock64() - t_prog > kWaitBudget) ? 1 : 0, 0)) {
-                    ok = false;
-                    break;
-                }
+            ok = issue_s(0);
+            for (int jj = 0; ok && jj < n; ++jj) {
+                if (jj + 1 < n) ok = issue_s(jj + 1);
+                if (ok) ok = issue_pv(jj);
             }
-            if (lane == 0) {
-                if (!ok) fail_timeout(a, abort, 1);
-                // Every MMA this warp issued must have finished before TMEM is released.
-                mma_commit(bar(BAR_DONE));
-                mbar_wait(bar(BAR_DONE), 0, abort, kWaitBudget);
-            }
-            __syncwarp();
+            if (!ok) fail_timeout(a, abort, 1);
+            // Every MMA this thread issued must have finished before TMEM is released.
+            mma_commit(bar(BAR_DONE));
+            mbar_wait(bar(BAR_DONE), 0, abort, kWaitBudget);
         }
+        __syncwarp();
     } else if (warp == C::TMA_WARP) {
         // copy-engine feeder
-        int issued = 0;
-        for (int jj = 0; jj < n; ++jj) {
-            const int j = pl.j0 + jj;
-            if constexpr (Q8) {
+        if constexpr (Q8) {
+            int issued = 0;
+            for (int jj = 0; jj < n; ++jj) {
+                const int j = pl.j0 + jj;
                 if (j >= pl.np_tiles) break;  // suffix tiles are converted by the dequant warps
                 const int r = jj % C::NRAW;
                 if (jj >= C::NRAW &&
@@ -756,26 +948,48 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                     break;
                 }
                 if (lane == 0 && jj < 50) TRACE(450 + jj);
-                produce_q8_raw<D>(a, pl, (const uint8_t *const *)sPtr, j, sRaw + r * C::RAW_BYTES, bar(BAR_RAW_FULL + r), lane);
-            } else {
-                const int st = jj % NS;
-                if (jj >= NS && !mbar_wait(bar(BAR_OP_EMPTY + st), ((jj - NS) / NS) & 1, abort, kWaitBudget)) {
-                    fail_timeout(a, abort, 2);
-                    break;
-                }
-                if (lane == 0 && jj < 50) TRACE(450 + jj);
-                produce_bf16_tile<D>(a, pl, (const uint8_t *const *)sPtr, j, sK + st * C::KV_BYTES, sV + st * C::KV_BYTES,
-                                     bar(BAR_OP_FULL + st), lane);
+                produce_q8_raw<D>(a, pl, (const uint8_t *const *)sPtr, j, sRaw + r * C::RAW_BYTES, bar(BAR_RAW_FULL + r),
+                                  lane);
+                issued = jj + 1;
+                if (lane == 0 && jj < 50) TRACE(150 + jj);
             }
-            issued = jj + 1;
-            if (lane == 0 && jj < 50) TRACE(150 + jj);
-        }
-        // Do not leave the CTA with bulk copies still writing shared memory.
-        if (lane == 0 && *abort) {
-            constexpr int depth = Q8 ? C::NRAW : NS;
-            for (int jj = max(0, issued - depth); jj < issued; ++jj) {
-                const uint32_t b = Q8 ? bar(BAR_RAW_FULL + jj % depth) : bar(BAR_OP_FULL + jj % depth);
-                mbar_wait(b, (jj / depth) & 1, abort, kWaitBudget / 4);
+            // Do not leave the CTA with bulk copies still writing shared memory.
+            if (lane == 0 && *abort)
+                for (int jj = max(0, issued - C::NRAW); jj < issued; ++jj)
+                    mbar_wait(bar(BAR_RAW_FULL + jj % C::NRAW), (jj / C::NRAW) & 1, abort, kWaitBudget / 4);
+        } else {
+            // K(it) and V(it - 1) per step: V is needed one softmax later than K
+            int k_issued = 0, v_issued = 0;
+            for (int it = 0; it <= n; ++it) {
+                if (it < n) {
+                    const int st = it % NS;
+                    if (it >= NS && !mbar_wait(bar(BAR_K_EMPTY + st), ((it - NS) / NS) & 1, abort, kWaitBudget)) {
+                        fail_timeout(a, abort, 2);
+                        break;
+                    }
+                    if (lane == 0 && it < 50) TRACE(450 + it);
+                    produce_bf16_part<D>(a, pl, (const uint8_t *const *)sPtr, pl.j0 + it, 0, sK + st * C::KV_BYTES,
+                                         bar(BAR_K_FULL + st), lane);
+                    k_issued = it + 1;
+                }
+                if (it >= 1) {
+                    const int v = it - 1, st = v % NS;
+                    if (v >= NS && !mbar_wait(bar(BAR_V_EMPTY + st), ((v - NS) / NS) & 1, abort, kWaitBudget)) {
+                        fail_timeout(a, abort, 2);
+                        break;
+                    }
+                    produce_bf16_part<D>(a, pl, (const uint8_t *const *)sPtr, pl.j0 + v, 1, sV + st * C::KV_BYTES,
+                                         bar(BAR_V_FULL + st), lane);
+                    v_issued = v + 1;
+                    if (lane == 0 && v < 50) TRACE(150 + v);
+                }
+            }
+            // Do not leave the CTA with bulk copies still writing shared memory.
+            if (lane == 0 && *abort) {
+                for (int jj = max(0, k_issued - NS); jj < k_issued; ++jj)
+                    mbar_wait(bar(BAR_K_FULL + jj % NS), (jj / NS) & 1, abort, kWaitBudget / 4);
+                for (int jj = max(0, v_issued - NS); jj < v_issued; ++jj)
+                    mbar_wait(bar(BAR_V_FULL + jj % NS), (jj / NS) & 1, abort, kWaitBudget / 4);
             }
         }
     } else if (warp >= C::DQ_WARP0) {
@@ -786,30 +1000,40 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
             for (int jj = 0; jj < n; ++jj) {
                 const int j = pl.j0 + jj, st = jj % NS;
                 const bool prefix = j < pl.np_tiles;
+                const uint8_t *raw = sRaw + (jj % C::NRAW) * C::RAW_BYTES;
                 if (prefix && !mbar_wait(bar(BAR_RAW_FULL + jj % C::NRAW), (jj / C::NRAW) & 1, abort, kWaitBudget)) {
                     fail_timeout(a, abort, 5);
                     break;
                 }
                 if (dtid == 0 && jj < 50) TRACE(500 + jj);
-                if (jj >= NS && !mbar_wait(bar(BAR_OP_EMPTY + st), ((jj - NS) / NS) & 1, abort, kWaitBudget)) {
+                bool ok = true;
+#pragma unroll 1
+                for (int kv = 0; kv < 2; ++kv) {
+                    const int b_empty = kv ? BAR_V_EMPTY : BAR_K_EMPTY, b_full = kv ? BAR_V_FULL : BAR_K_FULL;
+                    uint8_t *dst = (kv ? sV : sK) + st * C::KV_BYTES;
+                    if (jj >= NS && !mbar_wait(bar(b_empty + st), ((jj - NS) / NS) & 1, abort, kWaitBudget)) {
+                        ok = false;
+                        break;
+                    }
+                    if (dtid == 0 && jj < 50) TRACE(550 + 250 * kv + jj);
+                    if (prefix) dequant_part<D>(raw, kv, dst, vbt_shift, dtid);
+                    else convert_suffix_part<D>(a, pl, j, kv, dst, dtid);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (prefix && kv == 1) mbar_arrive(bar(BAR_RAW_EMPTY + jj % C::NRAW));
+                        mbar_arrive(bar(b_full + st));
+                    }
+                }
+                if (!ok) {
                     fail_timeout(a, abort, 6);
                     break;
                 }
-                if (dtid == 0 && jj < 50) TRACE(550 + jj);
-                if (prefix) {
-                    dequant_tile<D>(sRaw + (jj % C::NRAW) * C::RAW_BYTES, sK + st * C::KV_BYTES,
-                                    sV + st * C::KV_BYTES, vbt_shift, dtid);
-                    if (dtid == 0 && jj < 50) TRACE(800 + jj);
-                    fence_proxy_async();
-                    mbar_arrive(bar(BAR_RAW_EMPTY + jj % C::NRAW));
-                } else {
-                    convert_suffix_tile<D>(a, pl, j, sK + st * C::KV_BYTES, sV + st * C::KV_BYTES, dtid);
-                }
-                fence_proxy_async();
-                mbar_arrive(bar(BAR_OP_FULL + st));
                 if (dtid == 0 && jj < 50) TRACE(100 + jj);
             }
         }
+    } else if (warp < C::SMW && C::SPLIT) {
+        if constexpr (C::SPLIT) softmax_split_role<D, Q8>(a, pl, smem, bar0, abort, tmem, lane_base, n, n_qtiles);
     } else if (warp < 4) {
         // ---- softmax / epilogue: thread = query row = TMEM lane ----
         const int r = threadIdx.x;
@@ -825,7 +1049,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
         for (int jj = 0; jj < n; ++jj) {
             const int sb = jj & 1;
             const int j = pl.j0 + jj;
-            if (!(ok = mbar_wait(bar(BAR_S_FULL + sb), (jj >> 1) & 1, abort, kWaitBudget))) break;
+            if (!(ok = mbar_wait(bar(BAR_K_EMPTY + jj % C::NSTAGE), s_done_parity(jj, C::NSTAGE), abort, kWaitBudget))) break;
             tc_fence_after();
             if (r == 0 && jj < 50) TRACE(300 + jj);
             const bool suffix = j >= pl.np_tiles;
@@ -880,7 +1104,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
             }
             if (__any_sync(0xffffffffu, rescale)) {
                 // O may only be touched once the previous P.V has landed in TMEM.
-                if (!(ok = mbar_wait(bar(BAR_P_EMPTY + ((jj - 1) & 1)), ((jj - 1) >> 1) & 1, abort, kWaitBudget)))
+                if (!(ok = mbar_wait(bar(BAR_V_EMPTY + (jj - 1) % C::NSTAGE), s_done_parity(jj - 1, C::NSTAGE), abort, kWaitBudget)))
                     break;
                 tc_fence_after();
 #pragma unroll 1
@@ -926,12 +1150,13 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
             }  // two-pass path
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(BAR_P_FULL + sb));
+            __syncwarp();
+            if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_P_FULL + sb));
             if (r == 0 && jj < 50) TRACE(350 + jj);
         }
         if (!ok) fail_timeout(a, abort, 3);
         if (ok && n > 0) {
-            ok = mbar_wait(bar(BAR_P_EMPTY + ((n - 1) & 1)), ((n - 1) >> 1) & 1, abort, kWaitBudget);
+            ok = mbar_wait(bar(BAR_V_EMPTY + (n - 1) % C::NSTAGE), s_done_parity(n - 1, C::NSTAGE), abort, kWaitBudget);
             if (!ok) fail_timeout(a, abort, 4);
             tc_fence_after();
         }
