@@ -39,6 +39,7 @@
 #include "ekv_device.cuh"
 #include "ekv_internal.h"
 #include "ekv_sm100.cuh"
+#include "ekv_attn_common.cuh"
 
 namespace ekv {
 namespace {
@@ -65,10 +66,6 @@ __device__ __forceinline__ void trace_clock(int slot) {
 #endif
 
 
-constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (~2-3 s) before giving up
-constexpr int kBM = 128;
-constexpr int kMaxSplits = 8;
-constexpr int kDq = 256;  // dequantising threads (Q8_0): 8 warps, two per SM sub-partition
 
 template <int D, bool Q8>
 struct TcCfg {
@@ -207,52 +204,6 @@ __device__ __forceinline__ Plan make_plan(const AttnArgs &a, int n_qtiles) {
 }
 
 
-// Bits of the keys [lo, hi) inside the 32-key word starting at key w0.
-__device__ __forceinline__ uint32_t range_bits(int lo, int hi, int w0) {
-    const int a = max(lo - w0, 0), b = min(hi - w0, 32);
-    if (b <= a) return 0u;
-    const uint32_t upto_b = b >= 32 ? 0xffffffffu : ((1u << b) - 1u);
-    const uint32_t below_a = (1u << a) - 1u;  // a < 32 here
-    return upto_b & ~below_a;
-}
-
-// Visibility of keys [w0, w0+32) for query token t, from key ranges (no per-key loop):
-// the predicate of prefix_allowed / suffix_allowed in closed form.
-__device__ __forceinline__ uint32_t vis_word(const MaskDesc &m, bool suffix, int w0, int t, int prefix_valid,
-                                             int span_b, int span_e, int suffix_len) {
-    if (suffix) {
-        int hi = suffix_len;
-        if (m.flags & EKV_MASK_SUFFIX_CAUSAL) hi = min(hi, t + 1);
-        if ((m.flags & EKV_MASK_SUFFIX_PREFIX_LM) && t == 0) hi = min(hi, 1);
-        return range_bits(0, hi, w0);
-    }
-    uint32_t bits = range_bits(0, prefix_valid, w0);
-    if (m.flags & EKV_MASK_SPAN_ONLY) bits &= range_bits(span_b, span_e, w0);
-    if (m.flags & EKV_MASK_SPAN_EXCLUDE) bits &= ~range_bits(span_b, span_e, w0);
-    if (m.flags & EKV_MASK_BLOCK_CAUSAL) {
-        const int qc = m.q_chunk0 + t / m.chunk_tokens;
-        const int kc_lo = max(qc - m.window_chunks + 1, max(w0, 0) / m.chunk_stride);
-        const int kc_hi = min(qc, (w0 + 31) / m.chunk_stride);
-        uint32_t win = 0u;
-        for (int kc = kc_lo; kc <= kc_hi; ++kc)
-            win |= range_bits(kc * m.chunk_stride, kc * m.chunk_stride + m.chunk_tokens, w0);
-        bits &= win;
-    }
-    return bits;
-}
-
-
-// Table index of key k, and the key's row inside its block (shift/mask for power-of-two blocks).
-__device__ __forceinline__ int block_index(const PoolView &p, int k, int &rib) {
-    if (p.bt_shift >= 0) {
-        rib = k & (p.block_tokens - 1);
-        return k >> p.bt_shift;
-    }
-    const int idx = k / p.block_tokens;
-    rib = k - idx * p.block_tokens;
-    return idx;
-}
-
 // K tile base (head g, this layer) of block-table entry `idx`: shared-memory copy when cached,
 // otherwise from the global table; nullptr for an invalid entry (reported by lookup_block).
 template <int TBL>
@@ -303,11 +254,6 @@ __device__ __forceinline__ void stage_q_store(const QStage<D, Q8> &qs, uint8_t *
         const int r = u / Q::UPR;
         *(uint4 *)(stg + r * TcCfg<D, Q8>::QSTR + (u - r * Q::UPR) * 16) = qs.val[i];
     }
-}
-
-__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
-    const __half2 h2 = __floats2half2_rn(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-    return *(const uint32_t *)&h2;
 }
 
 template <int D, bool Q8>
@@ -439,37 +385,6 @@ __device__ __forceinline__ void produce_q8_raw(const AttnArgs &a, const Plan &pl
         }
     }
 }
-
-// ---- Q8_0 producer: 128 threads; int8 + fp16 scale -> f16 in registers ----
-__device__ __forceinline__ void dequant16(const uint4 q, uint32_t dbits, uint4 &lo, uint4 &hi) {
-    const __half2 scale = __halves2half2(__ushort_as_half((uint16_t)dbits), __ushort_as_half((uint16_t)dbits));
-    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    uint32_t o[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t u = w[i] ^ 0x80808080u;                 // int8 -> uint8 (q + 128)
-        uint32_t e01 = __byte_perm(u, 0x64646464u, 0x5140);    // f16 (1024 + u0, 1024 + u1)
-        uint32_t e23 = __byte_perm(u, 0x64646464u, 0x5342);
-        __half2 h01 = __hmul2(__hsub2(*(__half2 *)&e01, bias), scale);  // exact q, one rounding
-        __half2 h23 = __hmul2(__hsub2(*(__half2 *)&e23, bias), scale);
-        o[2 * i] = *(uint32_t *)&h01;
-        o[2 * i + 1] = *(uint32_t *)&h23;
-    }
-    lo = make_uint4(o[0], o[1], o[2], o[3]);
-    hi = make_uint4(o[4], o[5], o[6], o[7]);
-}
-
-[[maybe_unused]] __device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const __half2 h2 = __floats2half2_rn(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
-        w[i] = *(const uint32_t *)&h2;
-    }
-    return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
 
 // raw stage -> the K (kv = 0) or V (kv = 1) f16 operand stage (kDq threads; every raw load before the
 // first store). Thread mapping: 8 consecutive threads take 8 consecutive rows of one 16-column
@@ -736,76 +651,66 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
     }
     const float l_row = ok ? xl[r] + xl[kBM + r] : 0.0f;  // same order in both warps
     const bool have_o = ok && n > 0;
-    const bool row_ok2 = row_ok;
-    if (a.n_splits > 1) {
-        const int64_t unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
-        float *wo = a.ws_o + (unit * kBM + r) * D;
-#pragma unroll 1
-        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 16) {
-            uint32_t o16[16];
-            if (have_o) {
-                tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), o16);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) o16[i] = 0u;
-            }
-            if (row_ok2) {
-#pragma unroll
-                for (int i = 0; i < 16; i += 4)
-                    *(float4 *)(wo + c0 + i) = make_float4(__uint_as_float(o16[i]), __uint_as_float(o16[i + 1]),
-                                                           __uint_as_float(o16[i + 2]), __uint_as_float(o16[i + 3]));
-            }
-        }
-        if (row_ok2 && h == 0) {
+    // O -> shared staging row r -> the softmax warps write whole rows with consecutive 16-byte lanes
+    // (the K/V stages are idle once the last P.V has landed). Without key splits: O / l as bf16 or
+    // f32 into `out`; with splits: the unnormalised f32 row into the workspace (a unit's 128 rows
+    // are contiguous there), plus the row's running max and sum.
+    const bool split = a.n_splits > 1;
+    const float inv = split ? 1.0f : ((have_o && l_row > 0.0f) ? 1.0f / l_row : 0.0f);
+    const bool f32 = split || a.out_dtype == EKV_DTYPE_F32;
+    int64_t unit = 0;
+    if (split) {
+        unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
+        if (row_ok && h == 0) {
             float *wml = a.ws_ml + (unit * kBM + r) * 2;
             wml[0] = have_o ? m_used : -INFINITY;
             wml[1] = have_o ? l_row : 0.0f;
         }
-    } else {
-        // O/l (bf16 or f32) -> shared staging row r -> the softmax warps write whole rows with
-        // consecutive 16-byte lanes (the K/V stages are idle once the last P.V has landed)
-        const float inv = (have_o && l_row > 0.0f) ? 1.0f / l_row : 0.0f;
-        const bool f32 = a.out_dtype == EKV_DTYPE_F32;
-        uint8_t *orow = smem + C::OFF_K + r * C::OSTR;
+    }
+    uint8_t *orow = (smem + C::OFF_K) + r * C::OSTR;
 #pragma unroll 1
-        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
-            uint32_t o32[32];
-            if (have_o) {
-                tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
-            } else {
+    for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
+        uint32_t o32[32];
+        if (have_o) {
+            tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
+        } else {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o32[i] = 0u;
-            }
-            if (f32) {
+            for (int i = 0; i < 32; ++i) o32[i] = 0u;
+        }
+        if (f32) {
 #pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *(float4 *)(orow + (c0 + i) * 4) =
-                        make_float4(__uint_as_float(o32[i]) * inv, __uint_as_float(o32[i + 1]) * inv,
-                                    __uint_as_float(o32[i + 2]) * inv, __uint_as_float(o32[i + 3]) * inv);
-            } else {
+            for (int i = 0; i < 32; i += 4)
+                *(float4 *)(orow + (c0 + i) * 4) =
+                    make_float4(__uint_as_float(o32[i]) * inv, __uint_as_float(o32[i + 1]) * inv,
+                                __uint_as_float(o32[i + 2]) * inv, __uint_as_float(o32[i + 3]) * inv);
+        } else {
 #pragma unroll
-                for (int i0 = 0; i0 < 32; i0 += 8) {
-                    uint32_t w[4];
+            for (int i0 = 0; i0 < 32; i0 += 8) {
+                uint32_t w[4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o32[i0 + 2 * i]) * inv,
-                                                                        __uint_as_float(o32[i0 + 2 * i + 1]) * inv);
-                        w[i] = *(const uint32_t *)&b2;
-                    }
-                    *(uint4 *)(orow + (c0 + i0) * 2) = make_uint4(w[0], w[1], w[2], w[3]);
+                for (int i = 0; i < 4; ++i) {
+                    const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o32[i0 + 2 * i]) * inv,
+                                                                    __uint_as_float(o32[i0 + 2 * i + 1]) * inv);
+                    w[i] = *(const uint32_t *)&b2;
                 }
+                *(uint4 *)(orow + (c0 + i0) * 2) = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(C::SMW * 32) : "memory");  // the softmax warps only
-        const int row_bytes = D * (f32 ? 4 : 2);
-        for (int rw = warp; rw < pl.rows_valid; rw += C::SMW) {
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(C::SMW * 32) : "memory");  // the softmax warps only
+    const int row_bytes = D * (f32 ? 4 : 2);
+    for (int rw = warp; rw < pl.rows_valid; rw += C::SMW) {
+        uint8_t *dst;
+        if (split) {
+            dst = (uint8_t *)(a.ws_o + (unit * kBM + rw) * D);
+        } else {
             const int qrw = pl.qrow0 + rw;
             const int tw = qrw / a.group;
             const int hw = pl.g * a.group + (qrw - tw * a.group);
-            uint8_t *dst = (uint8_t *)a.out + ((((int64_t)pl.b * a.q_tokens + tw) * a.q_heads + hw) * D) * (f32 ? 4 : 2);
-            const uint8_t *srow = smem + C::OFF_K + rw * C::OSTR;
-            for (int o = lane * 16; o < row_bytes; o += 32 * 16) *(uint4 *)(dst + o) = *(const uint4 *)(srow + o);
+            dst = (uint8_t *)a.out + ((((int64_t)pl.b * a.q_tokens + tw) * a.q_heads + hw) * D) * (f32 ? 4 : 2);
         }
+        const uint8_t *srow = (smem + C::OFF_K) + rw * C::OSTR;
+        for (int o = lane * 16; o < row_bytes; o += 32 * 16) *(uint4 *)(dst + o) = *(const uint4 *)(srow + o);
     }
 }
 
@@ -1253,34 +1158,67 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
 }
 
 // Combine the per-split partial outputs: O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+// One warp per query row: lane s < n_splits reads split s's (m, l); the row's D floats of every
+// split are read as consecutive float4s across the lanes (coalesced), the output written likewise.
+constexpr int kMergeWarps = 8;
+
 template <int D>
-__global__ void merge_splits_kernel(const AttnArgs a, int n_qtiles) {
-    const int qt = blockIdx.x, g = blockIdx.y, b = blockIdx.z, r = threadIdx.x;
-    const int qr = qt * kBM + r;
-    if (qr >= a.q_tokens * a.group) return;
-    const int t = qr / a.group;
-    const int h = g * a.group + (qr - t * a.group);
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_splits_kernel(const AttnArgs a, int n_qtiles) {
+    static_assert(D % 4 == 0, "float4 columns");
+    constexpr int BPT = kBM / kMergeWarps;  // blocks per 128-row tile: every row gets its own warp
+    const int qt = blockIdx.x / BPT, g = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int64_t unit0 = (((int64_t)b * a.pool.kv_heads + g) * n_qtiles + qt) * a.n_splits;
-    float mmax = -INFINITY;
-    for (int s = 0; s < a.n_splits; ++s) mmax = fmaxf(mmax, a.ws_ml[((unit0 + s) * kBM + r) * 2]);
-    float wsum = 0.0f, wts[kMaxSplits];
-    for (int s = 0; s < a.n_splits; ++s) {
-        const float ms = a.ws_ml[((unit0 + s) * kBM + r) * 2];
+    const bool f32 = a.out_dtype == EKV_DTYPE_F32;
+    {
+        const int r = (blockIdx.x % BPT) * kMergeWarps + warp;
+        const int qr = qt * kBM + r;
+        if (qr >= a.q_tokens * a.group) return;
+        const int t = qr / a.group;
+        const int h = g * a.group + (qr - t * a.group);
+        float ms = -INFINITY, ls = 0.0f;
+        if (lane < a.n_splits) {
+            ms = a.ws_ml[((unit0 + lane) * kBM + r) * 2];
+            ls = a.ws_ml[((unit0 + lane) * kBM + r) * 2 + 1];
+        }
+        float mmax = ms;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
         const float wv = (ms == -INFINITY) ? 0.0f : ex2(ms - mmax);
-        wts[s] = wv;
-        wsum += wv * a.ws_ml[((unit0 + s) * kBM + r) * 2 + 1];
-    }
-    const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
-    const int64_t obase = (((int64_t)b * a.q_tokens + t) * a.q_heads + h) * D;
-    for (int d = 0; d < D; ++d) {
-        float acc = 0.0f;
-        for (int s = 0; s < a.n_splits; ++s)
-            if (wts[s] != 0.0f) acc += wts[s] * a.ws_o[((unit0 + s) * kBM + r) * D + d];
-        acc *= inv;
-        if (a.out_dtype == EKV_DTYPE_F32)
-            ((float *)a.out)[obase + d] = acc;
-        else
-            ((uint16_t *)a.out)[obase + d] = f32_to_bf16_bits(acc);
+        float wsum = wv * ls;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+        const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+        const int64_t obase = (((int64_t)b * a.q_tokens + t) * a.q_heads + h) * D;
+        for (int u = lane; u < D / 4; u += 32) {
+            // every split's float4 in flight before the first use
+            float4 o[kMaxSplits];
+#pragma unroll
+            for (int sp = 0; sp < kMaxSplits; ++sp)
+                if (sp < a.n_splits) o[sp] = *(const float4 *)(a.ws_o + ((unit0 + sp) * kBM + r) * D + 4 * u);
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int sp = 0; sp < kMaxSplits; ++sp) {
+                const float w = __shfl_sync(0xffffffffu, wv, sp);
+                if (sp >= a.n_splits || w == 0.0f) continue;
+                acc.x += w * o[sp].x;
+                acc.y += w * o[sp].y;
+                acc.z += w * o[sp].z;
+                acc.w += w * o[sp].w;
+            }
+            acc.x *= inv;
+            acc.y *= inv;
+            acc.z *= inv;
+            acc.w *= inv;
+            if (f32) {
+                *(float4 *)((float *)a.out + obase + 4 * u) = acc;
+            } else {
+                uint2 pk;
+                pk.x = (uint32_t)f32_to_bf16_bits(acc.x) | ((uint32_t)f32_to_bf16_bits(acc.y) << 16);
+                pk.y = (uint32_t)f32_to_bf16_bits(acc.z) | ((uint32_t)f32_to_bf16_bits(acc.w) << 16);
+                *(uint2 *)((uint16_t *)a.out + obase + 4 * u) = pk;
+            }
+        }
     }
 }
 
@@ -1291,23 +1229,7 @@ int sm_count() {
     return n;
 }
 
-// Split count that best fills the SMs with one CTA each: minimise waves per split (with a
-// small per-split merge cost), keeping at least 4 key tiles per split.
-int choose_splits(int64_t units, int max_tiles) {
-    const int sms = sm_count();
-    int best = 1;
-    double best_cost = 1e30;
-    for (int s = 1; s <= kMaxSplits; ++s) {
-        if (s > 1 && max_tiles / s < 4) break;
-        const double waves = (double)((units * s + sms - 1) / sms) / s;
-        const double cost = waves * (1.0 + 0.03 * (s - 1));
-        if (cost < best_cost - 1e-9) {
-            best_cost = cost;
-            best = s;
-        }
-    }
-    return best;
-}
+int choose_splits(int64_t units, int max_tiles) { return choose_split_count(units, max_tiles, sm_count()); }
 
 template <int D, bool Q8>
 int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
@@ -1343,7 +1265,8 @@ int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
     attn_tc_kernel<D, Q8><<<grid, C::THREADS, C::SMEM, s>>>(a, n_qtiles);
     if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
     if (a.n_splits > 1) {
-        merge_splits_kernel<D><<<dim3(n_qtiles, a.pool.kv_heads, a.n_batch), kBM, 0, s>>>(a, n_qtiles);
+        merge_splits_kernel<D><<<dim3(n_qtiles * (kBM / kMergeWarps), a.pool.kv_heads, a.n_batch), kMergeWarps * 32, 0, s>>>(
+            a, n_qtiles);
         if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
     }
     return EKV_OK;
@@ -1379,14 +1302,33 @@ size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int
     const int64_t units = (int64_t)prm.n_batch * p.kv_heads * n_qtiles;
     const int max_tiles = (max_prefix + bn - 1) / bn + (prm.suffix_len + bn - 1) / bn;
     const int sp = choose_splits(units, max_tiles);
-    if (sp <= 1) return 0;
-    return (size_t)units * sp * kBM * (p.head_dim + 2) * sizeof(float);
+    size_t need = sp <= 1 ? 0 : (size_t)units * sp * kBM * (p.head_dim + 2) * sizeof(float);
+    if (p.head_dim == 256) {  // the CTA-pair kernel's choice (pairs of 128-row tiles)
+        const int n_pairs = (prm.q_tokens * group + 2 * kBM - 1) / (2 * kBM);
+        const int64_t pair_units = (int64_t)prm.n_batch * p.kv_heads * n_pairs;
+        const int psp = pair_choose_splits(pair_units, max_tiles, sm_count());
+        if (psp > 1) need = std::max(need, (size_t)pair_units * 2 * psp * kBM * (p.head_dim + 2) * sizeof(float));
+    }
+    return need;
 }
 
-int launch_attention_tc(const AttnArgs &a, cudaStream_t s) {
+int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s) {
+    const dim3 grid((unsigned)(n_qtiles * (kBM / kMergeWarps)), (unsigned)a.pool.kv_heads, (unsigned)a.n_batch);
+    switch (a.pool.head_dim) {
+        case 48: merge_splits_kernel<48><<<grid, kMergeWarps * 32, 0, s>>>(a, n_qtiles); break;
+        case 64: merge_splits_kernel<64><<<grid, kMergeWarps * 32, 0, s>>>(a, n_qtiles); break;
+        case 128: merge_splits_kernel<128><<<grid, kMergeWarps * 32, 0, s>>>(a, n_qtiles); break;
+        case 256: merge_splits_kernel<256><<<grid, kMergeWarps * 32, 0, s>>>(a, n_qtiles); break;
+        default: return EKV_ERR_UNSUPPORTED;
+    }
+    return cudaGetLastError() == cudaSuccess ? EKV_OK : EKV_ERR_CUDA;
+}
+
+int launch_attention_tc(const AttnArgs &a, cudaStream_t s, bool allow_pair) {
     // a.n_splits == 0 means: a workspace was given at a.ws_o, choose the split count.
     size_t ws = 0;
     if (a.n_splits == 0) ws = (size_t)-1;  // the C-ABI checked the size against the maximum need
+    if (allow_pair && a.pool.head_dim == 256) return launch_attention_pair(a, s, ws, sm_count());
     return a.pool.dtype == EKV_DTYPE_Q8_0 ? dispatch<true>(a, s, ws) : dispatch<false>(a, s, ws);
 }
 

@@ -363,6 +363,7 @@ int ekv_gather_suffix(ekv_pool *p, int32_t layer, int32_t id, int32_t n_rows, in
 static int fill_attn_args(ekv_pool *p, const ekv_attn_params *prm, const void *q, void *out,
                           ekv::AttnArgs &a) {
     if (!p || !prm || !q || !out || !prm->seq_ids) return EKV_ERR_INVALID_ARG;
+    if (((uintptr_t)q | (uintptr_t)out) & 15) return EKV_ERR_INVALID_ARG;  // 16-byte vector loads/stores
     const ekv_pool_config &c = p->cfg;
     if (prm->layer < 0 || prm->layer >= c.n_layers) return EKV_ERR_INVALID_ARG;
     if (prm->n_batch <= 0 || prm->q_tokens <= 0 || prm->q_heads <= 0) return EKV_ERR_INVALID_ARG;
@@ -414,14 +415,15 @@ int ekv_attention_algo(ekv_pool *p, const ekv_attn_params *prm, const void *q, v
     if (rc) return rc;
     if (const int e = set_device(p)) return e;
     if (algo == EKV_ALGO_SIMT) return ekv::launch_attention_simt(a, (cudaStream_t)stream);
-    if (algo != EKV_ALGO_TC) return EKV_ERR_INVALID_ARG;
+    if (algo != EKV_ALGO_TC && algo != EKV_ALGO_TC_PAIR) return EKV_ERR_INVALID_ARG;
     const size_t need = ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens);
+    if (workspace && ((uintptr_t)workspace & 15)) return EKV_ERR_INVALID_ARG;
     if (workspace && need && workspace_bytes >= need) {
         // The split count and the workspace carve-up are recomputed by the launcher.
         a.ws_o = (float *)workspace;
         a.n_splits = 0;  // 0 = let the launcher choose from the workspace it was given
     }
-    return ekv::launch_attention_tc(a, (cudaStream_t)stream);
+    return ekv::launch_attention_tc(a, (cudaStream_t)stream, algo == EKV_ALGO_TC_PAIR);
 }
 
 int ekv_attention(ekv_pool *p, const ekv_attn_params *prm, const void *q, void *out, void *workspace,

@@ -55,7 +55,13 @@ int launch_gather(const PoolView &p, int layer, int seq, int pos0, int n_rows, i
 int launch_gather_suffix(const PoolView &p, int layer, int seq, int n_rows, int format,
                          void *k_out, void *v_out, cudaStream_t s);
 int launch_attention_simt(const AttnArgs &a, cudaStream_t s);
-int launch_attention_tc(const AttnArgs &a, cudaStream_t s);
+// allow_pair: head_dim 256 runs on CTA pairs (ekv_attn_pair.cu) instead of one CTA per 128 rows
+int launch_attention_tc(const AttnArgs &a, cudaStream_t s, bool allow_pair);
 size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix);
+// CTA-pair kernel (head_dim 256); n_splits == 0 in `a` = choose from the workspace at a.ws_o
+int launch_attention_pair(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms);
+int pair_choose_splits(int64_t pair_units, int max_tiles, int sms);
+// combine key-split partial outputs (head_dim of the pool) into a.out
+int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s);
 
 }  // namespace ekv

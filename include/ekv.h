@@ -181,7 +181,8 @@ size_t ekv_attention_workspace_size(const ekv_pool *pool, const ekv_attn_params 
  * layer p->layer followed by p->suffix_len suffix-slot keys. q is bf16 [B][Tq][Hq][D]; out is
  * [B][Tq][Hq][D] in p->out_dtype. q head h reads kv head h / (Hq/Hkv), the ggml broadcast of
  * mul_mat (models/pi05.cpp:414). Rows without a visible key are 0
- * (models/lingbot_va.cpp:9503-9506). `workspace` may be NULL (no key splitting).
+ * (models/lingbot_va.cpp:9503-9506). `workspace` may be NULL (no key splitting). q, out and
+ * workspace must be 16-byte aligned (EKV_ERR_INVALID_ARG otherwise).
  * Replaces models/pi05.cpp:410-421 and ggml_flash_attn_ext (models/hy_vla.cpp:1075). */
 int ekv_attention(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                   void *workspace, size_t workspace_bytes, ekv_stream_t stream);
@@ -201,6 +202,9 @@ int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, const void *
 
 #define EKV_ALGO_TC 0     /* tcgen05 tensor-core kernel (default)                           */
 #define EKV_ALGO_SIMT 1   /* one-warp-per-row CUDA-core kernel, kept as a GPU cross-check   */
+#define EKV_ALGO_TC_PAIR 2 /* head_dim 256 on CTA pairs (tcgen05 cta_group::2, 256 query rows
+                              per pair, each K/V tile split between the two CTAs); other head
+                              dims fall back to EKV_ALGO_TC                                    */
 int ekv_attention_algo(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                        void *workspace, size_t workspace_bytes, int32_t algo,
                        ekv_stream_t stream);

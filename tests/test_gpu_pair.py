@@ -1,0 +1,103 @@
+"""head_dim 256 on CTA pairs (tcgen05 cta_group::2, EKV_ALGO_TC_PAIR) against the CPU oracle and
+against the default one-CTA tensor-core kernel, through the C-ABI.
+
+The pair kernel splits every K/V tile between the two CTAs of a cluster (K rows by key, V columns by
+head_dim) and runs 256 query rows per pair, so the cases cover: query-row counts that leave the
+second CTA of the last pair partly or entirely empty; one and two KV heads; 16- and 64-token blocks;
+bf16 and Q8_0 pools; every mask family; key splits through a workspace; prefixes that end inside a
+tile and inside a block."""
+import numpy as np
+import pytest
+import torch
+
+import ekv
+from cases import Filled, bf16_randn
+from test_gpu_parity import TOL, check, oracle_attention, run_attention
+
+pytestmark = pytest.mark.gpu
+
+D = 256
+
+
+def both(f, q, *, Hq, scale, **kw):
+    got = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC_PAIR, **kw)
+    single = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC, **kw)
+    return got, single
+
+
+@pytest.mark.parametrize("dtype", [ekv.DTYPE_BF16, ekv.DTYPE_Q8_0])
+@pytest.mark.parametrize("tokens,heads,hkv", [(50, 8, 1), (37, 8, 1), (16, 8, 1), (3, 8, 1), (20, 8, 2)])
+def test_pair_row_counts(dtype, tokens, heads, hkv):
+    """400, 296, 128, 24 and 80 query rows per KV head: a full pair plus a part-empty one, a pair
+    whose second CTA is empty, and GQA with two KV heads."""
+    gen = torch.Generator().manual_seed(21)
+    plens = [758, 301, 64, 33]
+    f = Filled(dtype=dtype, B=4, prefix_lens=plens, Hkv=hkv, D=D, suffix_len=tokens, seed=21)
+    q = bf16_randn(gen, (4, tokens, heads, D))
+    got, single = both(f, q, Hq=heads, scale=1 / 16)
+    want = oracle_attention(f, 0, q, scale=1 / 16)
+    check(got, want, TOL[dtype])
+    check(single, want, TOL[dtype])
+    assert np.abs(got - single).max() <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [ekv.DTYPE_BF16, ekv.DTYPE_Q8_0])
+@pytest.mark.parametrize("flag", [ekv.MASK_SUFFIX_CAUSAL, ekv.MASK_SUFFIX_PREFIX_LM, ekv.MASK_SPAN_EXCLUDE,
+                                  ekv.MASK_SPAN_ONLY])
+def test_pair_masks(dtype, flag):
+    gen = torch.Generator().manual_seed(22)
+    f = Filled(dtype=dtype, B=3, prefix_lens=[300, 517, 96], Hkv=1, D=D, suffix_len=50, seed=22)
+    q = bf16_randn(gen, (3, 50, 8, D))
+    span = ([20, 100, 0], [276, 400, 64])
+    valid = [300, 500, 90]
+    kw = dict(mask_flags=flag, prefix_valid=valid)
+    if flag in (ekv.MASK_SPAN_EXCLUDE, ekv.MASK_SPAN_ONLY):
+        kw["span"] = span
+    got, single = both(f, q, Hq=8, scale=1 / 16, **kw)
+    want = oracle_attention(f, 0, q, scale=1 / 16, **kw)
+    check(got, want, TOL[dtype])
+    check(single, want, TOL[dtype])
+
+
+@pytest.mark.parametrize("dtype", [ekv.DTYPE_BF16, ekv.DTYPE_Q8_0])
+def test_pair_block_causal_64_token_blocks(dtype):
+    """Block-causal window over 64-token blocks (a block is larger than a CTA's 32-key K half)."""
+    gen = torch.Generator().manual_seed(23)
+    n_chunks, ct, stride = 3, 40, 64
+    f = Filled(dtype=dtype, B=2, prefix_lens=[n_chunks * stride] * 2, Hkv=1, D=D, block_tokens=64, seed=23)
+    q = bf16_randn(gen, (2, ct, 8, D))
+    block = (ct, stride, 2, n_chunks - 1)
+    got, single = both(f, q, Hq=8, scale=1 / 16, mask_flags=ekv.MASK_BLOCK_CAUSAL, block=block)
+    want = oracle_attention(f, 0, q, scale=1 / 16, mask_flags=ekv.MASK_BLOCK_CAUSAL, block=block)
+    check(got, want, TOL[dtype])
+    check(single, want, TOL[dtype])
+
+
+@pytest.mark.parametrize("dtype", [ekv.DTYPE_BF16, ekv.DTYPE_Q8_0])
+def test_pair_split_keys(dtype):
+    """Few pairs and long prefixes: the launcher splits keys across pairs through the workspace and
+    merges the partial outputs."""
+    gen = torch.Generator().manual_seed(24)
+    f = Filled(dtype=dtype, B=2, prefix_lens=[2000, 1459], Hkv=1, D=D, suffix_len=10, seed=24)
+    q = bf16_randn(gen, (2, 10, 8, D))
+    prm = f.pool.attention_params(layer=0, seq_ids=f.seq_ids, q_tokens=10, q_heads=8, scale=1 / 16,
+                                  suffix_len=f.suffix_len, out_dtype=ekv.DTYPE_F32)
+    assert f.pool.workspace_size(prm) > 0  # the splitter engages for this shape
+    a = run_attention(f, 0, q, Hq=8, scale=1 / 16, algo=ekv.ALGO_TC_PAIR)
+    b = run_attention(f, 0, q, Hq=8, scale=1 / 16, algo=ekv.ALGO_TC_PAIR, workspace=True)
+    want = oracle_attention(f, 0, q, scale=1 / 16)
+    check(a, want, TOL[dtype])
+    check(b, want, TOL[dtype])
+
+
+def test_pair_bf16_output_pi05_batch():
+    """The bench shape at a small batch, bf16 output: pair and single-CTA kernels agree to bf16
+    rounding of the same f32 results."""
+    gen = torch.Generator().manual_seed(25)
+    plens = [700, 816, 759, 701, 788, 730, 777, 812]
+    f = Filled(dtype=ekv.DTYPE_Q8_0, B=8, prefix_lens=plens, Hkv=1, D=D, suffix_len=50, seed=25)
+    q = bf16_randn(gen, (8, 50, 8, D))
+    got, single = both(f, q, Hq=8, scale=1 / 16, out_dtype=ekv.DTYPE_BF16)
+    want = oracle_attention(f, 0, q, scale=1 / 16)
+    check(got, want, TOL[ekv.DTYPE_Q8_0])
+    assert np.abs(got - single).max() <= 2e-2
