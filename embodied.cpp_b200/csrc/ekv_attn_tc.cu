@@ -90,7 +90,9 @@ struct TcCfg {
     static constexpr int TBL_ROOM = (232448 - 1024 - OFF_TBL) / 8;
     static constexpr int TBL = TBL_ROOM > 512 ? 512 : TBL_ROOM;
     static constexpr int SMEM = OFF_TBL + TBL * 8 + 1024;  // + 1 KB alignment slack
-    static constexpr int QSTR = D * 2 + 16;               // Q staging row stride (bank-conflict free)
+    // Q staging: rows of D*2 bytes whose 16-byte units are XOR-swizzled by the row (q_stage_off), so
+    // both the row-major stores and the per-row reads of a warp hit distinct bank groups
+    static constexpr int QSTR = D * 2;
     // BN = 64: two softmax warps per TMEM lane quarter, each owning half of the tile's columns
     static constexpr bool SPLIT = BN == 64;
     static constexpr int SMW = SPLIT ? 8 : 4;  // softmax warps
@@ -106,7 +108,7 @@ struct TcCfg {
     static_assert(Q_COL % 8 == 0, "TMEM alignment");
     static_assert(SMEM <= 232448, "shared-memory budget");
     static_assert(TBL >= 64, "block-table cache");
-    static_assert(BM * QSTR <= 2 * NSTAGE * KV_BYTES, "Q staging fits in the K/V stages");
+    static_assert(BM * QSTR <= NSTAGE * KV_BYTES, "Q staging fits in the V stages");
     static constexpr int OSTR = D * 4 + 16;  // epilogue staging row stride (f32 worst case)
     static_assert(BM * OSTR <= OFF_BAR, "epilogue staging fits below the barriers");
     static_assert(D % 16 == 0, "head_dim must be a multiple of 16");
@@ -124,7 +126,8 @@ enum {
     BAR_P_FULL = 16,     // [2] P(j) in TMEM
     BAR_DONE = 18,
     BAR_XCH = 19,        // [4] softmax pair exchange (one per TMEM lane quarter; SPLIT only)
-    N_BARS = 23
+    BAR_Q_READY = 23,    // Q in TMEM and its shared staging (in the V stages) read
+    N_BARS = 24
 };
 // One commit per MMA group: "S(j) done" is the completion of K stage j % NS and "P.V(j) done"
 // that of V stage j % NS. A waiter for S(j) or P.V(j - 1) in the softmax cannot be overtaken by a
@@ -216,6 +219,15 @@ __device__ __forceinline__ const uint8_t *ptr_of(const AttnArgs &a, const Plan &
                    : a.pool.prefix + prefix_tile_index(a.pool, a.layer, blk, 0, pl.g) * a.pool.tile_bytes;
 }
 
+// Byte offset of 16-byte unit `c` of staged Q row `r` (rows of `qstr` bytes). When a row has a
+// multiple of 8 units (head_dim 64, 128, 256), the units are XOR-swizzled by r & 7, so 8
+// consecutive rows of one unit land in 8 different bank groups; other widths are not swizzled.
+__device__ __forceinline__ uint32_t q_stage_off(int r, int c, int qstr) {
+    const int units = qstr / 16;
+    const int m = (units % 8 == 0) ? 7 : 0;
+    return (uint32_t)(r * qstr + ((c ^ (r & m)) << 4));
+}
+
 // ---- Q: bf16 [B][Tq][Hq][D] rows -> shared staging (all threads, every load in flight before
 // the first store) -> TMEM Q columns (softmax warps, one row per thread; f16 for Q8_0 pools) ----
 template <int D, bool Q8>
@@ -252,7 +264,7 @@ __device__ __forceinline__ void stage_q_store(const QStage<D, Q8> &qs, uint8_t *
         const int u = threadIdx.x + i * TcCfg<D, Q8>::THREADS;
         if (u >= Q::UNITS) break;
         const int r = u / Q::UPR;
-        *(uint4 *)(stg + r * TcCfg<D, Q8>::QSTR + (u - r * Q::UPR) * 16) = qs.val[i];
+        *(uint4 *)(stg + q_stage_off(r, u - r * Q::UPR, TcCfg<D, Q8>::QSTR)) = qs.val[i];
     }
 }
 
@@ -261,8 +273,8 @@ __device__ __forceinline__ void q_to_tmem(const uint8_t *stg, int r, uint32_t ta
     using C = TcCfg<D, Q8>;
 #pragma unroll 1
     for (int c = c_lo; c < c_hi; ++c) {  // 16 elements = 8 columns per store
-        const uint4 a0 = *(const uint4 *)(stg + r * C::QSTR + c * 32);
-        const uint4 a1 = *(const uint4 *)(stg + r * C::QSTR + c * 32 + 16);
+        const uint4 a0 = *(const uint4 *)(stg + q_stage_off(r, 2 * c, C::QSTR));
+        const uint4 a1 = *(const uint4 *)(stg + q_stage_off(r, 2 * c + 1, C::QSTR));
         uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         if (Q8) {
 #pragma unroll
@@ -753,6 +765,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
         }
         mbar_init(bar(BAR_DONE), 1);
         for (int q = 0; q < 4; ++q) mbar_init(bar(BAR_XCH + q), 2);
+        mbar_init(bar(BAR_Q_READY), C::SMW);
         *abort = 0;
         mbar_init_fence();
     }
@@ -766,7 +779,9 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
             sPtr[i] = blk < 0 ? nullptr
                               : a.pool.prefix + prefix_tile_index(a.pool, a.layer, blk, 0, pl.g) * a.pool.tile_bytes;
         }
-    stage_q_store<D, Q8>(qstage, smem + C::OFF_K);
+    // Q is staged in the V stages: the K stages and the raw ring can fill while Q goes to TMEM;
+    // the first V write and the first MMA wait for BAR_Q_READY.
+    stage_q_store<D, Q8>(qstage, smem + C::OFF_V);
     if (threadIdx.x == 0) TRACE(2);
     tc_fence_before();
     __syncthreads();
@@ -776,14 +791,14 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
     if (warp < C::SMW) {
         // row (warp & 3) * 32 + lane; with SPLIT the two warps of a lane quarter take half the columns each
         const int h = C::SPLIT ? warp >> 2 : 0, nh = C::SPLIT ? 2 : 1;
-        q_to_tmem<D, Q8>(smem + C::OFF_K, (warp & 3) * 32 + lane, tmem + lane_base + C::Q_COL, h * (D / 16) / nh,
+        q_to_tmem<D, Q8>(smem + C::OFF_V, (warp & 3) * 32 + lane, tmem + lane_base + C::Q_COL, h * (D / 16) / nh,
                          (h + 1) * (D / 16) / nh);
         tmem_wait_st();
+        fence_proxy_async();  // staging reads (generic) before the copy engine refills the V stages
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(BAR_Q_READY));
     }
-    fence_proxy_async();  // staging reads (generic) before the copy engine refills the stages
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
     if (threadIdx.x == 0) TRACE(3);
     const int n = pl.j1 - pl.j0;
 
@@ -828,7 +843,9 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                 if (jj < 50) TRACE(250 + jj);
                 return true;
             };
-            ok = issue_s(0);
+            ok = mbar_wait(bar(BAR_Q_READY), 0, abort, kWaitBudget);
+            tc_fence_after();
+            if (ok) ok = issue_s(0);
             for (int jj = 0; ok && jj < n; ++jj) {
                 if (jj + 1 < n) ok = issue_s(jj + 1);
                 if (ok) ok = issue_pv(jj);
@@ -879,6 +896,10 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                 }
                 if (it >= 1) {
                     const int v = it - 1, st = v % NS;
+                    if (v == 0 && !mbar_wait(bar(BAR_Q_READY), 0, abort, kWaitBudget)) {  // Q staging read
+                        fail_timeout(a, abort, 2);
+                        break;
+                    }
                     if (v >= NS && !mbar_wait(bar(BAR_V_EMPTY + st), ((v - NS) / NS) & 1, abort, kWaitBudget)) {
                         fail_timeout(a, abort, 2);
                         break;
@@ -916,6 +937,10 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
                 for (int kv = 0; kv < 2; ++kv) {
                     const int b_empty = kv ? BAR_V_EMPTY : BAR_K_EMPTY, b_full = kv ? BAR_V_FULL : BAR_K_FULL;
                     uint8_t *dst = (kv ? sV : sK) + st * C::KV_BYTES;
+                    if (kv == 1 && jj == 0 && !mbar_wait(bar(BAR_Q_READY), 0, abort, kWaitBudget)) {  // Q staging read
+                        ok = false;
+                        break;
+                    }
                     if (jj >= NS && !mbar_wait(bar(b_empty + st), ((jj - NS) / NS) & 1, abort, kWaitBudget)) {
                         ok = false;
                         break;
