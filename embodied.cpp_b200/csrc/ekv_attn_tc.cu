@@ -31,10 +31,14 @@
 // Every mbarrier wait is bounded (clock64 budget); on expiry the kernel records
 // DEV_ERR_TIMEOUT in the pool status word, raises a CTA-local abort flag and unwinds, waiting
 // for its own in-flight copies and MMAs before releasing tensor memory.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <climits>
+#include <cstring>
 
 #include "ekv_device.cuh"
 #include "ekv_internal.h"
@@ -111,6 +115,7 @@ struct TcCfg {
     static_assert(BM * QSTR <= NSTAGE * KV_BYTES, "Q staging fits in the V stages");
     static constexpr int OSTR = D * 4 + 16;  // epilogue staging row stride (f32 worst case)
     static_assert(BM * OSTR <= OFF_BAR, "epilogue staging fits below the barriers");
+    static_assert(((D + 31) / 32) * 4 * 4096 <= OFF_BAR, "epilogue boxes (f32) fit below the barriers");
     static_assert(D % 16 == 0, "head_dim must be a multiple of 16");
 };
 
@@ -526,6 +531,72 @@ __device__ __forceinline__ bool pair_sync(uint32_t xbar, int use, volatile int *
     return mbar_wait(xbar, (uint32_t)use & 1u, abort, kWaitBudget);
 }
 
+// ---- output epilogue through the copy engine ----
+// O rows are staged as 4 KB boxes of 32 rows (one TMEM lane quarter) x 128 bytes (64 bf16 or 32
+// f32 columns), 128-byte swizzled: 16-byte unit u of box row i sits at unit u ^ (i & 7), the layout
+// a CU_TENSOR_MAP_SWIZZLE_128B map reads, so the 8 lanes of a store phase hit 8 distinct bank
+// groups. Box (cb, quarter) is at cb * 4 + quarter. Lane 0 of each warp then stores the warp's
+// boxes with cp.async.bulk.tensor: no cross-warp barrier, and no thread-issued global stores (which
+// drain several times slower than the copy engine's from this kernel).
+enum { OUT_THREADS = 0, OUT_TMA_ROWS = 1, OUT_TMA_WS = 2 };
+constexpr int kOutBox = 4096;
+
+// Stage columns [c0, c0 + EC) of this thread's row (`lane` of lane quarter `quarter`), times inv.
+template <int EC>
+__device__ __forceinline__ void stage_o_box(uint8_t *boxes, int quarter, int lane, int c0, const uint32_t *o, float inv,
+                                            bool f32) {
+    static_assert(EC == 16 || EC == 32, "column chunk");
+    const int sw = lane & 7;
+    if (f32) {
+        uint8_t *row = boxes + ((c0 >> 5) * 4 + quarter) * kOutBox + lane * 128;
+        const int u0 = (c0 & 31) >> 2;
+#pragma unroll
+        for (int i = 0; i < EC / 4; ++i)
+            *(float4 *)(row + (((u0 + i) ^ sw) << 4)) =
+                make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                            __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+    } else {
+        uint8_t *row = boxes + ((c0 >> 6) * 4 + quarter) * kOutBox + lane * 128;
+        const int u0 = (c0 & 63) >> 3;
+#pragma unroll
+        for (int i = 0; i < EC / 8; ++i) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 2 * e]) * inv,
+                                                                __uint_as_float(o[8 * i + 2 * e + 1]) * inv);
+                w[e] = *(const uint32_t *)&b2;
+            }
+            *(uint4 *)(row + (((u0 + i) ^ sw) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// Whole warp, after staging its boxes [cb0, cb1) of lane quarter `quarter`: lane 0 stores them and
+// waits until the copy engine has read them (the CTA may exit afterwards). OUT_TMA_ROWS maps the
+// output as (head_dim, head in group, KV head, token, batch): box row i of the quarter is query
+// row qrow0 + quarter * 32 + i, and rows past the call's tokens fall outside the map. OUT_TMA_WS
+// maps the workspace as (head_dim, unit * 128 + row).
+__device__ __forceinline__ void store_o_boxes(const AttnArgs &a, const Plan &pl, const void *omap, int omode,
+                                              const uint8_t *boxes, int quarter, int cb0, int cb1, int boxc,
+                                              int64_t unit) {
+    fence_proxy_async();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0 && quarter * 32 < pl.rows_valid) {
+        const int row0 = pl.qrow0 + quarter * 32;
+        for (int cb = cb0; cb < cb1; ++cb) {
+            const uint32_t src = smem_addr(boxes + (cb * 4 + quarter) * kOutBox);
+            if (omode == OUT_TMA_ROWS)
+                tma_store_5d(omap, src, cb * boxc, row0 % a.group, pl.g, row0 / a.group, pl.b);
+            else
+                tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM) + quarter * 32);
+        }
+        bulk_commit_group();
+        bulk_wait_group_read0();
+    }
+    __syncwarp();
+}
+
 // ---- softmax / epilogue with two warps per TMEM lane quarter (BN = 64): warp w owns query row
 // (w & 3) * 32 + lane and S columns [h * 32, h * 32 + 32) of every tile, h = w >> 2. Per tile the
 // two warps swap their masked chunk maxima through shared memory; P for the 32 keys goes back as
@@ -534,7 +605,7 @@ __device__ __forceinline__ bool pair_sync(uint32_t xbar, int use, volatile int *
 template <int D, bool Q8>
 __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan &pl, uint8_t *smem, uint32_t bar0,
                                                    volatile int *abort, uint32_t tmem, uint32_t lane_base, int n,
-                                                   int n_qtiles) {
+                                                   int n_qtiles, const void *omap, int omode) {
     using C = TcCfg<D, Q8>;
     constexpr int BN = C::BN, DH = D / 2;
     static_assert(BN == 64, "split softmax: 32 columns per warp");
@@ -679,6 +750,23 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
             wml[1] = have_o ? l_row : 0.0f;
         }
     }
+    if (omode != OUT_THREADS) {
+        // this warp's columns [h * D/2, (h + 1) * D/2) of its lane quarter -> swizzled boxes -> copy engine
+        const int boxc = f32 ? 32 : 64;
+#pragma unroll 1
+        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
+            uint32_t o32[32];
+            if (have_o) {
+                tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o32[i] = 0u;
+            }
+            stage_o_box<32>(smem + C::OFF_K, quarter, lane, c0, o32, inv, f32);
+        }
+        store_o_boxes(a, pl, omap, omode, smem + C::OFF_K, quarter, h * DH / boxc, (h + 1) * DH / boxc, boxc, unit);
+        return;
+    }
     uint8_t *orow = (smem + C::OFF_K) + r * C::OSTR;
 #pragma unroll 1
     for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
@@ -727,7 +815,8 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
 }
 
 template <int D, bool Q8>
-__global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const AttnArgs a, int n_qtiles) {
+__global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
+    attn_tc_kernel(const AttnArgs a, int n_qtiles, const __grid_constant__ CUtensorMap omap, int omode) {
     using C = TcCfg<D, Q8>;
     constexpr int BN = C::BN, W = C::W, NS = C::NSTAGE;
     extern __shared__ uint8_t smem_raw[];
@@ -963,7 +1052,8 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
             }
         }
     } else if (warp < C::SMW && C::SPLIT) {
-        if constexpr (C::SPLIT) softmax_split_role<D, Q8>(a, pl, smem, bar0, abort, tmem, lane_base, n, n_qtiles);
+        if constexpr (C::SPLIT)
+            softmax_split_role<D, Q8>(a, pl, smem, bar0, abort, tmem, lane_base, n, n_qtiles, &omap, omode);
     } else if (warp < 4) {
         // ---- softmax / epilogue: thread = query row = TMEM lane ----
         const int r = threadIdx.x;
@@ -1093,7 +1183,40 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1) attn_tc_kernel(const
         // ---- epilogue ----
         if (r == 0) TRACE(10);
         const bool have_o = ok && n > 0;
-        if (a.n_splits > 1) {
+        if (omode != OUT_THREADS) {
+            // O (or O / l) of this warp's lane quarter -> swizzled boxes -> copy engine
+            const bool split = a.n_splits > 1;
+            const bool f32 = split || a.out_dtype == EKV_DTYPE_F32;
+            const float inv = split ? 1.0f : ((have_o && l > 0.0f) ? 1.0f / l : 0.0f);
+            int64_t unit = 0;
+            if (split) {
+                unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
+                if (row_ok) {
+                    float *wml = a.ws_ml + (unit * kBM + r) * 2;
+                    wml[0] = have_o ? m_used : -INFINITY;
+                    wml[1] = have_o ? l : 0.0f;
+                }
+            }
+            constexpr int EC = (D % 32 == 0) ? 32 : 16;  // columns per TMEM load
+#pragma unroll 2
+            for (int c0 = 0; c0 < D; c0 += EC) {
+                uint32_t rr[32];
+                if (have_o) {
+                    if constexpr (EC == 32) {
+                        tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), rr);
+                    } else {
+                        uint32_t (&r16)[16] = *reinterpret_cast<uint32_t (*)[16]>(rr);
+                        tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), r16);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < EC; ++i) rr[i] = 0u;
+                }
+                stage_o_box<EC>(smem + C::OFF_K, warp, lane, c0, rr, inv, f32);
+            }
+            const int boxc = f32 ? 32 : 64;
+            store_o_boxes(a, pl, &omap, omode, smem + C::OFF_K, warp, 0, (D + boxc - 1) / boxc, boxc, unit);
+        } else if (a.n_splits > 1) {
             const int64_t unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
             float *wo = a.ws_o + (unit * kBM + r) * D;
             float *wml = a.ws_ml + (unit * kBM + r) * 2;
@@ -1256,6 +1379,58 @@ int sm_count() {
 
 int choose_splits(int64_t units, int max_tiles) { return choose_split_count(units, max_tiles, sm_count()); }
 
+// cuTensorMapEncodeTiled from the driver the runtime loaded (no link-time libcuda dependency).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+        return (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }();
+    return fn;
+}
+
+// The epilogue's store route for this call (OUT_*), and the tensor map it stores through.
+// With key splits: the f32 workspace as (head_dim, unit * 128 + row), 32 x 32 boxes. Otherwise the
+// output [B, Tq, Hq, D] as (head_dim, head in group, KV head, token, batch) with boxes of 32 query
+// rows: min(group, 32) heads x max(1, 32 / group) tokens, which needs a group dividing 128 (then a
+// quarter's rows never straddle the end of the call's tokens unless the map clips them). Other
+// shapes keep the thread-store epilogue.
+int make_out_map(const AttnArgs &a, int D, int64_t units, CUtensorMap *map) {
+    std::memset(map, 0, sizeof(*map));
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return OUT_THREADS;
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    if (a.n_splits > 1) {
+        const int64_t rows = units * a.n_splits * kBM;
+        if (D % 32 || rows > INT_MAX || ((uintptr_t)a.ws_o & 15)) return OUT_THREADS;
+        const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+        const cuuint32_t box[2] = {32, 32};
+        return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.ws_o, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+                   ? OUT_TMA_WS
+                   : OUT_THREADS;
+    }
+    const bool f32 = a.out_dtype == EKV_DTYPE_F32;
+    const int es = f32 ? 4 : 2, boxc = f32 ? 32 : 64;
+    if (D % boxc || a.group <= 0 || kBM % a.group || ((uintptr_t)a.out & 15)) return OUT_THREADS;
+    const cuuint64_t dims[5] = {(cuuint64_t)D, (cuuint64_t)a.group, (cuuint64_t)a.pool.kv_heads,
+                                (cuuint64_t)a.q_tokens, (cuuint64_t)a.n_batch};
+    const cuuint64_t strides[4] = {(cuuint64_t)D * es, (cuuint64_t)a.group * D * es, (cuuint64_t)a.q_heads * D * es,
+                                   (cuuint64_t)a.q_tokens * a.q_heads * D * es};
+    const cuuint32_t box[5] = {(cuuint32_t)boxc, (cuuint32_t)std::min(a.group, 32), 1,
+                               (cuuint32_t)std::max(1, 32 / a.group), 1};
+    return enc(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, a.out, dims, strides,
+               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+               ? OUT_TMA_ROWS
+               : OUT_THREADS;
+}
+
 template <int D, bool Q8>
 int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
     using C = TcCfg<D, Q8>;
@@ -1287,7 +1462,9 @@ int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
     if ((int64_t)n_qtiles * a.n_splits > 0x7fffffff || a.pool.kv_heads > 65535 || a.n_batch > 65535)
         return EKV_ERR_INVALID_ARG;
     dim3 grid((unsigned)(n_qtiles * a.n_splits), (unsigned)a.pool.kv_heads, (unsigned)a.n_batch);
-    attn_tc_kernel<D, Q8><<<grid, C::THREADS, C::SMEM, s>>>(a, n_qtiles);
+    CUtensorMap omap;
+    const int omode = make_out_map(a, D, units, &omap);
+    attn_tc_kernel<D, Q8><<<grid, C::THREADS, C::SMEM, s>>>(a, n_qtiles, omap, omode);
     if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
     if (a.n_splits > 1) {
         merge_splits_kernel<D><<<dim3(n_qtiles * (kBM / kMergeWarps), a.pool.kv_heads, a.n_batch), kMergeWarps * 32, 0, s>>>(

@@ -251,6 +251,23 @@ def test_attention_split_keys_matches_unsplit(dtype):
     check(b, want, TOL[dtype])
 
 
+@pytest.mark.parametrize("out_dtype", [ekv.DTYPE_F32, ekv.DTYPE_BF16])
+@pytest.mark.parametrize("Hq,Hkv,Tq", [(16, 1, 9), (32, 2, 5), (64, 1, 3), (128, 1, 3), (2, 1, 70), (12, 4, 11)])
+def test_attention_output_row_boxes(out_dtype, Hq, Hkv, Tq):
+    """The tensor-core epilogue stores 32 query rows at a time: min(group, 32) heads x
+    max(1, 32 / group) tokens. Groups from 2 to 128 (both box shapes), row counts that end inside a
+    32-row quarter and inside a 128-row tile, and a group of 3 that keeps the thread-store epilogue.
+    The output starts as NaN, so an unwritten row fails the finiteness check."""
+    gen = torch.Generator().manual_seed(12)
+    f = Filled(dtype=ekv.DTYPE_BF16, B=2, prefix_lens=[150, 77], Hkv=Hkv, D=64, suffix_len=Tq, seed=12)
+    q = bf16_randn(gen, (2, Tq, Hq, 64))
+    want = oracle_attention(f, 0, q, scale=0.125)
+    got = run_attention(f, 0, q, Hq=Hq, scale=0.125, algo=ekv.ALGO_TC, out_dtype=out_dtype)
+    check(got, want, 2e-2)
+    got = run_attention(f, 0, q, Hq=Hq, scale=0.125, algo=ekv.ALGO_TC, out_dtype=out_dtype, workspace=True)
+    check(got, want, 2e-2)
+
+
 def test_attention_bf16_output_and_fully_masked_rows():
     """bf16 output; a request whose every key is masked returns zeros
     (models/lingbot_va.cpp:9503-9506)."""
