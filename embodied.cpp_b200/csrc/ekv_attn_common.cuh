@@ -2,13 +2,56 @@
 // closed-form key-visibility words, paged-block indexing, Q8_0 -> f16 and bf16 -> f16 conversion.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <climits>
+#include <cstring>
 
 #include "ekv_device.cuh"
 #include "ekv_internal.h"
+#include "ekv_sm100.cuh"
 
 namespace ekv {
+namespace {
+#ifdef EKV_TRACE
+// Diagnostic builds only: CTAs (0, 0, 0) and (1, 0, 0) stamp globaltimer (low 32 bits) into shared memory, flushed
+// to the host buffer at the end (a global store per stamp would perturb the roles it times).
+__constant__ unsigned long long *c_trace = nullptr;
+constexpr int kTraceSlots = 1024;
+__shared__ unsigned int s_trace[kTraceSlots];
+__device__ __forceinline__ bool trace_cta() { return c_trace && blockIdx.x < 2 && blockIdx.y == 0 && blockIdx.z == 0; }
+__device__ __forceinline__ void trace_at(int slot) {
+    if (trace_cta()) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        s_trace[slot] = (unsigned int)t;
+    }
+}
+#define TRACE(slot) trace_at(slot)
+__device__ __forceinline__ void trace_clock(int slot) {
+    if (trace_cta()) s_trace[slot] = (unsigned int)clock64();
+}
+#define TRACE_CLK(slot) trace_clock(slot)
+__device__ __forceinline__ void trace_init() {
+    if (trace_cta())
+        for (int i = 0; i < kTraceSlots; ++i) s_trace[i] = 0u;
+}
+__device__ __forceinline__ void trace_flush() {
+    if (trace_cta())
+        for (int i = threadIdx.x; i < kTraceSlots; i += blockDim.x) c_trace[blockIdx.x * kTraceSlots + i] = s_trace[i];
+}
+#else
+#define TRACE(slot) ((void)0)
+#define TRACE_CLK(slot) ((void)0)
+__device__ __forceinline__ void trace_init() {}
+__device__ __forceinline__ void trace_flush() {}
+#endif
+}  // namespace
+
 namespace {
 
 constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (~2-3 s) before giving up
@@ -119,6 +162,131 @@ __device__ __forceinline__ void dequant16(const uint4 q, uint32_t dbits, uint4 &
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+
+using sm100::bulk_commit_group;
+using sm100::bulk_wait_group_read0;
+using sm100::fence_proxy_async;
+using sm100::smem_addr;
+using sm100::tma_store_2d;
+using sm100::tma_store_5d;
+
+// ---- output epilogue through the copy engine ----
+// O rows are staged as 4 KB boxes of 32 rows (one TMEM lane quarter) x 128 bytes (64 bf16 or 32
+// f32 columns), 128-byte swizzled: 16-byte unit u of box row i sits at unit u ^ (i & 7), the layout
+// a CU_TENSOR_MAP_SWIZZLE_128B map reads, so the 8 lanes of a store phase hit 8 distinct bank
+// groups. Box (cb, quarter) is at cb * 4 + quarter. Lane 0 of each warp then stores the warp's
+// boxes with cp.async.bulk.tensor: no cross-warp barrier, and no thread-issued global stores (which
+// drain several times slower than the copy engine's from this kernel).
+enum { OUT_THREADS = 0, OUT_TMA_ROWS = 1, OUT_TMA_WS = 2 };
+constexpr int kOutBox = 4096;
+
+// Stage columns [c0, c0 + EC) of this thread's row (`lane` of lane quarter `quarter`), times inv.
+template <int EC>
+__device__ __forceinline__ void stage_o_box(uint8_t *boxes, int quarter, int lane, int c0, const uint32_t *o, float inv,
+                                            bool f32) {
+    static_assert(EC == 16 || EC == 32, "column chunk");
+    const int sw = lane & 7;
+    if (f32) {
+        uint8_t *row = boxes + ((c0 >> 5) * 4 + quarter) * kOutBox + lane * 128;
+        const int u0 = (c0 & 31) >> 2;
+#pragma unroll
+        for (int i = 0; i < EC / 4; ++i)
+            *(float4 *)(row + (((u0 + i) ^ sw) << 4)) =
+                make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                            __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+    } else {
+        uint8_t *row = boxes + ((c0 >> 6) * 4 + quarter) * kOutBox + lane * 128;
+        const int u0 = (c0 & 63) >> 3;
+#pragma unroll
+        for (int i = 0; i < EC / 8; ++i) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 2 * e]) * inv,
+                                                                __uint_as_float(o[8 * i + 2 * e + 1]) * inv);
+                w[e] = *(const uint32_t *)&b2;
+            }
+            *(uint4 *)(row + (((u0 + i) ^ sw) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// Whole warp, after staging its boxes [cb0, cb1) of lane quarter `quarter`: lane 0 stores them and
+// waits until the copy engine has read them (the CTA may exit afterwards). OUT_TMA_ROWS maps the
+// output as (head_dim, head in group, KV head, token, batch): box row i of the quarter is query
+// row qrow0 + quarter * 32 + i, and rows past the call's tokens fall outside the map. OUT_TMA_WS
+// maps the workspace as (head_dim, unit * 128 + row).
+__device__ __forceinline__ void store_o_boxes(const AttnArgs &a, int qrow0, int rows_valid, int g, int b,
+                                              const void *omap, int omode, const uint8_t *boxes, int quarter, int cb0,
+                                              int cb1, int boxc, int64_t unit) {
+    fence_proxy_async();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0 && quarter * 32 < rows_valid) {
+        const int row0 = qrow0 + quarter * 32;
+        for (int cb = cb0; cb < cb1; ++cb) {
+            const uint32_t src = smem_addr(boxes + (cb * 4 + quarter) * kOutBox);
+            if (omode == OUT_TMA_ROWS)
+                tma_store_5d(omap, src, cb * boxc, row0 % a.group, g, row0 / a.group, b);
+            else
+                tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM) + quarter * 32);
+        }
+        bulk_commit_group();
+        bulk_wait_group_read0();
+    }
+    __syncwarp();
+}
+
+// cuTensorMapEncodeTiled from the driver the runtime loaded (no link-time libcuda dependency).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+        return (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }();
+    return fn;
+}
+
+// The epilogue's store route for this call (OUT_*), and the tensor map it stores through.
+// With key splits: the f32 workspace as (head_dim, unit * 128 + row), 32 x 32 boxes. Otherwise the
+// output [B, Tq, Hq, D] as (head_dim, head in group, KV head, token, batch) with boxes of 32 query
+// rows: min(group, 32) heads x max(1, 32 / group) tokens, which needs a group dividing 128 (then a
+// quarter's rows never straddle the end of the call's tokens unless the map clips them). Other
+// shapes keep the thread-store epilogue.
+int make_out_map(const AttnArgs &a, int D, int64_t units, CUtensorMap *map) {
+    std::memset(map, 0, sizeof(*map));
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return OUT_THREADS;
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    if (a.n_splits > 1) {
+        const int64_t rows = units * a.n_splits * kBM;
+        if (D % 32 || rows > INT_MAX || ((uintptr_t)a.ws_o & 15)) return OUT_THREADS;
+        const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+        const cuuint32_t box[2] = {32, 32};
+        return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.ws_o, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+                   ? OUT_TMA_WS
+                   : OUT_THREADS;
+    }
+    const bool f32 = a.out_dtype == EKV_DTYPE_F32;
+    const int es = f32 ? 4 : 2, boxc = f32 ? 32 : 64;
+    if (D % boxc || a.group <= 0 || kBM % a.group || ((uintptr_t)a.out & 15)) return OUT_THREADS;
+    const cuuint64_t dims[5] = {(cuuint64_t)D, (cuuint64_t)a.group, (cuuint64_t)a.pool.kv_heads,
+                                (cuuint64_t)a.q_tokens, (cuuint64_t)a.n_batch};
+    const cuuint64_t strides[4] = {(cuuint64_t)D * es, (cuuint64_t)a.group * D * es, (cuuint64_t)a.q_heads * D * es,
+                                   (cuuint64_t)a.q_tokens * a.q_heads * D * es};
+    const cuuint32_t box[5] = {(cuuint32_t)boxc, (cuuint32_t)std::min(a.group, 32), 1,
+                               (cuuint32_t)std::max(1, 32 / a.group), 1};
+    return enc(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, a.out, dims, strides,
+               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+               ? OUT_TMA_ROWS
+               : OUT_THREADS;
+}
 
 }  // namespace
 }  // namespace ekv

@@ -49,8 +49,11 @@ struct PairCfg {
     static constexpr uint32_t V_LBO = 8 * W;                      // 1024 (chunk stride along d)
     static constexpr uint32_t V_SBO = (VH_COLS * 2 / W) * 8 * W;  // 2048 (8-row group stride)
     static constexpr int NSTAGE = Q8 ? 4 : 6;
-    static constexpr int NRAW = Q8 ? 2 : 0;
-    static constexpr int RAW_BYTES = BN * (D + D / 16) * 2;  // whole raw tile: K and V of 64 rows
+    // raw Q8_0 ring: per tile, K and V of this CTA's 32 key rows, then V of the peer's 32 rows
+    // (int8 + fp16 scales)
+    static constexpr int NRAW = Q8 ? 3 : 0;
+    static constexpr int RAW_ROWB = D + D / 16;  // raw bytes per key row
+    static constexpr int RAW_BYTES = 3 * KH_ROWS * RAW_ROWB;
     static constexpr int OFF_K = 0;
     static constexpr int OFF_V = NSTAGE * KH_BYTES;
     static constexpr int OFF_RAW = OFF_V + NSTAGE * VH_BYTES;
@@ -64,29 +67,35 @@ struct PairCfg {
     static constexpr int QSTR = D * 2 + 16;  // Q staging row stride
     static constexpr int OSTR = D * 4 + 16;  // epilogue staging row stride (f32 worst case)
     static constexpr int SMW = 8;
-    static constexpr int MMA_WARP = 8, TMA_WARP = 9, DQ_WARP0 = 10;
-    static constexpr int THREADS = (SMW + 2) * 32 + (Q8 ? kDq : 0);
+    // 8 = MMA issue (rank 0) / relay (rank 1); 9, 10 = K and V copy feeders; 11-18 = dequantisation
+    static constexpr int MMA_WARP = 8, TMA_WARP = 9, DQ_WARP0 = 11;
+    static constexpr int THREADS = (SMW + 3) * 32 + (Q8 ? kDq : 0);
     static constexpr int TMEM_COLS = 512;
     static constexpr int S_COL = 0, O_COL = 2 * BN, Q_COL = 512 - D / 2;
     static_assert(O_COL + D <= Q_COL, "TMEM budget");
     static_assert(SMEM <= 232448, "shared-memory budget");
     static_assert(TBL >= 64, "block-table cache");
     static_assert(kBM * QSTR <= OFF_BAR && kBM * OSTR <= OFF_BAR, "Q and epilogue staging fit below the barriers");
+    static_assert((D / 32) * 4 * kOutBox <= OFF_BAR, "epilogue boxes (f32) fit below the barriers");
 };
 
+// Rank 1's softmax and dequantisation warps arrive directly on rank 0's barriers (P_FULL, K_PEER,
+// V_PEER); for bf16, rank 1's relay thread forwards its copies' completion to K_PEER / V_PEER. All
+// arrivals release at CTA scope (mbar_arrive_remote).
 enum {
-    PB_K_FULL = 0,     // [6] this CTA's K half landed (local producer)
-    PB_K_PEER = 6,     // [6] rank 1's K half landed (rank 0 only: relay / remote arrivals)
-    PB_K_EMPTY = 12,   // [6] S(j) done (committed to both CTAs): K stage free, S(j) readable
-    PB_V_FULL = 18,    // [6]
-    PB_V_PEER = 24,    // [6]
-    PB_V_EMPTY = 30,   // [6] P.V(j) done (both CTAs): V stage free, P(j) consumed, O updated
-    PB_RAW_FULL = 36,  // [2] raw Q8_0 tile landed
-    PB_RAW_EMPTY = 38, // [2] raw Q8_0 tile read by the dequant warps
-    PB_P_FULL = 40,    // [2] P(j) written by the softmax warps of both CTAs (rank 0 only)
-    PB_DONE = 42,
-    PB_XCH = 43,       // [4] softmax pair exchange
-    PB_N = 47
+    PB_K_FULL = 0,       // [6] this CTA's K half landed / dequantised
+    PB_K_PEER = 6,       // [6] rank 1's K half ready (rank 0 only)
+    PB_K_EMPTY = 12,     // [6] S(j) done (committed to both CTAs): K stage free, S(j) readable
+    PB_V_FULL = 18,      // [6]
+    PB_V_PEER = 24,      // [6]
+    PB_V_EMPTY = 30,     // [6] P.V(j) done (both CTAs): V stage free, P(j) consumed, O updated
+    PB_RAW_FULL = 36,    // [3] raw Q8_0 stage landed (both feeders' copies)
+    PB_RAW_EMPTY = 39,   // [3] raw Q8_0 stage read by the dequant warps
+                         // 42-45 unused
+    PB_P_FULL = 46,      // [2] P(j) written by the softmax warps of both CTAs (rank 0 only)
+    PB_DONE = 48,
+    PB_XCH = 49,         // [4] softmax pair exchange
+    PB_N = 53
 };
 static_assert(PB_N * 8 + 16 <= 512, "barrier block");
 
@@ -246,65 +255,68 @@ __device__ __forceinline__ void pair_produce_bf16(const AttnArgs &a, const PairP
     if (src) bulk_g2s(smem_addr(sDst + dst), src, bytes, bar_full);
 }
 
-// ---- Q8_0 feeder: the whole raw tile (K and V of 64 rows), one copy per block when a block's K
-// and V tiles are adjacent (one KV head), as in the one-CTA kernel. ----
+// ---- Q8_0 feeders. A raw stage holds, per segment of ks = min(block_tokens, 32) key rows: first the
+// K and V parts of this CTA's rows [32r, 32r + 32) of the tile (own = 1), then the V parts of the
+// peer's rows (own = 0). Each part is [qs ks x D][fp16 scales ks x D/32] -- exactly a pool tile, so
+// a whole block with adjacent K and V tiles (one KV head) is ONE copy of both parts. One lane per
+// segment; both feeders arrive on the stage's barrier with their byte counts. ----
 __device__ __forceinline__ void pair_produce_q8_raw(const AttnArgs &a, const PairPlan &pl, const uint8_t *const *sPtr,
-                                                    int j, uint8_t *raw, uint32_t bar_full, int lane) {
+                                                    int j, int own, uint8_t *raw, uint32_t bar_full, int lane) {
     using C = PairCfg<true>;
     constexpr int BN = C::BN, D = C::D, SCB = D / 16;
     const PoolView &p = a.pool;
     const int bt = p.block_tokens;
-    const int vbt = min(bt, BN), n_seg = BN / vbt;
-    const uint32_t vtile = (uint32_t)vbt * (D + SCB);
-    const uint32_t part = 2 * vtile;
+    const int ks = min(bt, C::KH_ROWS), n_seg = C::KH_ROWS / ks;
+    const int row0 = (own ? pl.rank : 1 - pl.rank) * C::KH_ROWS;
+    const uint32_t part = (uint32_t)ks * (D + SCB);
+    const uint32_t seg_bytes = own ? 2 * part : part;
+    uint8_t *base = raw + (own ? 0 : 2 * C::KH_ROWS * C::RAW_ROWB);
     const uint8_t *tk = nullptr;
     int rib = 0;
     if (lane < n_seg) {
-        const int k = pl.kbeg + j * BN + lane * vbt;
+        const int k = pl.kbeg + j * BN + row0 + lane * ks;
         const int idx = block_index(p, k, rib);
         if (k < pl.sk.n_prefix) tk = pair_ptr_of<C::TBL>(a, pl, sPtr, idx);
     }
-    const uint32_t segmask = n_seg >= 32 ? 0xffffffffu : ((1u << n_seg) - 1u);
+    const uint32_t segmask = (1u << n_seg) - 1u;
     const uint32_t valid = __ballot_sync(0xffffffffu, tk != nullptr) & segmask;
     const uint32_t missing = ~valid & segmask;
     if (missing) {
         for (uint32_t m = missing; m; m &= m - 1) {
-            uint8_t *z = raw + (__ffs(m) - 1) * part;
-            for (uint32_t o = lane * 16; o < part; o += 32 * 16) *(uint4 *)(z + o) = make_uint4(0, 0, 0, 0);
+            uint8_t *z = base + (__ffs(m) - 1) * seg_bytes;
+            for (uint32_t o = lane * 16; o < seg_bytes; o += 32 * 16) *(uint4 *)(z + o) = make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async();
         __syncwarp();
     }
-    if (lane == 0) {
-        if (valid) mbar_arrive_expect_tx(bar_full, (uint32_t)__popc(valid) * part);
-        else mbar_arrive(bar_full);
-    }
+    if (lane == 0) mbar_arrive_expect_tx(bar_full, (uint32_t)__popc(valid) * seg_bytes);
     __syncwarp();
     if (!tk) return;
-    const int64_t v_off = (int64_t)p.kv_heads * p.tile_bytes;
-    uint8_t *dst = raw + lane * part;
-    if (vbt == bt) {
-        if (p.kv_heads == 1) {
-            bulk_g2s(smem_addr(dst), tk, part, bar_full);
+    const int64_t v_off = (int64_t)p.kv_heads * p.tile_bytes;  // V tile of the same head
+    uint8_t *dst = base + lane * seg_bytes;
+    if (ks == bt) {
+        if (own && p.kv_heads == 1) {
+            bulk_g2s(smem_addr(dst), tk, 2 * part, bar_full);  // K tile + V tile, contiguous
         } else {
-            bulk_g2s(smem_addr(dst), tk, vtile, bar_full);
-            bulk_g2s(smem_addr(dst + vtile), tk + v_off, vtile, bar_full);
+            if (own) bulk_g2s(smem_addr(dst), tk, part, bar_full);
+            bulk_g2s(smem_addr(dst + (own ? part : 0)), tk + v_off, part, bar_full);
         }
-    } else {
-        for (int kv = 0; kv < 2; ++kv) {
-            const uint8_t *sk = tk + kv * v_off;
-            uint8_t *d = dst + kv * vtile;
-            bulk_g2s(smem_addr(d), sk + (int64_t)rib * D, (uint32_t)BN * D, bar_full);
-            bulk_g2s(smem_addr(d + BN * D), sk + (int64_t)bt * D + (int64_t)rib * SCB, (uint32_t)BN * SCB, bar_full);
+    } else {  // rows [rib, rib + 32) of a larger block: qs and scale planes separately
+        for (int kv = own ? 0 : 1; kv < 2; ++kv) {
+            const uint8_t *src = tk + kv * v_off;
+            uint8_t *d = dst + (own && kv ? part : 0);
+            bulk_g2s(smem_addr(d), src + (int64_t)rib * D, (uint32_t)ks * D, bar_full);
+            bulk_g2s(smem_addr(d + ks * D), src + (int64_t)bt * D + (int64_t)rib * SCB, (uint32_t)ks * SCB, bar_full);
         }
     }
 }
 
-// ---- Q8_0 dequantisation of this CTA's half of a raw tile (kDq threads, 2 units of 16 values
-// each). K: rows [32r, 32r + 32), all 256 columns; V: all 64 rows, columns [128r, 128r + 128).
+// ---- Q8_0 dequantisation of this CTA's half of a tile (kDq threads, 2 units of 16 values each)
+// from its raw stage (segments of 2^seg_shift rows, laid out as pair_produce_q8_raw describes).
+// K: this CTA's 32 rows, all 256 columns; V: all 64 rows, columns [128r, 128r + 128).
 // 8 consecutive threads take 8 consecutive rows of one 16-column segment (distinct bank groups for
 // the swizzled int8 loads and the swizzled operand stores). ----
-__device__ __forceinline__ void pair_dequant(const uint8_t *raw, int kv, int rank, uint8_t *sDst, int vbt_shift,
+__device__ __forceinline__ void pair_dequant(const uint8_t *raw, int kv, int rank, uint8_t *sDst, int seg_shift,
                                              int dtid) {
     using C = PairCfg<true>;
     constexpr int D = C::D, SCB = D / 16;
@@ -312,20 +324,21 @@ __device__ __forceinline__ void pair_dequant(const uint8_t *raw, int kv, int ran
     const int rlow = dtid & 7, seg = (dtid >> 3) % segs, rhigh = (dtid >> 3) / segs;
     const int rpass = kDq / segs;  // rows covered per unit step: 16 (K) or 32 (V)
     const int r0 = rhigh * 8 + rlow;
-    const int vbt = 1 << vbt_shift;
-    const uint32_t vtile = (uint32_t)vbt * (D + SCB);
-    const int row_base = kv == 0 ? rank * C::KH_ROWS : 0;
+    const int srows = 1 << seg_shift;
+    const uint32_t part = (uint32_t)srows * (D + SCB);
     const int d0 = (kv == 0 ? 0 : rank * C::VH_COLS) + seg * 16;
     uint4 q[2];
     uint32_t d[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-        const int row = row_base + r0 + i * rpass;
-        const int s = row >> vbt_shift, rib = row & (vbt - 1);
-        const uint8_t *t = raw + s * 2 * vtile + kv * vtile;
+        const int row = r0 + i * rpass;  // K: local row 0-31; V: tile row 0-63
+        const bool own = kv == 0 || (row >> 5) == rank;
+        const int lr = row & 31, s = lr >> seg_shift, rib = lr & (srows - 1);
+        const uint8_t *t = own ? raw + s * 2 * part + kv * part : raw + 2 * C::KH_ROWS * C::RAW_ROWB + s * part;
         q[i] = *(const uint4 *)(t + q8_qs_off(rib, d0, D));
-        d[i] = *(const uint16_t *)(t + vbt * D + rib * SCB + (d0 >> 5) * 2);
+        d[i] = *(const uint16_t *)(t + srows * D + rib * SCB + (d0 >> 5) * 2);
     }
+
     // destination: K half [32 rows x 256] or V half [64 rows x 128] operand tile
     const int dD = kv == 0 ? D : C::VH_COLS;
     const uint32_t off_lo = tile_elem_off(r0, seg * 16, dD, C::W), off_hi = tile_elem_off(r0, seg * 16 + 8, dD, C::W);
@@ -387,8 +400,8 @@ __device__ __forceinline__ bool pair_xsync(uint32_t xbar, int use, volatile int 
 // per warp on rank 0's barrier. ----
 template <bool Q8>
 __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &pl, uint8_t *smem, uint32_t bar0,
-                                             uint32_t p_full_remote0, volatile int *abort, uint32_t tmem, int n,
-                                             int n_qtiles) {
+                                             uint32_t p_full0, volatile int *abort, uint32_t tmem, int n, int n_qtiles,
+                                             const void *omap, int omode) {
     using C = PairCfg<Q8>;
     constexpr int BN = C::BN, D = C::D, DH = D / 2, NS = C::NSTAGE;
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
@@ -413,6 +426,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         const int j = pl.j0 + jj;
         if (!(ok = mbar_wait_cluster(bar(PB_K_EMPTY + jj % NS), stage_parity(jj, NS), abort, kWaitBudget))) break;
         tc_fence_after();
+        if (r == 0 && h == 0 && jj < 50) TRACE(300 + jj);
         const bool suffix = j >= pl.np_tiles;
         const int key0 = (suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN) + h * 32;
         const bool all_vis = suffix ? (suffix_simple && key0 + 32 <= a.suffix_len)
@@ -493,7 +507,8 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(p_full_remote0 + 8u * (uint32_t)sb);
+        if (lane == 0) mbar_arrive_remote(p_full0 + 8u * (uint32_t)sb);
+        if (r == 0 && h == 0 && jj < 50) TRACE(350 + jj);
     }
     if (!ok) pair_fail(a, abort, 3);
     if (ok && n > 0) {
@@ -502,6 +517,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         tc_fence_after();
     }
     // ---- epilogue: row sum over both halves, then this warp's D/2 columns of O ----
+    if (r == 0 && h == 0) TRACE(10);
     xl[h * kBM + r] = l;
     if (ok && !pair_xsync(xbar, uses++, abort)) {
         ok = false;
@@ -524,6 +540,24 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
             wml[0] = have_o ? m_used : -INFINITY;
             wml[1] = have_o ? l_row : 0.0f;
         }
+    }
+    if (omode != OUT_THREADS) {
+        // this warp's columns of its lane quarter -> swizzled boxes -> copy engine
+        const int boxc = f32 ? 32 : 64;
+#pragma unroll 1
+        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
+            uint32_t o32[32];
+            if (have_o) {
+                tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o32[i] = 0u;
+            }
+            stage_o_box<32>(smem, quarter, lane, c0, o32, inv, f32);
+        }
+        store_o_boxes(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem, quarter, h * DH / boxc,
+                      (h + 1) * DH / boxc, boxc, unit);
+        return;
     }
     uint8_t *orow = smem + r * C::OSTR;
 #pragma unroll 1
@@ -573,7 +607,8 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
 }
 
 template <bool Q8>
-__global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(const AttnArgs a, int n_qtiles) {
+__global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
+    attn_pair_kernel(const AttnArgs a, int n_qtiles, const __grid_constant__ CUtensorMap omap, int omode) {
     using C = PairCfg<Q8>;
     constexpr int BN = C::BN, D = C::D, NS = C::NSTAGE;
     extern __shared__ uint8_t smem_raw[];
@@ -589,6 +624,11 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
     const uint32_t bar0 = smem_addr(bars);
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) {
+        trace_init();
+        TRACE(0);
+        TRACE_CLK(20);
+    }
     const PairPlan pl = make_pair_plan(a);
     const uint32_t peer = (uint32_t)(pl.rank ^ 1);
     const uint32_t bar0_rank0 = mapa_shared(bar0, 0);  // rank 0's barrier block (cluster window)
@@ -604,11 +644,11 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
             mbar_init(bar(PB_K_EMPTY + s), 1);
             mbar_init(bar(PB_V_EMPTY + s), 1);
         }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(bar(PB_RAW_FULL + s), 1);
+        for (int s = 0; s < 3; ++s) {
+            mbar_init(bar(PB_RAW_FULL + s), 2);
             mbar_init(bar(PB_RAW_EMPTY + s), kDq / 32);
-            mbar_init(bar(PB_P_FULL + s), 2 * C::SMW);
         }
+        for (int s = 0; s < 2; ++s) mbar_init(bar(PB_P_FULL + s), 2 * C::SMW);
         mbar_init(bar(PB_DONE), 1);
         for (int q = 0; q < 4; ++q) mbar_init(bar(PB_XCH + q), 2);
         *abort = 0;
@@ -671,6 +711,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (threadIdx.x == 0) TRACE(3);
     const int n = pl.j1 - pl.j0;
 
     if (warp == C::MMA_WARP) {
@@ -694,6 +735,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
                     }
                     mma_commit_pair(bar(PB_K_EMPTY + st));
                     mma_commit_pair(bar0_peer + 8u * (uint32_t)(PB_K_EMPTY + st));
+                    if (jj < 50) TRACE(200 + jj);
                     return true;
                 };
                 auto issue_pv = [&](int jj) {
@@ -709,6 +751,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
                                     bd0 + ((uint32_t)kk * 2u * C::V_SBO >> 4), idO, (jj > 0 || kk > 0) ? 1u : 0u);
                     mma_commit_pair(bar(PB_V_EMPTY + st));
                     mma_commit_pair(bar0_peer + 8u * (uint32_t)(PB_V_EMPTY + st));
+                    if (jj < 50) TRACE(250 + jj);
                     return true;
                 };
                 bool ok = issue_s(0);
@@ -724,14 +767,13 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
             // ---- rank 1, bf16: forward "my K/V half landed" to rank 0, in the order its MMAs use
             // them: K(0), then K(j+1) before V(j) ----
             if (n > 0 && lane == 0) {
-                bool ok = true;
                 auto relay = [&](int base_full, int base_peer, int jj) {
                     const int st = jj % NS;
                     if (!mbar_wait(bar(base_full + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
-                    mbar_arrive_cluster(bar0_rank0 + 8u * (uint32_t)(base_peer + st));
+                    mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)(base_peer + st));
                     return true;
                 };
-                ok = relay(PB_K_FULL, PB_K_PEER, 0);
+                bool ok = relay(PB_K_FULL, PB_K_PEER, 0);
                 for (int jj = 0; ok && jj < n; ++jj) {
                     if (jj + 1 < n) ok = relay(PB_K_FULL, PB_K_PEER, jj + 1);
                     if (ok) ok = relay(PB_V_FULL, PB_V_PEER, jj);
@@ -740,73 +782,60 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
             }
         }
         __syncwarp();
-    } else if (warp == C::TMA_WARP) {
+    } else if (warp == C::TMA_WARP || warp == C::TMA_WARP + 1) {
+        // copy-engine feeders, one warp for K and one for V (a bulk-copy issue stalls its warp)
+        const int kv = warp - C::TMA_WARP;
         if constexpr (Q8) {
+            // warp TMA_WARP: this CTA's rows (K and V); TMA_WARP + 1: the peer's rows (V)
+            constexpr int NR = C::NRAW;
+            const int np = min(n, max(0, pl.np_tiles - pl.j0));  // suffix tiles are converted by the dequant warps
             int issued = 0;
-            for (int jj = 0; jj < n; ++jj) {
-                const int j = pl.j0 + jj;
-                if (j >= pl.np_tiles) break;  // suffix tiles are converted by the dequant warps
-                const int r = jj % C::NRAW;
-                if (jj >= C::NRAW &&
-                    !mbar_wait(bar(PB_RAW_EMPTY + r), stage_parity(jj - C::NRAW, C::NRAW), abort, kWaitBudget)) {
+            for (int it = 0; it < np; ++it) {
+                const int r = it % NR;
+                if (it >= NR && !mbar_wait(bar(PB_RAW_EMPTY + r), stage_parity(it - NR, NR), abort, kWaitBudget)) {
                     pair_fail(a, abort, 2);
                     break;
                 }
-                pair_produce_q8_raw(a, pl, (const uint8_t *const *)sPtr, j, sRaw + r * C::RAW_BYTES,
+                if (lane == 0 && it < 50) TRACE((kv ? 150 : 450) + it);
+                pair_produce_q8_raw(a, pl, (const uint8_t *const *)sPtr, pl.j0 + it, 1 - kv, sRaw + r * C::RAW_BYTES,
                                     bar(PB_RAW_FULL + r), lane);
-                issued = jj + 1;
+                issued = it + 1;
             }
             if (lane == 0 && *abort)
-                for (int jj = max(0, issued - C::NRAW); jj < issued; ++jj)
-                    mbar_wait(bar(PB_RAW_FULL + jj % C::NRAW), stage_parity(jj, C::NRAW), abort, kWaitBudget / 4);
+                for (int jj = max(0, issued - NR); jj < issued; ++jj)
+                    mbar_wait(bar(PB_RAW_FULL + jj % NR), stage_parity(jj, NR), abort, kWaitBudget / 4);
         } else {
-            // K(it) and V(it - 1) per step (V is needed one softmax later than K)
-            int k_issued = 0, v_issued = 0;
-            for (int it = 0; it <= n; ++it) {
-                if (it < n) {
-                    const int st = it % NS;
-                    if (it >= NS &&
-                        !mbar_wait_cluster(bar(PB_K_EMPTY + st), stage_parity(it - NS, NS), abort, kWaitBudget)) {
-                        pair_fail(a, abort, 2);
-                        break;
-                    }
-                    pair_produce_bf16(a, pl, (const uint8_t *const *)sPtr, pl.j0 + it, 0, sK + st * C::KH_BYTES,
-                                      bar(PB_K_FULL + st), lane);
-                    k_issued = it + 1;
+            uint8_t *stages = kv ? sV : sK;
+            const int sbytes = kv ? C::VH_BYTES : C::KH_BYTES;
+            const int b_full = kv ? PB_V_FULL : PB_K_FULL, b_empty = kv ? PB_V_EMPTY : PB_K_EMPTY;
+            int issued = 0;
+            for (int it = 0; it < n; ++it) {
+                const int st = it % NS;
+                if (it >= NS && !mbar_wait_cluster(bar(b_empty + st), stage_parity(it - NS, NS), abort, kWaitBudget)) {
+                    pair_fail(a, abort, 2);
+                    break;
                 }
-                if (it >= 1) {
-                    const int v = it - 1, st = v % NS;
-                    if (v >= NS &&
-                        !mbar_wait_cluster(bar(PB_V_EMPTY + st), stage_parity(v - NS, NS), abort, kWaitBudget)) {
-                        pair_fail(a, abort, 2);
-                        break;
-                    }
-                    pair_produce_bf16(a, pl, (const uint8_t *const *)sPtr, pl.j0 + v, 1, sV + st * C::VH_BYTES,
-                                      bar(PB_V_FULL + st), lane);
-                    v_issued = v + 1;
-                }
+                if (lane == 0 && it < 50) TRACE((kv ? 150 : 450) + it);
+                pair_produce_bf16(a, pl, (const uint8_t *const *)sPtr, pl.j0 + it, kv, stages + st * sbytes,
+                                  bar(b_full + st), lane);
+                issued = it + 1;
             }
-            if (lane == 0 && *abort) {
-                for (int jj = max(0, k_issued - NS); jj < k_issued; ++jj)
-                    mbar_wait(bar(PB_K_FULL + jj % NS), stage_parity(jj, NS), abort, kWaitBudget / 4);
-                for (int jj = max(0, v_issued - NS); jj < v_issued; ++jj)
-                    mbar_wait(bar(PB_V_FULL + jj % NS), stage_parity(jj, NS), abort, kWaitBudget / 4);
-            }
+            if (lane == 0 && *abort)
+                for (int jj = max(0, issued - NS); jj < issued; ++jj)
+                    mbar_wait(bar(b_full + jj % NS), stage_parity(jj, NS), abort, kWaitBudget / 4);
         }
     } else if (warp >= C::DQ_WARP0) {
         if constexpr (Q8) {
             const int dtid = threadIdx.x - C::DQ_WARP0 * 32;
-            const int vbt = min(a.pool.block_tokens, BN);
-            const int vbt_shift = 31 - __clz(vbt);
-            // rank 0's dequant warps arrive on its own "full" barriers, rank 1's on rank 0's "peer" ones
-            const uint32_t kfull0 = pl.rank == 0 ? bar(PB_K_FULL) : bar0_rank0 + 8u * PB_K_PEER;
-            const uint32_t vfull0 = pl.rank == 0 ? bar(PB_V_FULL) : bar0_rank0 + 8u * PB_V_PEER;
+            const int bt = a.pool.block_tokens;  // a power of two (checked by the launcher)
+            const int seg_shift = 31 - __clz(min(bt, C::KH_ROWS));
             for (int jj = 0; jj < n; ++jj) {
                 const int j = pl.j0 + jj, st = jj % NS;
                 const bool prefix = j < pl.np_tiles;
-                const uint8_t *raw = sRaw + (jj % C::NRAW) * C::RAW_BYTES;
-                if (prefix &&
-                    !mbar_wait(bar(PB_RAW_FULL + jj % C::NRAW), stage_parity(jj, C::NRAW), abort, kWaitBudget)) {
+                if (dtid == 0 && jj < 50) TRACE(500 + jj);
+                const int rs = jj % C::NRAW;
+                const uint8_t *raw = sRaw + rs * C::RAW_BYTES;
+                if (prefix && !mbar_wait(bar(PB_RAW_FULL + rs), stage_parity(jj, C::NRAW), abort, kWaitBudget)) {
                     pair_fail(a, abort, 5);
                     break;
                 }
@@ -820,23 +849,31 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
                         ok = false;
                         break;
                     }
-                    if (prefix) pair_dequant(raw, kv, pl.rank, dst, vbt_shift, dtid);
+                    if (dtid == 0 && jj < 50) TRACE(550 + 250 * kv + jj);
+                    if (prefix) pair_dequant(raw, kv, pl.rank, dst, seg_shift, dtid);
                     else pair_convert_suffix(a, pl, j, kv, dst, dtid);
                     fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) {
-                        if (prefix && kv == 1) mbar_arrive(bar(PB_RAW_EMPTY + jj % C::NRAW));
-                        mbar_arrive_cluster((kv ? vfull0 : kfull0) + 8u * (uint32_t)st);
+                        if (prefix && kv == 1) mbar_arrive(bar(PB_RAW_EMPTY + rs));
+                        // rank 0: its own "full" barrier; rank 1: rank 0's "peer" barrier
+                        if (pl.rank == 0) mbar_arrive(bar((kv ? PB_V_FULL : PB_K_FULL) + st));
+                        else mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)((kv ? PB_V_PEER : PB_K_PEER) + st));
                     }
                 }
                 if (!ok) {
                     pair_fail(a, abort, 6);
                     break;
                 }
+                if (dtid == 0 && jj < 50) TRACE(100 + jj);
             }
         }
     } else {
-        pair_softmax<Q8>(a, pl, smem, bar0, bar0_rank0 + 8u * PB_P_FULL, abort, tmem, n, n_qtiles);
+        pair_softmax<Q8>(a, pl, smem, bar0, bar0_rank0 + 8u * PB_P_FULL, abort, tmem, n, n_qtiles, &omap, omode);
+    }
+    if (threadIdx.x == 0) {
+        TRACE(11);
+        TRACE_CLK(21);
     }
     __syncwarp();
     tc_fence_before();
@@ -844,9 +881,18 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1) attn_pair_kernel(cons
     cluster_sync();  // rank 0's MMAs are finished; neither CTA releases memory the other still uses
     tc_fence_after();
     if (warp == C::MMA_WARP) tmem_dealloc_pair(tmem, C::TMEM_COLS);
+    if (threadIdx.x == 0) TRACE(12);
+    __syncthreads();
+    trace_flush();
 }
 
 }  // namespace
+
+#ifdef EKV_TRACE
+int pair_debug_set_trace(unsigned long long *buf) {
+    return cudaMemcpyToSymbol(c_trace, &buf, sizeof(buf)) == cudaSuccess ? 0 : -2;
+}
+#endif
 
 // Split count for `pair_units` CTA pairs on `sms` SMs (two per pair).
 int pair_choose_splits(int64_t pair_units, int max_tiles, int sms) {
@@ -898,8 +944,10 @@ int launch_attention_pair(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms) 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = q8 ? cudaLaunchKernelEx(&cfg, attn_pair_kernel<true>, a, n_qtiles)
-                             : cudaLaunchKernelEx(&cfg, attn_pair_kernel<false>, a, n_qtiles);
+    CUtensorMap omap;
+    const int omode = make_out_map(a, 256, (int64_t)a.n_batch * a.pool.kv_heads * n_qtiles, &omap);
+    const cudaError_t e = q8 ? cudaLaunchKernelEx(&cfg, attn_pair_kernel<true>, a, n_qtiles, omap, omode)
+                             : cudaLaunchKernelEx(&cfg, attn_pair_kernel<false>, a, n_qtiles, omap, omode);
     if (e != cudaSuccess) return EKV_ERR_CUDA;
     if (a.n_splits > 1) return launch_merge_splits(a, n_qtiles, s);
     return EKV_OK;

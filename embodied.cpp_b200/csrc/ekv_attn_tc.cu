@@ -50,24 +50,6 @@ namespace {
 
 using namespace sm100;
 
-#ifdef EKV_TRACE
-__device__ unsigned long long *g_trace = nullptr;
-__device__ __forceinline__ void trace_at(int slot) {
-    if (g_trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
-        unsigned long long t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        g_trace[slot] = t;
-    }
-}
-#define TRACE(slot) trace_at(slot)
-__device__ __forceinline__ void trace_clock(int slot) {
-    if (g_trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_trace[slot] = (unsigned long long)clock64();
-}
-#define TRACE_CLK(slot) trace_clock(slot)
-#else
-#define TRACE(slot) ((void)0)
-#define TRACE_CLK(slot) ((void)0)
-#endif
 
 
 
@@ -79,15 +61,17 @@ struct TcCfg {
     static constexpr uint32_t LAYOUT = W == 128 ? 2u : (W == 64 ? 4u : 6u);
     static constexpr uint32_t SBO = (D * 2 / W) * 8 * W;  // bytes between 8-row groups (= 16 * D)
     static constexpr int NSTAGE = Q8 ? 2 : 3;  // K/V operand stages
-    static constexpr int NRAW = Q8 ? 2 : 0;    // raw Q8_0 staging stages
+    // raw Q8_0 staging: separate K and V rings; K is dequantised first, so its stage frees half a
+    // tile earlier and its ring runs one tile deeper
+    static constexpr int NRAW_K = Q8 ? 3 : 0;
+    static constexpr int NRAW_V = Q8 ? 2 : 0;
     static constexpr int KV_BYTES = BN * D * 2;
-    static constexpr int RAW_QS = BN * D;         // int8 of K (or V) for one tile
-    static constexpr int RAW_SC = BN * (D / 16);  // fp16 scales of K (or V): BN rows x D/32 x 2 B
-    static constexpr int RAW_BYTES = 2 * (RAW_QS + RAW_SC);
+    static constexpr int RAW_HALF = BN * (D + D / 16);  // K (or V) of one tile: int8 + fp16 scales
     static constexpr int OFF_K = 0;
     static constexpr int OFF_V = NSTAGE * KV_BYTES;
     static constexpr int OFF_RAW = 2 * NSTAGE * KV_BYTES;
-    static constexpr int OFF_BAR = OFF_RAW + NRAW * RAW_BYTES;
+    static constexpr int OFF_RAW_V = OFF_RAW + NRAW_K * RAW_HALF;
+    static constexpr int OFF_BAR = OFF_RAW_V + NRAW_V * RAW_HALF;
     static constexpr int OFF_XCH = OFF_BAR + 256;  // softmax pair exchange: row maxima [2][2][128], sums [2][128]
     static constexpr int OFF_TBL = OFF_XCH + 6 * kBM * 4;
     // tile base pointers of the split's block-table entries (whatever fits, at most 512)
@@ -101,9 +85,9 @@ struct TcCfg {
     static constexpr bool SPLIT = BN == 64;
     static constexpr int SMW = SPLIT ? 8 : 4;  // softmax warps
     static constexpr int MMA_WARP = SMW;
-    static constexpr int TMA_WARP = SMW + 1;
-    static constexpr int DQ_WARP0 = SMW + 2;
-    static constexpr int THREADS = (SMW + 2) * 32 + (Q8 ? kDq : 0);
+    static constexpr int TMA_WARP = SMW + 1;  // K feeder; TMA_WARP + 1 feeds V
+    static constexpr int DQ_WARP0 = SMW + 3;
+    static constexpr int THREADS = (SMW + 3) * 32 + (Q8 ? kDq : 0);
     static constexpr int TMEM_COLS = 512;
     static constexpr int S_COL = 0;
     static constexpr int O_COL = 2 * BN;
@@ -126,13 +110,15 @@ enum {
     BAR_K_EMPTY = 3,     // [3] K operand stage consumed (S done)
     BAR_V_FULL = 6,      // [3] V operand stage filled
     BAR_V_EMPTY = 9,     // [3] V operand stage consumed (P.V done)
-    BAR_RAW_FULL = 12,   // [2] raw Q8_0 stage landed
-    BAR_RAW_EMPTY = 14,  // [2] raw Q8_0 stage read
-    BAR_P_FULL = 16,     // [2] P(j) in TMEM
-    BAR_DONE = 18,
-    BAR_XCH = 19,        // [4] softmax pair exchange (one per TMEM lane quarter; SPLIT only)
-    BAR_Q_READY = 23,    // Q in TMEM and its shared staging (in the V stages) read
-    N_BARS = 24
+    BAR_RAW_K_FULL = 12,   // [3] raw Q8_0 K stage landed
+    BAR_RAW_K_EMPTY = 15,  // [3] raw Q8_0 K stage read
+    BAR_RAW_V_FULL = 18,   // [2] raw Q8_0 V stage landed
+    BAR_RAW_V_EMPTY = 20,  // [2] raw Q8_0 V stage read
+    BAR_P_FULL = 22,       // [2] P(j) in TMEM
+    BAR_DONE = 24,
+    BAR_XCH = 25,          // [4] softmax pair exchange (one per TMEM lane quarter; SPLIT only)
+    BAR_Q_READY = 29,      // Q in TMEM and its shared staging (in the V stages) read
+    N_BARS = 30
 };
 // One commit per MMA group: "S(j) done" is the completion of K stage j % NS and "P.V(j) done"
 // that of V stage j % NS. A waiter for S(j) or P.V(j - 1) in the softmax cannot be overtaken by a
@@ -346,20 +332,19 @@ __device__ __forceinline__ void produce_bf16_part(const AttnArgs &a, const Plan 
     if (src) bulk_g2s(smem_addr(sDst + dst), src, bytes, bar_full);
 }
 
-// ---- Q8_0 feeder: the raw stage holds, per segment of vbt = min(block_tokens, BN) rows, a K part
-// then a V part, each [qs vbt x D][fp16 scales vbt x D/32] -- exactly the pool's Q8_0 tile, so a
-// whole block whose K and V tiles are adjacent (one KV head) is ONE copy; otherwise one per tile,
-// or one per plane for a partial block. One lane per segment. ----
+// ---- Q8_0 feeder: one raw stage holds the K (kv = 0) or V (kv = 1) part of a tile: per segment of
+// vbt = min(block_tokens, BN) rows, [qs vbt x D][fp16 scales vbt x D/32] -- exactly the pool's
+// Q8_0 tile, so a whole block is ONE copy and a partial block one per plane. One lane per
+// segment. ----
 template <int D>
 __device__ __forceinline__ void produce_q8_raw(const AttnArgs &a, const Plan &pl, const uint8_t *const *sPtr, int j,
-                                               uint8_t *raw, uint32_t bar_full, int lane) {
+                                               int kv, uint8_t *raw, uint32_t bar_full, int lane) {
     using C = TcCfg<D, true>;
     constexpr int BN = C::BN, SCB = D / 16;  // scale bytes per row
     const PoolView &p = a.pool;
     const int bt = p.block_tokens;
     const int vbt = min(bt, BN), n_seg = BN / vbt;
     const uint32_t vtile = (uint32_t)vbt * (D + SCB);
-    const uint32_t part = 2 * vtile;
     const uint8_t *tk = nullptr;
     int rib = 0;
     if (lane < n_seg) {
@@ -372,44 +357,35 @@ __device__ __forceinline__ void produce_q8_raw(const AttnArgs &a, const Plan &pl
     const uint32_t missing = ~valid & segmask;
     if (missing) {
         for (uint32_t m = missing; m; m &= m - 1) {
-            uint8_t *z = raw + (__ffs(m) - 1) * part;
-            for (uint32_t o = lane * 16; o < part; o += 32 * 16) *(uint4 *)(z + o) = make_uint4(0, 0, 0, 0);
+            uint8_t *z = raw + (__ffs(m) - 1) * vtile;
+            for (uint32_t o = lane * 16; o < vtile; o += 32 * 16) *(uint4 *)(z + o) = make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async();
         __syncwarp();
     }
     if (lane == 0) {
-        if (valid) mbar_arrive_expect_tx(bar_full, (uint32_t)__popc(valid) * part);
+        if (valid) mbar_arrive_expect_tx(bar_full, (uint32_t)__popc(valid) * vtile);
         else mbar_arrive(bar_full);
     }
     __syncwarp();
     if (!tk) return;
-    const int64_t v_off = (int64_t)p.kv_heads * p.tile_bytes;  // V tile of the same head
-    uint8_t *dst = raw + lane * part;
+    const uint8_t *src = tk + (int64_t)kv * p.kv_heads * p.tile_bytes;  // K or V tile of this head
+    uint8_t *dst = raw + lane * vtile;
     if (vbt == bt) {
-        if (p.kv_heads == 1) {
-            bulk_g2s(smem_addr(dst), tk, part, bar_full);  // K tile + V tile, contiguous
-        } else {
-            bulk_g2s(smem_addr(dst), tk, vtile, bar_full);
-            bulk_g2s(smem_addr(dst + vtile), tk + v_off, vtile, bar_full);
-        }
+        bulk_g2s(smem_addr(dst), src, vtile, bar_full);
     } else {  // rows [rib, rib + BN) of a larger block: qs and scale planes separately
-        for (int kv = 0; kv < 2; ++kv) {
-            const uint8_t *sk = tk + kv * v_off;
-            uint8_t *d = dst + kv * vtile;
-            bulk_g2s(smem_addr(d), sk + (int64_t)rib * D, (uint32_t)BN * D, bar_full);
-            bulk_g2s(smem_addr(d + BN * D), sk + (int64_t)bt * D + (int64_t)rib * SCB, (uint32_t)BN * SCB, bar_full);
-        }
+        bulk_g2s(smem_addr(dst), src + (int64_t)rib * D, (uint32_t)BN * D, bar_full);
+        bulk_g2s(smem_addr(dst + BN * D), src + (int64_t)bt * D + (int64_t)rib * SCB, (uint32_t)BN * SCB, bar_full);
     }
 }
 
-// raw stage -> the K (kv = 0) or V (kv = 1) f16 operand stage (kDq threads; every raw load before the
+// raw K or V stage -> the matching f16 operand stage (kDq threads; every raw load before the
 // first store). Thread mapping: 8 consecutive threads take 8 consecutive rows of one 16-column
 // segment, so both the swizzled int8 loads and the swizzled operand stores of a thread-phase hit 8
 // distinct bank groups; each thread keeps one segment and one row-in-group, so its operand offsets
 // are one base plus a constant stride per unit.
 template <int D>
-__device__ __forceinline__ void dequant_part(const uint8_t *raw, int kv, uint8_t *sDst, int vbt_shift, int dtid) {
+__device__ __forceinline__ void dequant_part(const uint8_t *raw, uint8_t *sDst, int vbt_shift, int dtid) {
     using C = TcCfg<D, true>;
     constexpr int BN = C::BN, W = C::W, UPR = D / 16, RS = kDq / UPR, PER = BN / RS, SCB = D / 16;
     static_assert(kDq % (8 * UPR) == 0 && BN % RS == 0, "dequant thread mapping");
@@ -423,7 +399,7 @@ __device__ __forceinline__ void dequant_part(const uint8_t *raw, int kv, uint8_t
     for (int i = 0; i < PER; ++i) {
         const int row = r0 + i * RS;
         const int s = row >> vbt_shift, rib = row & (vbt - 1);
-        const uint8_t *t = raw + s * 2 * vtile + kv * vtile;
+        const uint8_t *t = raw + s * vtile;
         q[i] = *(const uint4 *)(t + q8_qs_off(rib, seg * 16, D));
         d[i] = *(const uint16_t *)(t + vbt * D + rib * SCB + (seg >> 1) * 2);
     }
@@ -529,72 +505,6 @@ __device__ __forceinline__ bool pair_sync(uint32_t xbar, int use, volatile int *
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(xbar);
     return mbar_wait(xbar, (uint32_t)use & 1u, abort, kWaitBudget);
-}
-
-// ---- output epilogue through the copy engine ----
-// O rows are staged as 4 KB boxes of 32 rows (one TMEM lane quarter) x 128 bytes (64 bf16 or 32
-// f32 columns), 128-byte swizzled: 16-byte unit u of box row i sits at unit u ^ (i & 7), the layout
-// a CU_TENSOR_MAP_SWIZZLE_128B map reads, so the 8 lanes of a store phase hit 8 distinct bank
-// groups. Box (cb, quarter) is at cb * 4 + quarter. Lane 0 of each warp then stores the warp's
-// boxes with cp.async.bulk.tensor: no cross-warp barrier, and no thread-issued global stores (which
-// drain several times slower than the copy engine's from this kernel).
-enum { OUT_THREADS = 0, OUT_TMA_ROWS = 1, OUT_TMA_WS = 2 };
-constexpr int kOutBox = 4096;
-
-// Stage columns [c0, c0 + EC) of this thread's row (`lane` of lane quarter `quarter`), times inv.
-template <int EC>
-__device__ __forceinline__ void stage_o_box(uint8_t *boxes, int quarter, int lane, int c0, const uint32_t *o, float inv,
-                                            bool f32) {
-    static_assert(EC == 16 || EC == 32, "column chunk");
-    const int sw = lane & 7;
-    if (f32) {
-        uint8_t *row = boxes + ((c0 >> 5) * 4 + quarter) * kOutBox + lane * 128;
-        const int u0 = (c0 & 31) >> 2;
-#pragma unroll
-        for (int i = 0; i < EC / 4; ++i)
-            *(float4 *)(row + (((u0 + i) ^ sw) << 4)) =
-                make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                            __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
-    } else {
-        uint8_t *row = boxes + ((c0 >> 6) * 4 + quarter) * kOutBox + lane * 128;
-        const int u0 = (c0 & 63) >> 3;
-#pragma unroll
-        for (int i = 0; i < EC / 8; ++i) {
-            uint32_t w[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 2 * e]) * inv,
-                                                                __uint_as_float(o[8 * i + 2 * e + 1]) * inv);
-                w[e] = *(const uint32_t *)&b2;
-            }
-            *(uint4 *)(row + (((u0 + i) ^ sw) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-    }
-}
-
-// Whole warp, after staging its boxes [cb0, cb1) of lane quarter `quarter`: lane 0 stores them and
-// waits until the copy engine has read them (the CTA may exit afterwards). OUT_TMA_ROWS maps the
-// output as (head_dim, head in group, KV head, token, batch): box row i of the quarter is query
-// row qrow0 + quarter * 32 + i, and rows past the call's tokens fall outside the map. OUT_TMA_WS
-// maps the workspace as (head_dim, unit * 128 + row).
-__device__ __forceinline__ void store_o_boxes(const AttnArgs &a, const Plan &pl, const void *omap, int omode,
-                                              const uint8_t *boxes, int quarter, int cb0, int cb1, int boxc,
-                                              int64_t unit) {
-    fence_proxy_async();
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0 && quarter * 32 < pl.rows_valid) {
-        const int row0 = pl.qrow0 + quarter * 32;
-        for (int cb = cb0; cb < cb1; ++cb) {
-            const uint32_t src = smem_addr(boxes + (cb * 4 + quarter) * kOutBox);
-            if (omode == OUT_TMA_ROWS)
-                tma_store_5d(omap, src, cb * boxc, row0 % a.group, pl.g, row0 / a.group, pl.b);
-            else
-                tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM) + quarter * 32);
-        }
-        bulk_commit_group();
-        bulk_wait_group_read0();
-    }
-    __syncwarp();
 }
 
 // ---- softmax / epilogue with two warps per TMEM lane quarter (BN = 64): warp w owns query row
@@ -764,7 +674,8 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
             }
             stage_o_box<32>(smem + C::OFF_K, quarter, lane, c0, o32, inv, f32);
         }
-        store_o_boxes(a, pl, omap, omode, smem + C::OFF_K, quarter, h * DH / boxc, (h + 1) * DH / boxc, boxc, unit);
+        store_o_boxes(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem + C::OFF_K, quarter, h * DH / boxc,
+                      (h + 1) * DH / boxc, boxc, unit);
         return;
     }
     uint8_t *orow = (smem + C::OFF_K) + r * C::OSTR;
@@ -823,7 +734,8 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sK = smem + C::OFF_K;
     uint8_t *sV = smem + C::OFF_V;
-    uint8_t *sRaw = smem + C::OFF_RAW;
+    uint8_t *sRawK = smem + C::OFF_RAW;
+    uint8_t *sRawV = smem + C::OFF_RAW_V;
     uint64_t *bars = (uint64_t *)(smem + C::OFF_BAR);
     uint32_t *tmem_holder = (uint32_t *)(bars + N_BARS);
     volatile int *abort = (volatile int *)(bars + N_BARS + 1);
@@ -833,6 +745,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     if (threadIdx.x == 0) {
+        trace_init();
         TRACE(0);
         TRACE_CLK(20);
     }
@@ -847,9 +760,13 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
             mbar_init(bar(BAR_V_FULL + s), Q8 ? kDq / 32 : 1);
             mbar_init(bar(BAR_V_EMPTY + s), 1);
         }
+        for (int s = 0; s < 3; ++s) {
+            mbar_init(bar(BAR_RAW_K_FULL + s), 1);
+            mbar_init(bar(BAR_RAW_K_EMPTY + s), kDq / 32);
+        }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(bar(BAR_RAW_FULL + s), 1);
-            mbar_init(bar(BAR_RAW_EMPTY + s), kDq / 32);
+            mbar_init(bar(BAR_RAW_V_FULL + s), 1);
+            mbar_init(bar(BAR_RAW_V_EMPTY + s), kDq / 32);
             mbar_init(bar(BAR_P_FULL + s), C::SMW);
         }
         mbar_init(bar(BAR_DONE), 1);
@@ -945,67 +862,58 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
             mbar_wait(bar(BAR_DONE), 0, abort, kWaitBudget);
         }
         __syncwarp();
-    } else if (warp == C::TMA_WARP) {
-        // copy-engine feeder
+    } else if (warp == C::TMA_WARP || warp == C::TMA_WARP + 1) {
+        // copy-engine feeders, one warp for K and one for V: a bulk-copy issue stalls its warp for a
+        // few hundred cycles, so the two rings are fed in parallel
+        const int kv = warp - C::TMA_WARP;
         if constexpr (Q8) {
+            // raw prefix tiles (suffix tiles are converted by the dequant warps); the K ring is one
+            // stage deeper since K is dequantised first
+            const int nr = kv ? C::NRAW_V : C::NRAW_K;
+            uint8_t *ring = kv ? sRawV : sRawK;
+            const int b_full = kv ? BAR_RAW_V_FULL : BAR_RAW_K_FULL, b_empty = kv ? BAR_RAW_V_EMPTY : BAR_RAW_K_EMPTY;
+            const int np = min(n, max(0, pl.np_tiles - pl.j0));
             int issued = 0;
-            for (int jj = 0; jj < n; ++jj) {
-                const int j = pl.j0 + jj;
-                if (j >= pl.np_tiles) break;  // suffix tiles are converted by the dequant warps
-                const int r = jj % C::NRAW;
-                if (jj >= C::NRAW &&
-                    !mbar_wait(bar(BAR_RAW_EMPTY + r), ((jj - C::NRAW) / C::NRAW) & 1, abort, kWaitBudget)) {
+            for (int it = 0; it < np; ++it) {
+                const int r = it % nr;
+                if (it >= nr && !mbar_wait(bar(b_empty + r), ((it - nr) / nr) & 1, abort, kWaitBudget)) {
                     fail_timeout(a, abort, 2);
                     break;
                 }
-                if (lane == 0 && jj < 50) TRACE(450 + jj);
-                produce_q8_raw<D>(a, pl, (const uint8_t *const *)sPtr, j, sRaw + r * C::RAW_BYTES, bar(BAR_RAW_FULL + r),
-                                  lane);
-                issued = jj + 1;
-                if (lane == 0 && jj < 50) TRACE(150 + jj);
+                if (lane == 0 && it < 50) TRACE((kv ? 150 : 450) + it);
+                produce_q8_raw<D>(a, pl, (const uint8_t *const *)sPtr, pl.j0 + it, kv, ring + r * C::RAW_HALF,
+                                  bar(b_full + r), lane);
+                issued = it + 1;
             }
             // Do not leave the CTA with bulk copies still writing shared memory.
             if (lane == 0 && *abort)
-                for (int jj = max(0, issued - C::NRAW); jj < issued; ++jj)
-                    mbar_wait(bar(BAR_RAW_FULL + jj % C::NRAW), (jj / C::NRAW) & 1, abort, kWaitBudget / 4);
+                for (int jj = max(0, issued - nr); jj < issued; ++jj)
+                    mbar_wait(bar(b_full + jj % nr), (jj / nr) & 1, abort, kWaitBudget / 4);
         } else {
-            // K(it) and V(it - 1) per step: V is needed one softmax later than K
-            int k_issued = 0, v_issued = 0;
-            for (int it = 0; it <= n; ++it) {
-                if (it < n) {
-                    const int st = it % NS;
-                    if (it >= NS && !mbar_wait(bar(BAR_K_EMPTY + st), ((it - NS) / NS) & 1, abort, kWaitBudget)) {
-                        fail_timeout(a, abort, 2);
-                        break;
-                    }
-                    if (lane == 0 && it < 50) TRACE(450 + it);
-                    produce_bf16_part<D>(a, pl, (const uint8_t *const *)sPtr, pl.j0 + it, 0, sK + st * C::KV_BYTES,
-                                         bar(BAR_K_FULL + st), lane);
-                    k_issued = it + 1;
+            // K stage it once S(it - NS) is done; V stage it once P.V(it - NS) is done (and, for the
+            // first V, once Q's staging in the V stages has been read)
+            uint8_t *stages = kv ? sV : sK;
+            const int b_full = kv ? BAR_V_FULL : BAR_K_FULL, b_empty = kv ? BAR_V_EMPTY : BAR_K_EMPTY;
+            int issued = 0;
+            for (int it = 0; it < n; ++it) {
+                const int st = it % NS;
+                if (kv && it == 0 && !mbar_wait(bar(BAR_Q_READY), 0, abort, kWaitBudget)) {
+                    fail_timeout(a, abort, 2);
+                    break;
                 }
-                if (it >= 1) {
-                    const int v = it - 1, st = v % NS;
-                    if (v == 0 && !mbar_wait(bar(BAR_Q_READY), 0, abort, kWaitBudget)) {  // Q staging read
-                        fail_timeout(a, abort, 2);
-                        break;
-                    }
-                    if (v >= NS && !mbar_wait(bar(BAR_V_EMPTY + st), ((v - NS) / NS) & 1, abort, kWaitBudget)) {
-                        fail_timeout(a, abort, 2);
-                        break;
-                    }
-                    produce_bf16_part<D>(a, pl, (const uint8_t *const *)sPtr, pl.j0 + v, 1, sV + st * C::KV_BYTES,
-                                         bar(BAR_V_FULL + st), lane);
-                    v_issued = v + 1;
-                    if (lane == 0 && v < 50) TRACE(150 + v);
+                if (it >= NS && !mbar_wait(bar(b_empty + st), ((it - NS) / NS) & 1, abort, kWaitBudget)) {
+                    fail_timeout(a, abort, 2);
+                    break;
                 }
+                if (lane == 0 && it < 50) TRACE((kv ? 150 : 450) + it);
+                produce_bf16_part<D>(a, pl, (const uint8_t *const *)sPtr, pl.j0 + it, kv, stages + st * C::KV_BYTES,
+                                     bar(b_full + st), lane);
+                issued = it + 1;
             }
             // Do not leave the CTA with bulk copies still writing shared memory.
-            if (lane == 0 && *abort) {
-                for (int jj = max(0, k_issued - NS); jj < k_issued; ++jj)
-                    mbar_wait(bar(BAR_K_FULL + jj % NS), (jj / NS) & 1, abort, kWaitBudget / 4);
-                for (int jj = max(0, v_issued - NS); jj < v_issued; ++jj)
-                    mbar_wait(bar(BAR_V_FULL + jj % NS), (jj / NS) & 1, abort, kWaitBudget / 4);
-            }
+            if (lane == 0 && *abort)
+                for (int jj = max(0, issued - NS); jj < issued; ++jj)
+                    mbar_wait(bar(b_full + jj % NS), (jj / NS) & 1, abort, kWaitBudget / 4);
         }
     } else if (warp >= C::DQ_WARP0) {
         if constexpr (Q8) {
@@ -1015,17 +923,19 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
             for (int jj = 0; jj < n; ++jj) {
                 const int j = pl.j0 + jj, st = jj % NS;
                 const bool prefix = j < pl.np_tiles;
-                const uint8_t *raw = sRaw + (jj % C::NRAW) * C::RAW_BYTES;
-                if (prefix && !mbar_wait(bar(BAR_RAW_FULL + jj % C::NRAW), (jj / C::NRAW) & 1, abort, kWaitBudget)) {
-                    fail_timeout(a, abort, 5);
-                    break;
-                }
                 if (dtid == 0 && jj < 50) TRACE(500 + jj);
                 bool ok = true;
 #pragma unroll 1
                 for (int kv = 0; kv < 2; ++kv) {
+                    const int nr = kv ? C::NRAW_V : C::NRAW_K, rs = jj % nr;
+                    const uint8_t *raw = (kv ? sRawV : sRawK) + rs * C::RAW_HALF;
+                    const int b_raw = kv ? BAR_RAW_V_FULL : BAR_RAW_K_FULL;
                     const int b_empty = kv ? BAR_V_EMPTY : BAR_K_EMPTY, b_full = kv ? BAR_V_FULL : BAR_K_FULL;
                     uint8_t *dst = (kv ? sV : sK) + st * C::KV_BYTES;
+                    if (prefix && !mbar_wait(bar(b_raw + rs), (jj / nr) & 1, abort, kWaitBudget)) {
+                        ok = false;
+                        break;
+                    }
                     if (kv == 1 && jj == 0 && !mbar_wait(bar(BAR_Q_READY), 0, abort, kWaitBudget)) {  // Q staging read
                         ok = false;
                         break;
@@ -1035,12 +945,12 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
                         break;
                     }
                     if (dtid == 0 && jj < 50) TRACE(550 + 250 * kv + jj);
-                    if (prefix) dequant_part<D>(raw, kv, dst, vbt_shift, dtid);
+                    if (prefix) dequant_part<D>(raw, dst, vbt_shift, dtid);
                     else convert_suffix_part<D>(a, pl, j, kv, dst, dtid);
                     fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) {
-                        if (prefix && kv == 1) mbar_arrive(bar(BAR_RAW_EMPTY + jj % C::NRAW));
+                        if (prefix) mbar_arrive(bar((kv ? BAR_RAW_V_EMPTY : BAR_RAW_K_EMPTY) + rs));
                         mbar_arrive(bar(b_full + st));
                     }
                 }
@@ -1215,7 +1125,8 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
                 stage_o_box<EC>(smem + C::OFF_K, warp, lane, c0, rr, inv, f32);
             }
             const int boxc = f32 ? 32 : 64;
-            store_o_boxes(a, pl, &omap, omode, smem + C::OFF_K, warp, 0, (D + boxc - 1) / boxc, boxc, unit);
+            store_o_boxes(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, &omap, omode, smem + C::OFF_K, warp, 0,
+                          (D + boxc - 1) / boxc, boxc, unit);
         } else if (a.n_splits > 1) {
             const int64_t unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
             float *wo = a.ws_o + (unit * kBM + r) * D;
@@ -1303,6 +1214,8 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
     tc_fence_after();
     if (warp == C::MMA_WARP) tmem_dealloc(tmem, C::TMEM_COLS);
     if (threadIdx.x == 0) TRACE(12);
+    __syncthreads();
+    trace_flush();
 }
 
 // Combine the per-split partial outputs: O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
@@ -1379,58 +1292,6 @@ int sm_count() {
 
 int choose_splits(int64_t units, int max_tiles) { return choose_split_count(units, max_tiles, sm_count()); }
 
-// cuTensorMapEncodeTiled from the driver the runtime loaded (no link-time libcuda dependency).
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
-        return (PFN_cuTensorMapEncodeTiled_v12000)p;
-    }();
-    return fn;
-}
-
-// The epilogue's store route for this call (OUT_*), and the tensor map it stores through.
-// With key splits: the f32 workspace as (head_dim, unit * 128 + row), 32 x 32 boxes. Otherwise the
-// output [B, Tq, Hq, D] as (head_dim, head in group, KV head, token, batch) with boxes of 32 query
-// rows: min(group, 32) heads x max(1, 32 / group) tokens, which needs a group dividing 128 (then a
-// quarter's rows never straddle the end of the call's tokens unless the map clips them). Other
-// shapes keep the thread-store epilogue.
-int make_out_map(const AttnArgs &a, int D, int64_t units, CUtensorMap *map) {
-    std::memset(map, 0, sizeof(*map));
-    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-    if (!enc) return OUT_THREADS;
-    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    if (a.n_splits > 1) {
-        const int64_t rows = units * a.n_splits * kBM;
-        if (D % 32 || rows > INT_MAX || ((uintptr_t)a.ws_o & 15)) return OUT_THREADS;
-        const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-        const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
-        const cuuint32_t box[2] = {32, 32};
-        return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.ws_o, dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
-                   ? OUT_TMA_WS
-                   : OUT_THREADS;
-    }
-    const bool f32 = a.out_dtype == EKV_DTYPE_F32;
-    const int es = f32 ? 4 : 2, boxc = f32 ? 32 : 64;
-    if (D % boxc || a.group <= 0 || kBM % a.group || ((uintptr_t)a.out & 15)) return OUT_THREADS;
-    const cuuint64_t dims[5] = {(cuuint64_t)D, (cuuint64_t)a.group, (cuuint64_t)a.pool.kv_heads,
-                                (cuuint64_t)a.q_tokens, (cuuint64_t)a.n_batch};
-    const cuuint64_t strides[4] = {(cuuint64_t)D * es, (cuuint64_t)a.group * D * es, (cuuint64_t)a.q_heads * D * es,
-                                   (cuuint64_t)a.q_tokens * a.q_heads * D * es};
-    const cuuint32_t box[5] = {(cuuint32_t)boxc, (cuuint32_t)std::min(a.group, 32), 1,
-                               (cuuint32_t)std::max(1, 32 / a.group), 1};
-    return enc(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, a.out, dims, strides,
-               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
-               ? OUT_TMA_ROWS
-               : OUT_THREADS;
-}
-
 template <int D, bool Q8>
 int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
     using C = TcCfg<D, Q8>;
@@ -1491,7 +1352,8 @@ int dispatch(const AttnArgs &a, cudaStream_t s, size_t ws) {
 #ifdef EKV_TRACE
 }  // namespace ekv
 extern "C" int ekv_debug_set_trace(unsigned long long *buf) {
-    return cudaMemcpyToSymbol(ekv::g_trace, &buf, sizeof(buf)) == cudaSuccess ? 0 : -2;
+    if (cudaMemcpyToSymbol(ekv::c_trace, &buf, sizeof(buf)) != cudaSuccess) return -2;
+    return ekv::pair_debug_set_trace(buf);
 }
 namespace ekv {
 #endif

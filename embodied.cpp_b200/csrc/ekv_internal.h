@@ -63,5 +63,8 @@ int launch_attention_pair(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms);
 int pair_choose_splits(int64_t pair_units, int max_tiles, int sms);
 // combine key-split partial outputs (head_dim of the pool) into a.out
 int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s);
+#ifdef EKV_TRACE
+int pair_debug_set_trace(unsigned long long *buf);
+#endif
 
 }  // namespace ekv

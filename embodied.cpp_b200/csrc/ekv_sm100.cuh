@@ -249,6 +249,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Arrive (release at CTA scope) on an mbarrier of another CTA of the cluster, as CUTLASS's cluster
+// barriers do. Used where the signalled data is read on the arriving CTA's own SM -- its shared
+// memory or tensor memory, by the CTA pair's tensor core -- and its writes completed before the
+// arrive (tcgen05.wait::st, or fence.proxy.async). A cluster-scope release drains the SM's memory
+// traffic first, which took 0.7-0.9 us per arrive inside the attention kernel.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // Phase test with cluster-scope acquire (the barrier receives arrivals from the peer CTA).
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
     uint32_t ok;
