@@ -316,8 +316,13 @@ __device__ __forceinline__ void pair_produce_q8_raw(const AttnArgs &a, const Pai
 // K: this CTA's 32 rows, all 256 columns; V: all 64 rows, columns [128r, 128r + 128).
 // 8 consecutive threads take 8 consecutive rows of one 16-column segment (distinct bank groups for
 // the swizzled int8 loads and the swizzled operand stores). ----
-__device__ __forceinline__ void pair_dequant(const uint8_t *raw, int kv, int rank, uint8_t *sDst, int seg_shift,
-                                             int dtid) {
+struct PairDqUnits {
+    uint4 q[2];
+    uint32_t d[2];
+};
+
+// This thread's two int8 units (and their scales) of part kv of a raw stage.
+__device__ __forceinline__ PairDqUnits pair_dq_load(const uint8_t *raw, int kv, int rank, int seg_shift, int dtid) {
     using C = PairCfg<true>;
     constexpr int D = C::D, SCB = D / 16;
     const int segs = kv == 0 ? D / 16 : C::VH_COLS / 16;  // 16 or 8 segments per row
@@ -327,26 +332,34 @@ __device__ __forceinline__ void pair_dequant(const uint8_t *raw, int kv, int ran
     const int srows = 1 << seg_shift;
     const uint32_t part = (uint32_t)srows * (D + SCB);
     const int d0 = (kv == 0 ? 0 : rank * C::VH_COLS) + seg * 16;
-    uint4 q[2];
-    uint32_t d[2];
+    PairDqUnits u;
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         const int row = r0 + i * rpass;  // K: local row 0-31; V: tile row 0-63
         const bool own = kv == 0 || (row >> 5) == rank;
         const int lr = row & 31, s = lr >> seg_shift, rib = lr & (srows - 1);
         const uint8_t *t = own ? raw + s * 2 * part + kv * part : raw + 2 * C::KH_ROWS * C::RAW_ROWB + s * part;
-        q[i] = *(const uint4 *)(t + q8_qs_off(rib, d0, D));
-        d[i] = *(const uint16_t *)(t + srows * D + rib * SCB + (d0 >> 5) * 2);
+        u.q[i] = *(const uint4 *)(t + q8_qs_off(rib, d0, D));
+        u.d[i] = *(const uint16_t *)(t + srows * D + rib * SCB + (d0 >> 5) * 2);
     }
+    return u;
+}
 
-    // destination: K half [32 rows x 256] or V half [64 rows x 128] operand tile
+// Dequantise the units into the K half [32 rows x 256] or V half [64 rows x 128] operand tile.
+__device__ __forceinline__ void pair_dq_store(const PairDqUnits &u, int kv, uint8_t *sDst, int dtid) {
+    using C = PairCfg<true>;
+    constexpr int D = C::D;
+    const int segs = kv == 0 ? D / 16 : C::VH_COLS / 16;
+    const int rlow = dtid & 7, seg = (dtid >> 3) % segs, rhigh = (dtid >> 3) / segs;
+    const int rpass = kDq / segs;
+    const int r0 = rhigh * 8 + rlow;
     const int dD = kv == 0 ? D : C::VH_COLS;
     const uint32_t off_lo = tile_elem_off(r0, seg * 16, dD, C::W), off_hi = tile_elem_off(r0, seg * 16 + 8, dD, C::W);
     const uint32_t step = (uint32_t)(rpass / 8) * (kv == 0 ? C::K_SBO : C::V_SBO);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         uint4 lo, hi;
-        dequant16(q[i], d[i], lo, hi);
+        dequant16(u.q[i], u.d[i], lo, hi);
         *(uint4 *)(sDst + off_lo + i * step) = lo;
         *(uint4 *)(sDst + off_hi + i * step) = hi;
     }
@@ -424,7 +437,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
     for (int jj = 0; jj < n; ++jj) {
         const int sb = jj & 1;
         const int j = pl.j0 + jj;
-        if (!(ok = mbar_wait_cluster(bar(PB_K_EMPTY + jj % NS), stage_parity(jj, NS), abort, kWaitBudget))) break;
+        if (!(ok = mbar_wait(bar(PB_K_EMPTY + jj % NS), stage_parity(jj, NS), abort, kWaitBudget))) break;
         tc_fence_after();
         if (r == 0 && h == 0 && jj < 50) TRACE(300 + jj);
         const bool suffix = j >= pl.np_tiles;
@@ -465,7 +478,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
                 }
             }
             if (__any_sync(0xffffffffu, rescale)) {
-                if (!(ok = mbar_wait_cluster(bar(PB_V_EMPTY + (jj - 1) % NS), stage_parity(jj - 1, NS), abort,
+                if (!(ok = mbar_wait(bar(PB_V_EMPTY + (jj - 1) % NS), stage_parity(jj - 1, NS), abort,
                                              kWaitBudget)))
                     break;
                 tc_fence_after();
@@ -508,11 +521,12 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(p_full0 + 8u * (uint32_t)sb);
+        if (lane == 0 && jj == 7) TRACE(1016 + warp);
         if (r == 0 && h == 0 && jj < 50) TRACE(350 + jj);
     }
     if (!ok) pair_fail(a, abort, 3);
     if (ok && n > 0) {
-        ok = mbar_wait_cluster(bar(PB_V_EMPTY + (n - 1) % NS), stage_parity(n - 1, NS), abort, kWaitBudget);
+        ok = mbar_wait(bar(PB_V_EMPTY + (n - 1) % NS), stage_parity(n - 1, NS), abort, kWaitBudget);
         if (!ok) pair_fail(a, abort, 4);
         tc_fence_after();
     }
@@ -724,8 +738,9 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 auto issue_s = [&](int jj) {
                     const int st = jj % NS, sb = jj & 1;
                     if (!mbar_wait(bar(PB_K_FULL + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
-                    if (!mbar_wait_cluster(bar(PB_K_PEER + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
+                    if (!mbar_wait(bar(PB_K_PEER + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
                     tc_fence_after();
+                    if (jj < 50) TRACE(850 + jj);
                     const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)(sb * BN);
                     const uint64_t bd0 = sdesc(k_addr + st * C::KH_BYTES, 16, C::K_SBO, C::LAYOUT);
 #pragma unroll
@@ -740,10 +755,11 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 };
                 auto issue_pv = [&](int jj) {
                     const int st = jj % NS, sb = jj & 1;
-                    if (!mbar_wait_cluster(bar(PB_P_FULL + sb), (uint32_t)(jj >> 1) & 1u, abort, kWaitBudget)) return false;
+                    if (!mbar_wait(bar(PB_P_FULL + sb), (uint32_t)(jj >> 1) & 1u, abort, kWaitBudget)) return false;
                     if (!mbar_wait(bar(PB_V_FULL + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
-                    if (!mbar_wait_cluster(bar(PB_V_PEER + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
+                    if (!mbar_wait(bar(PB_V_PEER + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
                     tc_fence_after();
+                    if (jj < 50) TRACE(900 + jj);
                     const uint64_t bd0 = sdesc(v_addr + st * C::VH_BYTES, C::V_LBO, C::V_SBO, C::LAYOUT);
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; ++kk)
@@ -811,7 +827,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             int issued = 0;
             for (int it = 0; it < n; ++it) {
                 const int st = it % NS;
-                if (it >= NS && !mbar_wait_cluster(bar(b_empty + st), stage_parity(it - NS, NS), abort, kWaitBudget)) {
+                if (it >= NS && !mbar_wait(bar(b_empty + st), stage_parity(it - NS, NS), abort, kWaitBudget)) {
                     pair_fail(a, abort, 2);
                     break;
                 }
@@ -835,23 +851,17 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 if (dtid == 0 && jj < 50) TRACE(500 + jj);
                 const int rs = jj % C::NRAW;
                 const uint8_t *raw = sRaw + rs * C::RAW_BYTES;
-                if (prefix && !mbar_wait(bar(PB_RAW_FULL + rs), stage_parity(jj, C::NRAW), abort, kWaitBudget)) {
-                    pair_fail(a, abort, 5);
+                uint8_t *kdst = sK + st * C::KH_BYTES, *vdst = sV + st * C::VH_BYTES;
+                // both operand stages free (S(j - NS) and P.V(j - NS) done), raw landed
+                bool ok = jj < NS || (mbar_wait(bar(PB_K_EMPTY + st), stage_parity(jj - NS, NS), abort, kWaitBudget) &&
+                                      mbar_wait(bar(PB_V_EMPTY + st), stage_parity(jj - NS, NS), abort, kWaitBudget));
+                if (ok && prefix) ok = mbar_wait(bar(PB_RAW_FULL + rs), stage_parity(jj, C::NRAW), abort, kWaitBudget);
+                if (!ok) {
+                    pair_fail(a, abort, 6);
                     break;
                 }
-                bool ok = true;
-#pragma unroll 1
-                for (int kv = 0; kv < 2; ++kv) {
-                    const int b_empty = kv ? PB_V_EMPTY : PB_K_EMPTY;
-                    uint8_t *dst = kv ? sV + st * C::VH_BYTES : sK + st * C::KH_BYTES;
-                    if (jj >= NS &&
-                        !mbar_wait_cluster(bar(b_empty + st), stage_parity(jj - NS, NS), abort, kWaitBudget)) {
-                        ok = false;
-                        break;
-                    }
-                    if (dtid == 0 && jj < 50) TRACE(550 + 250 * kv + jj);
-                    if (prefix) pair_dequant(raw, kv, pl.rank, dst, seg_shift, dtid);
-                    else pair_convert_suffix(a, pl, j, kv, dst, dtid);
+                if (dtid == 0 && jj < 50) TRACE(550 + jj);
+                auto publish = [&](int kv) {
                     fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) {
@@ -860,10 +870,23 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                         if (pl.rank == 0) mbar_arrive(bar((kv ? PB_V_FULL : PB_K_FULL) + st));
                         else mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)((kv ? PB_V_PEER : PB_K_PEER) + st));
                     }
-                }
-                if (!ok) {
-                    pair_fail(a, abort, 6);
-                    break;
+                };
+                if (prefix) {
+                    // every raw load of both parts in flight before the first conversion
+                    const PairDqUnits uk = pair_dq_load(raw, 0, pl.rank, seg_shift, dtid);
+                    const PairDqUnits uv = pair_dq_load(raw, 1, pl.rank, seg_shift, dtid);
+                    pair_dq_store(uk, 0, kdst, dtid);
+                    publish(0);
+                    if (dtid == 0 && jj < 50) TRACE(800 + jj);
+                    if (lane == 0 && jj == 7) TRACE(1000 + (dtid >> 5));
+                    pair_dq_store(uv, 1, vdst, dtid);
+                    publish(1);
+                    if (lane == 0 && jj == 7) TRACE(1008 + (dtid >> 5));
+                } else {
+                    pair_convert_suffix(a, pl, j, 0, kdst, dtid);
+                    publish(0);
+                    pair_convert_suffix(a, pl, j, 1, vdst, dtid);
+                    publish(1);
                 }
                 if (dtid == 0 && jj < 50) TRACE(100 + jj);
             }
