@@ -79,20 +79,22 @@ struct PairCfg {
     static_assert((D / 32) * 4 * kOutBox <= OFF_BAR, "epilogue boxes (f32) fit below the barriers");
 };
 
-// Rank 1's softmax and dequantisation warps arrive directly on rank 0's barriers (P_FULL, K_PEER,
-// V_PEER); for bf16, rank 1's relay thread forwards its copies' completion to K_PEER / V_PEER. All
-// arrivals release at CTA scope (mbar_arrive_remote).
+// Each MMA group waits on exactly one barrier: a wait in the issuing thread costs about 220 cycles
+// of idle tensor pipe (the issue queue is one MMA deep). S(j) waits K_FULL(j) (both CTAs' K halves);
+// P.V(j) waits V_FULL(j), which also counts the P(j) arrivals of both CTAs' softmax warps. Rank 1's
+// softmax and dequantisation warps arrive directly on rank 0's barriers; for bf16, rank 1's relay
+// thread forwards its copies' completion. All arrivals release at CTA scope (mbar_arrive_remote).
 enum {
-    PB_K_FULL = 0,       // [6] this CTA's K half landed / dequantised
-    PB_K_PEER = 6,       // [6] rank 1's K half ready (rank 0 only)
+    PB_K_FULL = 0,       // [6] K half ready: on rank 0 both CTAs' halves (rank 1 arrives remotely)
+                         // 6-11 unused
     PB_K_EMPTY = 12,     // [6] S(j) done (committed to both CTAs): K stage free, S(j) readable
-    PB_V_FULL = 18,      // [6]
-    PB_V_PEER = 24,      // [6]
+    PB_V_FULL = 18,      // [6] V half ready; on rank 0 also P(j) written by both CTAs' softmax warps
+                         // 24-29 unused
     PB_V_EMPTY = 30,     // [6] P.V(j) done (both CTAs): V stage free, P(j) consumed, O updated
     PB_RAW_FULL = 36,    // [3] raw Q8_0 stage landed (both feeders' copies)
     PB_RAW_EMPTY = 39,   // [3] raw Q8_0 stage read by the dequant warps
                          // 42-45 unused
-    PB_P_FULL = 46,      // [2] P(j) written by the softmax warps of both CTAs (rank 0 only)
+                         // 46-47 unused
     PB_DONE = 48,
     PB_XCH = 49,         // [4] softmax pair exchange
     PB_N = 53
@@ -413,7 +415,7 @@ __device__ __forceinline__ bool pair_xsync(uint32_t xbar, int use, volatile int 
 // per warp on rank 0's barrier. ----
 template <bool Q8>
 __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &pl, uint8_t *smem, uint32_t bar0,
-                                             uint32_t p_full0, volatile int *abort, uint32_t tmem, int n, int n_qtiles,
+                                             uint32_t v_full0, volatile int *abort, uint32_t tmem, int n, int n_qtiles,
                                              const void *omap, int omode) {
     using C = PairCfg<Q8>;
     constexpr int BN = C::BN, D = C::D, DH = D / 2, NS = C::NSTAGE;
@@ -520,7 +522,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_remote(p_full0 + 8u * (uint32_t)sb);
+        if (lane == 0) mbar_arrive_remote(v_full0 + 8u * (uint32_t)(jj % NS));
         if (lane == 0 && jj == 7) TRACE(1016 + warp);
         if (r == 0 && h == 0 && jj < 50) TRACE(350 + jj);
     }
@@ -650,11 +652,12 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
     if (threadIdx.x == 0 && !pl.sk.ok) report_error(a.pool.status, DEV_ERR_BAD_SEQ, pl.b, a.seq_ids[pl.b], 3);
 
     if (threadIdx.x == 0) {
+        // producers per CTA: the dequant warps (Q8_0) or the feeder's byte-counted arrival (bf16);
+        // rank 0's barriers also count rank 1's
+        const uint32_t n_full = (Q8 ? kDq / 32 : 1) * (pl.rank == 0 ? 2 : 1);
         for (int s = 0; s < NS; ++s) {
-            mbar_init(bar(PB_K_FULL + s), Q8 ? kDq / 32 : 1);
-            mbar_init(bar(PB_V_FULL + s), Q8 ? kDq / 32 : 1);
-            mbar_init(bar(PB_K_PEER + s), Q8 ? kDq / 32 : 1);
-            mbar_init(bar(PB_V_PEER + s), Q8 ? kDq / 32 : 1);
+            mbar_init(bar(PB_K_FULL + s), n_full);
+            mbar_init(bar(PB_V_FULL + s), n_full + (pl.rank == 0 ? 2 * C::SMW : 0));
             mbar_init(bar(PB_K_EMPTY + s), 1);
             mbar_init(bar(PB_V_EMPTY + s), 1);
         }
@@ -662,7 +665,6 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             mbar_init(bar(PB_RAW_FULL + s), 2);
             mbar_init(bar(PB_RAW_EMPTY + s), kDq / 32);
         }
-        for (int s = 0; s < 2; ++s) mbar_init(bar(PB_P_FULL + s), 2 * C::SMW);
         mbar_init(bar(PB_DONE), 1);
         for (int q = 0; q < 4; ++q) mbar_init(bar(PB_XCH + q), 2);
         *abort = 0;
@@ -738,16 +740,22 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 auto issue_s = [&](int jj) {
                     const int st = jj % NS, sb = jj & 1;
                     if (!mbar_wait(bar(PB_K_FULL + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
-                    if (!mbar_wait(bar(PB_K_PEER + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
                     tc_fence_after();
                     if (jj < 50) TRACE(850 + jj);
                     const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)(sb * BN);
                     const uint64_t bd0 = sdesc(k_addr + st * C::KH_BYTES, 16, C::K_SBO, C::LAYOUT);
+                    // K step kk: A columns Q_COL + 8kk; B = 32-byte step kk % 4 of swizzle chunk kk / 4
+                    uint32_t av[D / 16];
+                    uint64_t bv[D / 16];
 #pragma unroll
                     for (int kk = 0; kk < D / 16; ++kk) {
-                        const uint32_t off = (uint32_t)(kk / 4) * (8 * C::W) + (uint32_t)(kk % 4) * 32u;
-                        mma_ts_pair(d_tmem, tmem + C::Q_COL + (uint32_t)(kk * 8), bd0 + (off >> 4), idS, kk > 0 ? 1u : 0u);
+                        av[kk] = tmem + C::Q_COL + (uint32_t)(kk * 8);
+                        bv[kk] = bd0 + (((uint32_t)(kk / 4) * (8 * C::W) + (uint32_t)(kk % 4) * 32u) >> 4);
                     }
+#pragma unroll
+                    for (int g = 0; g < D / 64; ++g)
+                        mma_ts_x4<true>(d_tmem, *reinterpret_cast<const uint32_t(*)[4]>(av + 4 * g),
+                                        *reinterpret_cast<const uint64_t(*)[4]>(bv + 4 * g), idS, g > 0 ? 1u : 0u);
                     mma_commit_pair(bar(PB_K_EMPTY + st));
                     mma_commit_pair(bar0_peer + 8u * (uint32_t)(PB_K_EMPTY + st));
                     if (jj < 50) TRACE(200 + jj);
@@ -755,16 +763,19 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 };
                 auto issue_pv = [&](int jj) {
                     const int st = jj % NS, sb = jj & 1;
-                    if (!mbar_wait(bar(PB_P_FULL + sb), (uint32_t)(jj >> 1) & 1u, abort, kWaitBudget)) return false;
                     if (!mbar_wait(bar(PB_V_FULL + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
-                    if (!mbar_wait(bar(PB_V_PEER + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
                     tc_fence_after();
                     if (jj < 50) TRACE(900 + jj);
                     const uint64_t bd0 = sdesc(v_addr + st * C::VH_BYTES, C::V_LBO, C::V_SBO, C::LAYOUT);
+                    static_assert(BN == 64, "one group of four P.V steps");
+                    uint32_t av[4];
+                    uint64_t bv[4];
 #pragma unroll
-                    for (int kk = 0; kk < BN / 16; ++kk)
-                        mma_ts_pair(tmem + C::O_COL, tmem + C::S_COL + (uint32_t)(sb * BN + kk * 8),
-                                    bd0 + ((uint32_t)kk * 2u * C::V_SBO >> 4), idO, (jj > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 4; ++kk) {
+                        av[kk] = tmem + C::S_COL + (uint32_t)(sb * BN + kk * 8);
+                        bv[kk] = bd0 + ((uint32_t)kk * 2u * C::V_SBO >> 4);
+                    }
+                    mma_ts_x4<true>(tmem + C::O_COL, av, bv, idO, jj > 0 ? 1u : 0u);
                     mma_commit_pair(bar(PB_V_EMPTY + st));
                     mma_commit_pair(bar0_peer + 8u * (uint32_t)(PB_V_EMPTY + st));
                     if (jj < 50) TRACE(250 + jj);
@@ -789,10 +800,10 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                     mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)(base_peer + st));
                     return true;
                 };
-                bool ok = relay(PB_K_FULL, PB_K_PEER, 0);
+                bool ok = relay(PB_K_FULL, PB_K_FULL, 0);
                 for (int jj = 0; ok && jj < n; ++jj) {
-                    if (jj + 1 < n) ok = relay(PB_K_FULL, PB_K_PEER, jj + 1);
-                    if (ok) ok = relay(PB_V_FULL, PB_V_PEER, jj);
+                    if (jj + 1 < n) ok = relay(PB_K_FULL, PB_K_FULL, jj + 1);
+                    if (ok) ok = relay(PB_V_FULL, PB_V_FULL, jj);
                 }
                 if (!ok) pair_fail(a, abort, 8);
             }
@@ -866,9 +877,9 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                     __syncwarp();
                     if (lane == 0) {
                         if (prefix && kv == 1) mbar_arrive(bar(PB_RAW_EMPTY + rs));
-                        // rank 0: its own "full" barrier; rank 1: rank 0's "peer" barrier
+                        // both ranks: rank 0's "full" barrier
                         if (pl.rank == 0) mbar_arrive(bar((kv ? PB_V_FULL : PB_K_FULL) + st));
-                        else mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)((kv ? PB_V_PEER : PB_K_PEER) + st));
+                        else mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)((kv ? PB_V_FULL : PB_K_FULL) + st));
                     }
                 };
                 if (prefix) {
@@ -892,7 +903,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             }
         }
     } else {
-        pair_softmax<Q8>(a, pl, smem, bar0, bar0_rank0 + 8u * PB_P_FULL, abort, tmem, n, n_qtiles, &omap, omode);
+        pair_softmax<Q8>(a, pl, smem, bar0, bar0_rank0 + 8u * PB_V_FULL, abort, tmem, n, n_qtiles, &omap, omode);
     }
     if (threadIdx.x == 0) {
         TRACE(11);

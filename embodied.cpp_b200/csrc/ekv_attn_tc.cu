@@ -825,11 +825,22 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)(sb * BN);
                 const uint64_t bd0 = sdesc(k_addr + st * C::KV_BYTES, 16, C::SBO, C::LAYOUT);
+                constexpr int KS = D / 16, KPC = W / 32;  // K steps; K steps per swizzle chunk
+                uint32_t av[KS];
+                uint64_t bv[KS];
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    constexpr int KPC = W / 32;  // K-steps per swizzle chunk
-                    const uint32_t off = (uint32_t)(kk / KPC) * (8 * W) + (uint32_t)(kk % KPC) * 32u;
-                    mma_ts(d_tmem, tmem + C::Q_COL + (uint32_t)(kk * 8), bd0 + (off >> 4), idS, kk > 0 ? 1u : 0u);
+                for (int kk = 0; kk < KS; ++kk) {
+                    av[kk] = tmem + C::Q_COL + (uint32_t)(kk * 8);
+                    bv[kk] = bd0 + (((uint32_t)(kk / KPC) * (8 * W) + (uint32_t)(kk % KPC) * 32u) >> 4);
+                }
+                if constexpr (KS % 4 == 0) {
+#pragma unroll
+                    for (int g = 0; g < KS / 4; ++g)
+                        mma_ts_x4<false>(d_tmem, *reinterpret_cast<const uint32_t(*)[4]>(av + 4 * g),
+                                         *reinterpret_cast<const uint64_t(*)[4]>(bv + 4 * g), idS, g > 0 ? 1u : 0u);
+                } else {
+#pragma unroll
+                    for (int kk = 0; kk < KS; ++kk) mma_ts(d_tmem, av[kk], bv[kk], idS, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(bar(BAR_K_EMPTY + st));  // S(j) done: K stage free, S(j) readable
                 if (jj < 50) TRACE(200 + jj);
@@ -841,10 +852,18 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
                 if (!mbar_wait(bar(BAR_V_FULL + st), (jj / NS) & 1, abort, kWaitBudget)) return false;
                 tc_fence_after();
                 const uint64_t bd0 = sdesc(v_addr + st * C::KV_BYTES, 8 * W, C::SBO, C::LAYOUT);
+                constexpr int PS = BN / 16;  // P.V K steps (4 or 8)
+                uint32_t av[PS];
+                uint64_t bv[PS];
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk)
-                    mma_ts(tmem + C::O_COL, tmem + C::S_COL + (uint32_t)(sb * BN + kk * 8),
-                           bd0 + ((uint32_t)kk * 2u * C::SBO >> 4), idO, (jj > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < PS; ++kk) {
+                    av[kk] = tmem + C::S_COL + (uint32_t)(sb * BN + kk * 8);
+                    bv[kk] = bd0 + ((uint32_t)kk * 2u * C::SBO >> 4);
+                }
+#pragma unroll
+                for (int g = 0; g < PS / 4; ++g)
+                    mma_ts_x4<false>(tmem + C::O_COL, *reinterpret_cast<const uint32_t(*)[4]>(av + 4 * g),
+                                     *reinterpret_cast<const uint64_t(*)[4]>(bv + 4 * g), idO, (jj > 0 || g > 0) ? 1u : 0u);
                 mma_commit(bar(BAR_V_EMPTY + st));  // P.V(j) done: V stage free, P(j) consumed
                 if (jj < 50) TRACE(250 + jj);
                 return true;
@@ -1388,11 +1407,15 @@ int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s) {
     return cudaGetLastError() == cudaSuccess ? EKV_OK : EKV_ERR_CUDA;
 }
 
-int launch_attention_tc(const AttnArgs &a, cudaStream_t s, bool allow_pair) {
+int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k) {
     // a.n_splits == 0 means: a workspace was given at a.ws_o, choose the split count.
     size_t ws = 0;
     if (a.n_splits == 0) ws = (size_t)-1;  // the C-ABI checked the size against the maximum need
-    if (allow_pair && a.pool.head_dim == 256) return launch_attention_pair(a, s, ws, sm_count());
+    // Q8_0 at head_dim 256: each SM of a pair dequantises half of every tile and the copy engine
+    // fetches half the bytes, which the one-CTA kernel's dequantiser cannot keep up with
+    const bool pair = a.pool.head_dim == 256 &&
+                      (k == TcKernel::Pair || (k == TcKernel::Auto && a.pool.dtype == EKV_DTYPE_Q8_0));
+    if (pair) return launch_attention_pair(a, s, ws, sm_count());
     return a.pool.dtype == EKV_DTYPE_Q8_0 ? dispatch<true>(a, s, ws) : dispatch<false>(a, s, ws);
 }
 

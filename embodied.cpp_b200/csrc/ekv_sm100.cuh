@@ -309,6 +309,38 @@ __device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, ui
 
 // Arrive once on the mbarrier at `cluster_addr` (this CTA's or the peer's) when every pair MMA this
 // thread issued so far has finished.
+// Four tcgen05.mma back to back in one instruction block (cta_group::2 when PAIR), A in TMEM at
+// a[0..3], B descriptors b[0..3]; the first accumulates into D only when acc0 != 0, the others
+// always. The tensor pipe's issue queue is about one MMA deep, so every instruction between two
+// MMAs of a group lengthens an N = 64 MMA (45 cycles) by its own issue time.
+template <bool PAIR>
+__device__ __forceinline__ void mma_ts_x4(uint32_t d_tmem, const uint32_t (&a)[4], const uint64_t (&b)[4], uint32_t idesc,
+                                          uint32_t acc0) {
+    if constexpr (PAIR) {
+        asm volatile(
+            "{\n\t.reg .pred p, t;\n\t"
+            "setp.ne.b32 p, %10, 0;\n\t"
+            "setp.eq.b32 t, %10, %10;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %5, %9, p;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], [%2], %6, %9, t;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], [%3], %7, %9, t;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], [%4], %8, %9, t;\n\t}" ::"r"(d_tmem),
+            "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc), "r"(acc0)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p, t;\n\t"
+            "setp.ne.b32 p, %10, 0;\n\t"
+            "setp.eq.b32 t, %10, %10;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %5, %9, p;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %6, %9, t;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %7, %9, t;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %9, t;\n\t}" ::"r"(d_tmem),
+            "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc), "r"(acc0)
+            : "memory");
+    }
+}
+
 __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                  : "memory");

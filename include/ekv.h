@@ -200,11 +200,14 @@ int ekv_attention(ekv_pool *pool, const ekv_attn_params *p, const void *q, void 
 int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                           ekv_stream_t stream);
 
-#define EKV_ALGO_TC 0     /* tcgen05 tensor-core kernel (default)                           */
-#define EKV_ALGO_SIMT 1   /* one-warp-per-row CUDA-core kernel, kept as a GPU cross-check   */
+#define EKV_ALGO_TC 0      /* tcgen05 tensor cores (default): the CTA-pair kernel for Q8_0 pools
+                              with head_dim 256, the one-CTA kernel otherwise                 */
+#define EKV_ALGO_SIMT 1    /* one-warp-per-row CUDA-core kernel, kept as a GPU cross-check   */
 #define EKV_ALGO_TC_PAIR 2 /* head_dim 256 on CTA pairs (tcgen05 cta_group::2, 256 query rows
                               per pair, each K/V tile split between the two CTAs); other head
-                              dims fall back to EKV_ALGO_TC                                    */
+                              dims use the one-CTA kernel                                     */
+#define EKV_ALGO_TC_CTA 3  /* the one-CTA tcgen05 kernel (128 query rows per CTA) for every
+                              head dim                                                        */
 int ekv_attention_algo(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                        void *workspace, size_t workspace_bytes, int32_t algo,
                        ekv_stream_t stream);

@@ -21,7 +21,7 @@ D = 256
 
 def both(f, q, *, Hq, scale, **kw):
     got = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC_PAIR, **kw)
-    single = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC, **kw)
+    single = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC_CTA, **kw)
     return got, single
 
 

@@ -17,7 +17,7 @@ from cases import Filled, bf16_randn, to_f32_np
 pytestmark = pytest.mark.gpu
 
 TOL = {ekv.DTYPE_BF16: 2e-2, ekv.DTYPE_Q8_0: 5e-2}
-ALGOS = [ekv.ALGO_TC, ekv.ALGO_SIMT]
+ALGOS = [ekv.ALGO_TC, ekv.ALGO_TC_CTA, ekv.ALGO_SIMT]
 
 
 def gather_prefix(f, layer, b, fmt):
