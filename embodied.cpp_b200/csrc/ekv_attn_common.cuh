@@ -170,6 +170,15 @@ using sm100::smem_addr;
 using sm100::tma_store_2d;
 using sm100::tma_store_5d;
 
+// Byte offset of 16-byte unit `c` of staged Q row `r` (rows of `qstr` bytes). When a row has a
+// multiple of 8 units (head_dim 64, 128, 256), the units are XOR-swizzled by r & 7, so 8
+// consecutive rows of one unit land in 8 different bank groups; other widths are not swizzled.
+__device__ __forceinline__ uint32_t q_stage_off(int r, int c, int qstr) {
+    const int units = qstr / 16;
+    const int m = (units % 8 == 0) ? 7 : 0;
+    return (uint32_t)(r * qstr + ((c ^ (r & m)) << 4));
+}
+
 // ---- output epilogue through the copy engine ----
 // O rows are staged as 4 KB boxes of 32 rows (one TMEM lane quarter) x 128 bytes (64 bf16 or 32
 // f32 columns), 128-byte swizzled: 16-byte unit u of box row i sits at unit u ^ (i & 7), the layout
@@ -230,6 +239,46 @@ __device__ __forceinline__ void store_o_boxes(const AttnArgs &a, int qrow0, int 
             else
                 tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM) + quarter * 32);
         }
+        bulk_commit_group();
+        bulk_wait_group_read0();
+    }
+    __syncwarp();
+}
+
+// Whole warp, epilogue of O columns [c_lo, c_hi) (multiples of 64) of this warp's lane quarter:
+// two 32-column TMEM loads in flight, staged as boxes, and each 64 columns' boxes handed to the copy
+// engine as soon as they are staged; lane 0 waits once at the end until they have been read.
+// Store coordinates as in store_o_boxes.
+__device__ __forceinline__ void epilogue_o_tma(const AttnArgs &a, int qrow0, int rows_valid, int g, int b,
+                                               const void *omap, int omode, uint8_t *boxes, int quarter, int lane,
+                                               uint32_t o_taddr, int c_lo, int c_hi, bool have_o, float inv, bool f32,
+                                               int64_t unit) {
+    const int boxc = f32 ? 32 : 64;
+    const bool issuer = lane == 0 && quarter * 32 < rows_valid;
+    const int row0 = qrow0 + quarter * 32;
+#pragma unroll 1
+    for (int c0 = c_lo; c0 < c_hi; c0 += 64) {
+        uint32_t oa[32], ob[32];
+        if (have_o) {
+            sm100::tmem_load32x2(o_taddr + (uint32_t)c0, o_taddr + (uint32_t)(c0 + 32), oa, ob);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) oa[i] = ob[i] = 0u;
+        }
+        stage_o_box<32>(boxes, quarter, lane, c0, oa, inv, f32);
+        stage_o_box<32>(boxes, quarter, lane, c0 + 32, ob, inv, f32);
+        fence_proxy_async();
+        __syncwarp();
+        if (issuer)
+            for (int cb = c0 / boxc; cb < (c0 + 64) / boxc; ++cb) {
+                const uint32_t src = smem_addr(boxes + (cb * 4 + quarter) * kOutBox);
+                if (omode == OUT_TMA_ROWS)
+                    tma_store_5d(omap, src, cb * boxc, row0 % a.group, g, row0 / a.group, b);
+                else
+                    tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM) + quarter * 32);
+            }
+    }
+    if (issuer) {
         bulk_commit_group();
         bulk_wait_group_read0();
     }

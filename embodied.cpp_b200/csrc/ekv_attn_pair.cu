@@ -539,6 +539,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         ok = false;
         pair_fail(a, abort, 7);
     }
+    if (r == 0 && h == 0) TRACE(13);
     const float l_row = ok ? xl[r] + xl[kBM + r] : 0.0f;
     const bool have_o = ok && n > 0;
     // O -> shared staging row r -> the softmax warps write whole rows with consecutive 16-byte lanes
@@ -559,20 +560,10 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
     }
     if (omode != OUT_THREADS) {
         // this warp's columns of its lane quarter -> swizzled boxes -> copy engine
-        const int boxc = f32 ? 32 : 64;
-#pragma unroll 1
-        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
-            uint32_t o32[32];
-            if (have_o) {
-                tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) o32[i] = 0u;
-            }
-            stage_o_box<32>(smem, quarter, lane, c0, o32, inv, f32);
-        }
-        store_o_boxes(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem, quarter, h * DH / boxc,
-                      (h + 1) * DH / boxc, boxc, unit);
+        if (r == 0 && h == 0) TRACE(14);
+        epilogue_o_tma(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem, quarter, lane,
+                       tmem + lane_base + (uint32_t)C::O_COL, h * DH, (h + 1) * DH, have_o, inv, f32, unit);
+        if (r == 0 && h == 0) TRACE(15);
         return;
     }
     uint8_t *orow = smem + r * C::OSTR;
@@ -646,6 +637,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
         TRACE_CLK(20);
     }
     const PairPlan pl = make_pair_plan(a);
+    if (threadIdx.x == 0) TRACE(1);
     const uint32_t peer = (uint32_t)(pl.rank ^ 1);
     const uint32_t bar0_rank0 = mapa_shared(bar0, 0);  // rank 0's barrier block (cluster window)
     const uint32_t bar0_peer = mapa_shared(bar0, peer);
@@ -701,10 +693,12 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             }
         }
     }
+    if (threadIdx.x == 0) TRACE(2);
     tc_fence_before();
     __syncthreads();
-    cluster_sync();  // both CTAs' barriers initialised and tensor memory allocated
+    cluster_sync_relaxed();  // both CTAs' barriers initialised (fenced above) and tensor memory allocated
     tc_fence_after();
+    if (threadIdx.x == 0) TRACE(5);
     const uint32_t tmem = *tmem_holder;
     if (warp < C::SMW) {
         // row (warp & 3) * 32 + lane; the two warps of a lane quarter take 8 of the 16 column blocks each
@@ -912,7 +906,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
     __syncwarp();
     tc_fence_before();
     __syncthreads();
-    cluster_sync();  // rank 0's MMAs are finished; neither CTA releases memory the other still uses
+    cluster_sync_relaxed();  // rank 0's MMAs are finished; neither CTA releases memory the other still uses
     tc_fence_after();
     if (warp == C::MMA_WARP) tmem_dealloc_pair(tmem, C::TMEM_COLS);
     if (threadIdx.x == 0) TRACE(12);

@@ -210,14 +210,6 @@ __device__ __forceinline__ const uint8_t *ptr_of(const AttnArgs &a, const Plan &
                    : a.pool.prefix + prefix_tile_index(a.pool, a.layer, blk, 0, pl.g) * a.pool.tile_bytes;
 }
 
-// Byte offset of 16-byte unit `c` of staged Q row `r` (rows of `qstr` bytes). When a row has a
-// multiple of 8 units (head_dim 64, 128, 256), the units are XOR-swizzled by r & 7, so 8
-// consecutive rows of one unit land in 8 different bank groups; other widths are not swizzled.
-__device__ __forceinline__ uint32_t q_stage_off(int r, int c, int qstr) {
-    const int units = qstr / 16;
-    const int m = (units % 8 == 0) ? 7 : 0;
-    return (uint32_t)(r * qstr + ((c ^ (r & m)) << 4));
-}
 
 // ---- Q: bf16 [B][Tq][Hq][D] rows -> shared staging (all threads, every load in flight before
 // the first store) -> TMEM Q columns (softmax warps, one row per thread; f16 for Q8_0 pools) ----
@@ -662,20 +654,8 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
     }
     if (omode != OUT_THREADS) {
         // this warp's columns [h * D/2, (h + 1) * D/2) of its lane quarter -> swizzled boxes -> copy engine
-        const int boxc = f32 ? 32 : 64;
-#pragma unroll 1
-        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
-            uint32_t o32[32];
-            if (have_o) {
-                tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) o32[i] = 0u;
-            }
-            stage_o_box<32>(smem + C::OFF_K, quarter, lane, c0, o32, inv, f32);
-        }
-        store_o_boxes(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem + C::OFF_K, quarter, h * DH / boxc,
-                      (h + 1) * DH / boxc, boxc, unit);
+        epilogue_o_tma(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem + C::OFF_K, quarter, lane,
+                       tmem + lane_base + (uint32_t)C::O_COL, h * DH, (h + 1) * DH, have_o, inv, f32, unit);
         return;
     }
     uint8_t *orow = (smem + C::OFF_K) + r * C::OSTR;
