@@ -411,9 +411,8 @@ def main():
         with open(tp) as f:
             roof["traffic"] = json.load(f).get(args.workload)
     roof["peak_source"] = peaks["source"] + " (burst bf16 figure)"
-    # the library's default tcgen05 kernel for these pools (EKV_ALGO_TC): CTA pairs for Q8_0 at
-    # head_dim 256, one CTA per 128 query rows for bf16
-    roof["kernel"] = "attn_pair_kernel<Q8>" if wl.dtype == wl.ekv.DTYPE_Q8_0 else "attn_tc_kernel<256,bf16>"
+    # the library's default tcgen05 kernel at head_dim 256 (EKV_ALGO_TC): CTA pairs
+    roof["kernel"] = "attn_pair_kernel<Q8>" if wl.dtype == wl.ekv.DTYPE_Q8_0 else "attn_pair_kernel<bf16>"
     roof["avg_launch_us"] = attn_avg_s * 1e6
     roof["algorithmic_per_launch"] = {"flop": wl.flop_per_call, "bytes": wl.bytes_per_call}
 

@@ -67,9 +67,10 @@ struct PairCfg {
     static constexpr int QSTR = D * 2 + 16;  // Q staging row stride
     static constexpr int OSTR = D * 4 + 16;  // epilogue staging row stride (f32 worst case)
     static constexpr int SMW = 8;
-    // 8 = MMA issue (rank 0) / relay (rank 1); 9, 10 = K and V copy feeders; 11-18 = dequantisation
-    static constexpr int MMA_WARP = 8, TMA_WARP = 9, DQ_WARP0 = 11;
-    static constexpr int THREADS = (SMW + 3) * 32 + (Q8 ? kDq : 0);
+    // 8 = MMA issue (rank 0); 9, 10 = K and V copy feeders; 11-18 = dequantisation (Q8_0) or
+    // 11 = relay of the copies' completion (bf16)
+    static constexpr int MMA_WARP = 8, TMA_WARP = 9, DQ_WARP0 = 11, RELAY_WARP = 11;
+    static constexpr int THREADS = (SMW + 3) * 32 + (Q8 ? kDq : 32);
     static constexpr int TMEM_COLS = 512;
     static constexpr int S_COL = 0, O_COL = 2 * BN, Q_COL = 512 - D / 2;
     static_assert(O_COL + D <= Q_COL, "TMEM budget");
@@ -79,16 +80,19 @@ struct PairCfg {
     static_assert((D / 32) * 4 * kOutBox <= OFF_BAR, "epilogue boxes (f32) fit below the barriers");
 };
 
-// Each MMA group waits on exactly one barrier: a wait in the issuing thread costs about 220 cycles
-// of idle tensor pipe (the issue queue is one MMA deep). S(j) waits K_FULL(j) (both CTAs' K halves);
-// P.V(j) waits V_FULL(j), which also counts the P(j) arrivals of both CTAs' softmax warps. Rank 1's
-// softmax and dequantisation warps arrive directly on rank 0's barriers; for bf16, rank 1's relay
-// thread forwards its copies' completion. All arrivals release at CTA scope (mbar_arrive_remote).
+// The MMA thread waits once per tile: a wait in the issuing thread costs about 220 cycles of idle
+// tensor pipe (the issue queue is one MMA deep). After S(0) and S(1) (K_FULL), it issues for each j
+// P.V(j) and then S(j + 2) behind it, both gated by PVK(j), which counts the V(j) and P(j) arrivals
+// and the K(j + 2) arrivals of both CTAs. Rank 1's softmax and dequantisation warps arrive directly
+// on rank 0's barriers; for bf16, each CTA's relay warp forwards its copies' completion (the copies
+// signal per-stage barriers of their own CTA, which an aborting feeder can wait on). All arrivals
+// release at CTA scope (mbar_arrive_remote).
 enum {
-    PB_K_FULL = 0,       // [6] K half ready: on rank 0 both CTAs' halves (rank 1 arrives remotely)
-                         // 6-11 unused
+    PB_K_FULL = 0,       // [6] bf16: this CTA's K half landed (forwarded by its relay warp)
+    PB_KINIT = 6,        // [2] rank 0: both CTAs' K halves of tiles 0 and 1
+                         // 8-11 unused
     PB_K_EMPTY = 12,     // [6] S(j) done (committed to both CTAs): K stage free, S(j) readable
-    PB_V_FULL = 18,      // [6] V half ready; on rank 0 also P(j) written by both CTAs' softmax warps
+    PB_V_FULL = 18,      // [6] bf16: this CTA's V half landed (forwarded by its relay warp)
                          // 24-29 unused
     PB_V_EMPTY = 30,     // [6] P.V(j) done (both CTAs): V stage free, P(j) consumed, O updated
     PB_RAW_FULL = 36,    // [3] raw Q8_0 stage landed (both feeders' copies)
@@ -97,9 +101,17 @@ enum {
                          // 46-47 unused
     PB_DONE = 48,
     PB_XCH = 49,         // [4] softmax pair exchange
-    PB_N = 53
+    PB_PVK = 53,         // [6] rank 0: everything P.V(j) and the S(j + 2) issued behind it need --
+                         //     V(j) and P(j) of both CTAs, and both K halves of tile j + 2
+    PB_N = 59
 };
+
+// Barrier of rank 0 that the producers of K(t) arrive on: K(0) and K(1) on KINIT, later tiles on
+// the barrier of the P.V two tiles earlier, so that the MMA thread waits once per tile. A tile past
+// the end still arrives there (no data), so every phase completes.
+__device__ __forceinline__ int pair_k_bar(int t, int ns) { return t < 2 ? PB_KINIT + t : PB_PVK + (t - 2) % ns; }
 static_assert(PB_N * 8 + 16 <= 512, "barrier block");
+static_assert(PB_PVK + 6 <= PB_N, "PVK covers the deepest stage ring");
 
 __device__ __forceinline__ uint32_t stage_parity(int j, int ns) { return (uint32_t)(j / ns) & 1u; }
 
@@ -415,7 +427,7 @@ __device__ __forceinline__ bool pair_xsync(uint32_t xbar, int use, volatile int 
 // per warp on rank 0's barrier. ----
 template <bool Q8>
 __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &pl, uint8_t *smem, uint32_t bar0,
-                                             uint32_t v_full0, volatile int *abort, uint32_t tmem, int n, int n_qtiles,
+                                             uint32_t pvk0, volatile int *abort, uint32_t tmem, int n, int n_qtiles,
                                              const void *omap, int omode) {
     using C = PairCfg<Q8>;
     constexpr int BN = C::BN, D = C::D, DH = D / 2, NS = C::NSTAGE;
@@ -522,7 +534,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_remote(v_full0 + 8u * (uint32_t)(jj % NS));
+        if (lane == 0) mbar_arrive_remote(pvk0 + 8u * (uint32_t)(jj % NS));
         if (lane == 0 && jj == 7) TRACE(1016 + warp);
         if (r == 0 && h == 0 && jj < 50) TRACE(350 + jj);
     }
@@ -646,10 +658,12 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
     if (threadIdx.x == 0) {
         // producers per CTA: the dequant warps (Q8_0) or the feeder's byte-counted arrival (bf16);
         // rank 0's barriers also count rank 1's
-        const uint32_t n_full = (Q8 ? kDq / 32 : 1) * (pl.rank == 0 ? 2 : 1);
+        const uint32_t per_rank = Q8 ? kDq / 32 : 1;
+        for (int s = 0; s < 2; ++s) mbar_init(bar(PB_KINIT + s), 2 * per_rank);
         for (int s = 0; s < NS; ++s) {
-            mbar_init(bar(PB_K_FULL + s), n_full);
-            mbar_init(bar(PB_V_FULL + s), n_full + (pl.rank == 0 ? 2 * C::SMW : 0));
+            mbar_init(bar(PB_K_FULL + s), 1);
+            mbar_init(bar(PB_V_FULL + s), 1);
+            mbar_init(bar(PB_PVK + s), 4 * per_rank + 2 * C::SMW);
             mbar_init(bar(PB_K_EMPTY + s), 1);
             mbar_init(bar(PB_V_EMPTY + s), 1);
         }
@@ -731,10 +745,8 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 const uint32_t idS = idesc_f16_m(!Q8, false, BN, 256);
                 const uint32_t idO = idesc_f16_m(!Q8, true, D, 256);
                 const uint32_t k_addr = smem_addr(sK), v_addr = smem_addr(sV);
-                auto issue_s = [&](int jj) {
+                auto issue_s = [&](int jj) {  // K(jj) is known to be in place
                     const int st = jj % NS, sb = jj & 1;
-                    if (!mbar_wait(bar(PB_K_FULL + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
-                    tc_fence_after();
                     if (jj < 50) TRACE(850 + jj);
                     const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)(sb * BN);
                     const uint64_t bd0 = sdesc(k_addr + st * C::KH_BYTES, 16, C::K_SBO, C::LAYOUT);
@@ -753,11 +765,10 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                     mma_commit_pair(bar(PB_K_EMPTY + st));
                     mma_commit_pair(bar0_peer + 8u * (uint32_t)(PB_K_EMPTY + st));
                     if (jj < 50) TRACE(200 + jj);
-                    return true;
                 };
                 auto issue_pv = [&](int jj) {
                     const int st = jj % NS, sb = jj & 1;
-                    if (!mbar_wait(bar(PB_V_FULL + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
+                    if (!mbar_wait(bar(PB_PVK + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
                     tc_fence_after();
                     if (jj < 50) TRACE(900 + jj);
                     const uint64_t bd0 = sdesc(v_addr + st * C::VH_BYTES, C::V_LBO, C::V_SBO, C::LAYOUT);
@@ -775,31 +786,20 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                     if (jj < 50) TRACE(250 + jj);
                     return true;
                 };
-                bool ok = issue_s(0);
+                // S(0), S(1), then P.V(j) and S(j + 2) for each j: one wait per tile
+                bool ok = true;
+                for (int jj = 0; ok && jj < 2 && jj < n; ++jj) {
+                    ok = mbar_wait(bar(PB_KINIT + jj), 0, abort, kWaitBudget);
+                    tc_fence_after();
+                    if (ok) issue_s(jj);
+                }
                 for (int jj = 0; ok && jj < n; ++jj) {
-                    if (jj + 1 < n) ok = issue_s(jj + 1);
-                    if (ok) ok = issue_pv(jj);
+                    ok = issue_pv(jj);
+                    if (ok && jj + 2 < n) issue_s(jj + 2);
                 }
                 if (!ok) pair_fail(a, abort, 1);
                 mma_commit_pair(bar(PB_DONE));
                 mbar_wait(bar(PB_DONE), 0, abort, kWaitBudget);
-            }
-        } else if constexpr (!Q8) {
-            // ---- rank 1, bf16: forward "my K/V half landed" to rank 0, in the order its MMAs use
-            // them: K(0), then K(j+1) before V(j) ----
-            if (n > 0 && lane == 0) {
-                auto relay = [&](int base_full, int base_peer, int jj) {
-                    const int st = jj % NS;
-                    if (!mbar_wait(bar(base_full + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
-                    mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)(base_peer + st));
-                    return true;
-                };
-                bool ok = relay(PB_K_FULL, PB_K_FULL, 0);
-                for (int jj = 0; ok && jj < n; ++jj) {
-                    if (jj + 1 < n) ok = relay(PB_K_FULL, PB_K_FULL, jj + 1);
-                    if (ok) ok = relay(PB_V_FULL, PB_V_FULL, jj);
-                }
-                if (!ok) pair_fail(a, abort, 8);
             }
         }
         __syncwarp();
@@ -845,6 +845,25 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 for (int jj = max(0, issued - NS); jj < issued; ++jj)
                     mbar_wait(bar(b_full + jj % NS), stage_parity(jj, NS), abort, kWaitBudget / 4);
         }
+    } else if (!Q8 && warp == C::RELAY_WARP) {
+        // ---- bf16: forward "this CTA's K/V half landed" to rank 0, in the order its MMAs use
+        // them: K(0), K(1), then V(j) and K(j + 2) per tile ----
+        if (n > 0 && lane == 0) {
+            auto relay = [&](uint32_t local, uint32_t parity, int remote) {
+                if (!mbar_wait(local, parity, abort, kWaitBudget)) return false;
+                mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)remote);
+                return true;
+            };
+            bool ok = relay(bar(PB_K_FULL), 0u, PB_KINIT);
+            if (ok && n > 1) ok = relay(bar(PB_K_FULL + 1), 0u, PB_KINIT + 1);
+            for (int jj = 0; ok && jj < n; ++jj) {
+                ok = relay(bar(PB_V_FULL + jj % NS), stage_parity(jj, NS), PB_PVK + jj % NS);
+                const int t = jj + 2;  // K(t) arrives with P.V(jj); past the end, with no data
+                if (ok && t < n) ok = relay(bar(PB_K_FULL + t % NS), stage_parity(t, NS), pair_k_bar(t, NS));
+                else if (ok) mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)pair_k_bar(t, NS));
+            }
+            if (!ok) pair_fail(a, abort, 8);
+        }
     } else if (warp >= C::DQ_WARP0) {
         if constexpr (Q8) {
             const int dtid = threadIdx.x - C::DQ_WARP0 * 32;
@@ -871,9 +890,8 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                     __syncwarp();
                     if (lane == 0) {
                         if (prefix && kv == 1) mbar_arrive(bar(PB_RAW_EMPTY + rs));
-                        // both ranks: rank 0's "full" barrier
-                        if (pl.rank == 0) mbar_arrive(bar((kv ? PB_V_FULL : PB_K_FULL) + st));
-                        else mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)((kv ? PB_V_FULL : PB_K_FULL) + st));
+                        // both ranks: rank 0's barrier of the MMA group that uses this half
+                        mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)(kv ? PB_PVK + st : pair_k_bar(jj, NS)));
                     }
                 };
                 if (prefix) {
@@ -895,9 +913,12 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 }
                 if (dtid == 0 && jj < 50) TRACE(100 + jj);
             }
+            // K of the (up to two) tiles past the end still arrives, so the last PVK phases complete
+            if (lane == 0 && !*abort)
+                for (int t = max(n, 2); t < n + 2; ++t) mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)pair_k_bar(t, NS));
         }
     } else {
-        pair_softmax<Q8>(a, pl, smem, bar0, bar0_rank0 + 8u * PB_V_FULL, abort, tmem, n, n_qtiles, &omap, omode);
+        pair_softmax<Q8>(a, pl, smem, bar0, bar0_rank0 + 8u * PB_PVK, abort, tmem, n, n_qtiles, &omap, omode);
     }
     if (threadIdx.x == 0) {
         TRACE(11);

@@ -1391,10 +1391,9 @@ int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k) {
     // a.n_splits == 0 means: a workspace was given at a.ws_o, choose the split count.
     size_t ws = 0;
     if (a.n_splits == 0) ws = (size_t)-1;  // the C-ABI checked the size against the maximum need
-    // Q8_0 at head_dim 256: each SM of a pair dequantises half of every tile and the copy engine
-    // fetches half the bytes, which the one-CTA kernel's dequantiser cannot keep up with
-    const bool pair = a.pool.head_dim == 256 &&
-                      (k == TcKernel::Pair || (k == TcKernel::Auto && a.pool.dtype == EKV_DTYPE_Q8_0));
+    // head_dim 256: each SM of a pair copies (bf16) or dequantises (Q8_0) half of every tile, and
+    // each K/V byte crosses L2 -> SM twice per request instead of four times
+    const bool pair = a.pool.head_dim == 256 && k != TcKernel::OneCta;
     if (pair) return launch_attention_pair(a, s, ws, sm_count());
     return a.pool.dtype == EKV_DTYPE_Q8_0 ? dispatch<true>(a, s, ws) : dispatch<false>(a, s, ws);
 }

@@ -55,8 +55,8 @@ int launch_gather(const PoolView &p, int layer, int seq, int pos0, int n_rows, i
 int launch_gather_suffix(const PoolView &p, int layer, int seq, int n_rows, int format,
                          void *k_out, void *v_out, cudaStream_t s);
 int launch_attention_simt(const AttnArgs &a, cudaStream_t s);
-// Which tcgen05 kernel runs a call: Auto = the CTA-pair kernel (ekv_attn_pair.cu) for Q8_0 pools
-// with head_dim 256, one CTA per 128 query rows otherwise; Pair = CTA pairs whenever head_dim is 256.
+// Which tcgen05 kernel runs a call: Auto and Pair = the CTA-pair kernel (ekv_attn_pair.cu) for
+// head_dim 256, one CTA per 128 query rows otherwise; OneCta = one CTA per 128 query rows always.
 enum class TcKernel { Auto, Pair, OneCta };
 int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k);
 size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix);

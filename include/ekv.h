@@ -200,8 +200,8 @@ int ekv_attention(ekv_pool *pool, const ekv_attn_params *p, const void *q, void 
 int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                           ekv_stream_t stream);
 
-#define EKV_ALGO_TC 0      /* tcgen05 tensor cores (default): the CTA-pair kernel for Q8_0 pools
-                              with head_dim 256, the one-CTA kernel otherwise                 */
+#define EKV_ALGO_TC 0      /* tcgen05 tensor cores (default): the CTA-pair kernel for head_dim
+                              256, the one-CTA kernel otherwise                               */
 #define EKV_ALGO_SIMT 1    /* one-warp-per-row CUDA-core kernel, kept as a GPU cross-check   */
 #define EKV_ALGO_TC_PAIR 2 /* head_dim 256 on CTA pairs (tcgen05 cta_group::2, 256 query rows
                               per pair, each K/V tile split between the two CTAs); other head
