@@ -183,9 +183,9 @@ __device__ __forceinline__ uint32_t q_stage_off(int r, int c, int qstr) {
 // O rows are staged as 4 KB boxes of 32 rows (one TMEM lane quarter) x 128 bytes (64 bf16 or 32
 // f32 columns), 128-byte swizzled: 16-byte unit u of box row i sits at unit u ^ (i & 7), the layout
 // a CU_TENSOR_MAP_SWIZZLE_128B map reads, so the 8 lanes of a store phase hit 8 distinct bank
-// groups. Box (cb, quarter) is at cb * 4 + quarter. Lane 0 of each warp then stores the warp's
-// boxes with cp.async.bulk.tensor: no cross-warp barrier, and no thread-issued global stores (which
-// drain several times slower than the copy engine's from this kernel).
+// groups. Box (cb, quarter) is at cb * 4 + quarter, so the four quarters of column block cb form
+// one 128-row box, which one lane stores with cp.async.bulk.tensor (no thread-issued global stores,
+// which drain several times slower than the copy engine's from this kernel).
 enum { OUT_THREADS = 0, OUT_TMA_ROWS = 1, OUT_TMA_WS = 2 };
 constexpr int kOutBox = 4096;
 
@@ -220,42 +220,20 @@ __device__ __forceinline__ void stage_o_box(uint8_t *boxes, int quarter, int lan
     }
 }
 
-// Whole warp, after staging its boxes [cb0, cb1) of lane quarter `quarter`: lane 0 stores them and
-// waits until the copy engine has read them (the CTA may exit afterwards). OUT_TMA_ROWS maps the
-// output as (head_dim, head in group, KV head, token, batch): box row i of the quarter is query
-// row qrow0 + quarter * 32 + i, and rows past the call's tokens fall outside the map. OUT_TMA_WS
-// maps the workspace as (head_dim, unit * 128 + row).
-__device__ __forceinline__ void store_o_boxes(const AttnArgs &a, int qrow0, int rows_valid, int g, int b,
-                                              const void *omap, int omode, const uint8_t *boxes, int quarter, int cb0,
-                                              int cb1, int boxc, int64_t unit) {
-    fence_proxy_async();
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0 && quarter * 32 < rows_valid) {
-        const int row0 = qrow0 + quarter * 32;
-        for (int cb = cb0; cb < cb1; ++cb) {
-            const uint32_t src = smem_addr(boxes + (cb * 4 + quarter) * kOutBox);
-            if (omode == OUT_TMA_ROWS)
-                tma_store_5d(omap, src, cb * boxc, row0 % a.group, g, row0 / a.group, b);
-            else
-                tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM) + quarter * 32);
-        }
-        bulk_commit_group();
-        bulk_wait_group_read0();
-    }
-    __syncwarp();
-}
-
-// Whole warp, epilogue of O columns [c_lo, c_hi) (multiples of 64) of this warp's lane quarter:
-// two 32-column TMEM loads in flight, staged as boxes, and each 64 columns' boxes handed to the copy
-// engine as soon as they are staged; lane 0 waits once at the end until they have been read.
-// Store coordinates as in store_o_boxes.
+// Epilogue of O columns [c_lo, c_hi) (multiples of 64) by the four warps of one column range
+// (one per TMEM lane quarter), all four calling it: two 32-column TMEM loads in flight, staged as
+// 32-row boxes; the four quarter boxes of a column block are contiguous, i.e. one 128-row box,
+// which one lane stores as soon as the four warps have staged it (named barrier `bar_id`, 128
+// threads). Box coordinates: OUT_TMA_ROWS maps the output as (head_dim, head in group, KV head,
+// token, batch) with box row i = query row qrow0 + i (rows past the call's tokens fall outside the
+// map); OUT_TMA_WS maps the workspace as (head_dim, unit * 128 + row). Each issuing lane waits
+// once at the end until its stores have been read.
 __device__ __forceinline__ void epilogue_o_tma(const AttnArgs &a, int qrow0, int rows_valid, int g, int b,
                                                const void *omap, int omode, uint8_t *boxes, int quarter, int lane,
                                                uint32_t o_taddr, int c_lo, int c_hi, bool have_o, float inv, bool f32,
-                                               int64_t unit) {
+                                               int64_t unit, int bar_id) {
     const int boxc = f32 ? 32 : 64;
-    const bool issuer = lane == 0 && quarter * 32 < rows_valid;
-    const int row0 = qrow0 + quarter * 32;
+    bool issued = false;
 #pragma unroll 1
     for (int c0 = c_lo; c0 < c_hi; c0 += 64) {
         uint32_t oa[32], ob[32];
@@ -268,17 +246,19 @@ __device__ __forceinline__ void epilogue_o_tma(const AttnArgs &a, int qrow0, int
         stage_o_box<32>(boxes, quarter, lane, c0, oa, inv, f32);
         stage_o_box<32>(boxes, quarter, lane, c0 + 32, ob, inv, f32);
         fence_proxy_async();
-        __syncwarp();
-        if (issuer)
-            for (int cb = c0 / boxc; cb < (c0 + 64) / boxc; ++cb) {
-                const uint32_t src = smem_addr(boxes + (cb * 4 + quarter) * kOutBox);
-                if (omode == OUT_TMA_ROWS)
-                    tma_store_5d(omap, src, cb * boxc, row0 % a.group, g, row0 / a.group, b);
-                else
-                    tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM) + quarter * 32);
-            }
+        asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+        // the one (bf16) or two (f32) 128-row boxes of these 64 columns, one per issuing warp
+        const int cb = c0 / boxc + quarter;
+        if (lane == 0 && rows_valid > 0 && cb < (c0 + 64) / boxc) {
+            const uint32_t src = smem_addr(boxes + cb * 4 * kOutBox);
+            if (omode == OUT_TMA_ROWS)
+                tma_store_5d(omap, src, cb * boxc, qrow0 % a.group, g, qrow0 / a.group, b);
+            else
+                tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM));
+            issued = true;
+        }
     }
-    if (issuer) {
+    if (issued) {
         bulk_commit_group();
         bulk_wait_group_read0();
     }
@@ -299,11 +279,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // The epilogue's store route for this call (OUT_*), and the tensor map it stores through.
-// With key splits: the f32 workspace as (head_dim, unit * 128 + row), 32 x 32 boxes. Otherwise the
-// output [B, Tq, Hq, D] as (head_dim, head in group, KV head, token, batch) with boxes of 32 query
-// rows: min(group, 32) heads x max(1, 32 / group) tokens, which needs a group dividing 128 (then a
-// quarter's rows never straddle the end of the call's tokens unless the map clips them). Other
-// shapes keep the thread-store epilogue.
+// With key splits: the f32 workspace as (head_dim, unit * 128 + row), 32 x 128 boxes. Otherwise the
+// output [B, Tq, Hq, D] as (head_dim, head in group, KV head, token, batch) with boxes of 128 query
+// rows: min(group, 128) heads x max(1, 128 / group) tokens, which needs a group dividing 128 (then
+// the map clips exactly the rows past the call's tokens). Other shapes keep the thread-store
+// epilogue.
 int make_out_map(const AttnArgs &a, int D, int64_t units, CUtensorMap *map) {
     std::memset(map, 0, sizeof(*map));
     const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
@@ -311,10 +291,10 @@ int make_out_map(const AttnArgs &a, int D, int64_t units, CUtensorMap *map) {
     const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     if (a.n_splits > 1) {
         const int64_t rows = units * a.n_splits * kBM;
-        if (D % 32 || rows > INT_MAX || ((uintptr_t)a.ws_o & 15)) return OUT_THREADS;
+        if (D % 64 || rows > INT_MAX || ((uintptr_t)a.ws_o & 15)) return OUT_THREADS;
         const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
         const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
-        const cuuint32_t box[2] = {32, 32};
+        const cuuint32_t box[2] = {32, (cuuint32_t)kBM};
         return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.ws_o, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
@@ -323,13 +303,13 @@ int make_out_map(const AttnArgs &a, int D, int64_t units, CUtensorMap *map) {
     }
     const bool f32 = a.out_dtype == EKV_DTYPE_F32;
     const int es = f32 ? 4 : 2, boxc = f32 ? 32 : 64;
-    if (D % boxc || a.group <= 0 || kBM % a.group || ((uintptr_t)a.out & 15)) return OUT_THREADS;
+    if (D % 64 || a.group <= 0 || kBM % a.group || ((uintptr_t)a.out & 15)) return OUT_THREADS;
     const cuuint64_t dims[5] = {(cuuint64_t)D, (cuuint64_t)a.group, (cuuint64_t)a.pool.kv_heads,
                                 (cuuint64_t)a.q_tokens, (cuuint64_t)a.n_batch};
     const cuuint64_t strides[4] = {(cuuint64_t)D * es, (cuuint64_t)a.group * D * es, (cuuint64_t)a.q_heads * D * es,
                                    (cuuint64_t)a.q_tokens * a.q_heads * D * es};
-    const cuuint32_t box[5] = {(cuuint32_t)boxc, (cuuint32_t)std::min(a.group, 32), 1,
-                               (cuuint32_t)std::max(1, 32 / a.group), 1};
+    const cuuint32_t box[5] = {(cuuint32_t)boxc, (cuuint32_t)std::min(a.group, kBM), 1,
+                               (cuuint32_t)std::max(1, kBM / a.group), 1};
     return enc(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, a.out, dims, strides,
                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS

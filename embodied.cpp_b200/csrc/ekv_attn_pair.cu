@@ -574,7 +574,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         // this warp's columns of its lane quarter -> swizzled boxes -> copy engine
         if (r == 0 && h == 0) TRACE(14);
         epilogue_o_tma(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem, quarter, lane,
-                       tmem + lane_base + (uint32_t)C::O_COL, h * DH, (h + 1) * DH, have_o, inv, f32, unit);
+                       tmem + lane_base + (uint32_t)C::O_COL, h * DH, (h + 1) * DH, have_o, inv, f32, unit, 2 + h);
         if (r == 0 && h == 0) TRACE(15);
         return;
     }

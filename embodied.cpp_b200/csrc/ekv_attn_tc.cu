@@ -655,7 +655,7 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
     if (omode != OUT_THREADS) {
         // this warp's columns [h * D/2, (h + 1) * D/2) of its lane quarter -> swizzled boxes -> copy engine
         epilogue_o_tma(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem + C::OFF_K, quarter, lane,
-                       tmem + lane_base + (uint32_t)C::O_COL, h * DH, (h + 1) * DH, have_o, inv, f32, unit);
+                       tmem + lane_base + (uint32_t)C::O_COL, h * DH, (h + 1) * DH, have_o, inv, f32, unit, 2 + h);
         return;
     }
     uint8_t *orow = (smem + C::OFF_K) + r * C::OSTR;
@@ -1106,26 +1106,10 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
                     wml[1] = have_o ? l : 0.0f;
                 }
             }
-            constexpr int EC = (D % 32 == 0) ? 32 : 16;  // columns per TMEM load
-#pragma unroll 2
-            for (int c0 = 0; c0 < D; c0 += EC) {
-                uint32_t rr[32];
-                if (have_o) {
-                    if constexpr (EC == 32) {
-                        tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), rr);
-                    } else {
-                        uint32_t (&r16)[16] = *reinterpret_cast<uint32_t (*)[16]>(rr);
-                        tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), r16);
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < EC; ++i) rr[i] = 0u;
-                }
-                stage_o_box<EC>(smem + C::OFF_K, warp, lane, c0, rr, inv, f32);
-            }
-            const int boxc = f32 ? 32 : 64;
-            store_o_boxes(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, &omap, omode, smem + C::OFF_K, warp, 0,
-                          (D + boxc - 1) / boxc, boxc, unit);
+            // the host picks a copy-engine route only for head dims that are whole 64-column blocks
+            if constexpr (D % 64 == 0)
+                epilogue_o_tma(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, &omap, omode, smem + C::OFF_K, warp, lane,
+                               tmem + lane_base + (uint32_t)C::O_COL, 0, D, have_o, inv, f32, unit, 1);
         } else if (a.n_splits > 1) {
             const int64_t unit = (((int64_t)pl.b * a.pool.kv_heads + pl.g) * n_qtiles + pl.qt) * a.n_splits + pl.split;
             float *wo = a.ws_o + (unit * kBM + r) * D;
