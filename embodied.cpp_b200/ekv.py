@@ -59,13 +59,18 @@ class AttnParams(C.Structure):
                 ("span_begin", C.c_void_p), ("span_end", C.c_void_p)]
 
 
+class Tensor(C.Structure):
+    """ekv_tensor: a ggml-ordered strided device tensor (ne[0] fastest, nb in bytes)."""
+    _fields_ = [("data", C.c_void_p), ("type", C.c_int32), ("ne", C.c_int64 * 4), ("nb", C.c_int64 * 4)]
+
+
 # Every symbol include/ekv.h declares; tests check that the library exports all of them.
 EXPORTED = [
     "ekv_pool_create", "ekv_pool_destroy", "ekv_pool_get_info", "ekv_pool_status", "ekv_pool_sync",
     "ekv_seq_create", "ekv_seq_free", "ekv_seq_resize", "ekv_seq_set_blocks", "ekv_seq_evict_front",
     "ekv_seq_get", "ekv_append", "ekv_append_suffix", "ekv_gather", "ekv_gather_suffix",
     "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
-    "ekv_strerror", "ekv_attention_noalloc",
+    "ekv_strerror", "ekv_attention_noalloc", "ekv_flash_attn_ext",
 ]
 NOALLOC_SCRATCH_BYTES = 16 << 20  # EKV_NOALLOC_SCRATCH_BYTES
 
@@ -96,6 +101,7 @@ def _load():
         "ekv_attention": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, vp], C.c_int),
         "ekv_attention_algo": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, i32, vp], C.c_int),
         "ekv_attention_noalloc": ([vp, C.POINTER(AttnParams), vp, vp, vp], C.c_int),
+        "ekv_flash_attn_ext": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 3 + [C.POINTER(Tensor), vp], C.c_int),
         "ekv_version": ([], C.c_char_p),
         "ekv_strerror": ([C.c_int], C.c_char_p),
     }
@@ -238,6 +244,39 @@ class Pool:
         ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
         check(lib.ekv_attention_algo(self.h, C.byref(params), _ptr(q), _ptr(out), _ptr(workspace),
                                      ws_bytes, algo, _stream(stream)), "ekv_attention")
+
+
+_TORCH_DTYPES = {"torch.float32": DTYPE_F32, "torch.float16": DTYPE_F16, "torch.bfloat16": DTYPE_BF16}
+
+
+def ggml_view(t) -> Tensor:
+    """Describe a torch tensor (up to 4-D, any strides) as ekv_tensor in ggml order: the torch shape
+    reversed, so a [B, H, T, D] tensor is ne = {D, T, H, B} and nb = its strides in bytes."""
+    if t.dim() > 4:
+        raise ValueError("at most 4 dimensions")
+    dt = _TORCH_DTYPES.get(str(t.dtype))
+    if dt is None:
+        raise ValueError(f"unsupported dtype {t.dtype}")
+    shape = [1] * (4 - t.dim()) + list(t.shape)
+    strides = [0] * (4 - t.dim()) + list(t.stride())
+    es = t.element_size()
+    g = Tensor()
+    g.data = t.data_ptr()
+    g.type = dt
+    for i in range(4):
+        g.ne[i] = shape[3 - i]
+        g.nb[i] = strides[3 - i] * es
+    return g
+
+
+def flash_attn_ext(q, k, v, mask, dst, *, scale, max_bias=0.0, logit_softcap=0.0, stream=None):
+    """ggml_flash_attn_ext on torch tensors given in reversed ggml order: q [B, Hq, Tq, D],
+    k [Bk, Hkv, Tk, D], v [Bk, Hkv, Tk, Dv], mask [Mb, Mh, >=Tq, >=Tk] (or None) and the f32
+    result dst [B, Tq, Hq, Dv]; any of them may be a permuted or sliced view."""
+    gm = None if mask is None else C.byref(ggml_view(mask))
+    check(lib.ekv_flash_attn_ext(C.byref(ggml_view(q)), C.byref(ggml_view(k)), C.byref(ggml_view(v)), gm,
+                                 scale, max_bias, logit_softcap, C.byref(ggml_view(dst)), _stream(stream)),
+          "ekv_flash_attn_ext")
 
 
 def version() -> str:

@@ -212,6 +212,30 @@ int ekv_attention_algo(ekv_pool *pool, const ekv_attn_params *p, const void *q, 
                        void *workspace, size_t workspace_bytes, int32_t algo,
                        ekv_stream_t stream);
 
+/* ---- ggml op surface: GGML_OP_FLASH_ATTN_EXT on strided device tensors ----
+ * Replaces ggml_flash_attn_ext (models/hy_vla.cpp:376-378, :439-441, :460, :492, :859 (GQA, mask);
+ * models/lingbot_va.cpp:1263-1266) for a ggml backend that routes the op here: the tensors keep
+ * ggml's order (ne[0] fastest) and byte strides, so permuted views are passed as they are.
+ *   q    {D,  Tq, Hq,  B}     EKV_DTYPE_F32 / F16 / BF16
+ *   k    {D,  Tk, Hkv, Bk}    same types; Hq % Hkv == 0 and B % Bk == 0 (head h reads KV head
+ *   v    {Dv, Tk, Hkv, Bk}    h / (Hq / Hkv), batch b reads b / (B / Bk))
+ *   mask {>= Tk, >= Tq, Mh, Mb} or NULL: F16 or F32 additive mask; row i of query i, broadcast
+ *        over heads (h % Mh) and batch (b % Mb)
+ *   dst  {Dv, Hq, Tq, B}      EKV_DTYPE_F32, any strides (the op's own result is contiguous)
+ * score = scale * q.k, or logit_softcap * tanh(scale * q.k / logit_softcap) when logit_softcap != 0;
+ * then + slope(h) * mask (slope = 1 when max_bias == 0, else the ALiBi slope of head h; needs a
+ * mask); softmax over keys in f32; rows whose every score is -inf give 0. D <= 512, Dv <= 256.
+ * This is the op-surface shim: the paged pool and ekv_attention are the tensor-core hot path. */
+typedef struct ekv_tensor {
+    void *data;     /* device pointer */
+    int32_t type;   /* EKV_DTYPE_F32, EKV_DTYPE_F16 or EKV_DTYPE_BF16 */
+    int64_t ne[4];
+    int64_t nb[4];  /* bytes; nb[0] = element size for rows of consecutive elements */
+} ekv_tensor;
+int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask,
+                       float scale, float max_bias, float logit_softcap, const ekv_tensor *dst,
+                       ekv_stream_t stream);
+
 const char *ekv_version(void);
 const char *ekv_strerror(int code);
 

@@ -190,3 +190,56 @@ def attention(q, k, v, seqs, mask: Mask, scale: float, dense_mask=None, precisio
 
 def cache_attention_run(args: CacheArgs, n_threads: int) -> int:
     return lib().ekvo_cache_attention_run(C.byref(args), n_threads)
+
+
+def alibi_slopes(n_head: int, max_bias: float) -> np.ndarray:
+    """ALiBi slope of each head as ggml computes it for soft_max_ext / flash_attn_ext (llama.cpp
+    b9016, ggml-cpu ops.cpp): n_head_log2 = 2^floor(log2(n_head)), m0 = 2^(-max_bias/n_head_log2),
+    m1 = 2^(-max_bias/2/n_head_log2); head h < n_head_log2 gets m0^(h+1), the rest
+    m1^(2(h-n_head_log2)+1); every slope is 1 when max_bias == 0."""
+    if max_bias <= 0.0:
+        return np.ones(n_head, np.float64)
+    n_log2 = 1 << int(np.floor(np.log2(n_head)))
+    m0 = 2.0 ** (-max_bias / n_log2)
+    m1 = 2.0 ** (-(max_bias / 2.0) / n_log2)
+    h = np.arange(n_head)
+    return np.where(h < n_log2, m0 ** (h + 1), m1 ** (2 * (h - n_log2) + 1))
+
+
+def flash_attn_ext(q, k, v, mask=None, *, scale, max_bias=0.0, logit_softcap=0.0):
+    """GGML_OP_FLASH_ATTN_EXT restated in float64 (ggml_flash_attn_ext and its CPU kernel,
+    llama.cpp b9016 `ggml/src/ggml.c` and `ggml-cpu/ops.cpp`, an absent dependency pinned by the
+    reference's patches/init_third_party.sh:21-22; call sites models/hy_vla.cpp:376-378, :439-441,
+    :492, :859 and models/lingbot_va.cpp:1263-1266).
+
+    Arrays are in reversed ggml order: q [B, Hq, Tq, D], k [Bk, Hkv, Tk, D], v [Bk, Hkv, Tk, Dv],
+    mask [Mb, Mh, >=Tq, >=Tk] or None. Head h reads KV head h // (Hq // Hkv), batch b reads
+    b // (B // Bk); the mask broadcasts as mask[b % Mb, h % Mh]. Each score is
+    scale * q.k (with softcap: softcap * tanh(scale / softcap * q.k)) plus slope(h) * mask; keys whose
+    mask is -inf are skipped; a row with no key left gives 0. Returns dst [B, Tq, Hq, Dv]."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    B, Hq, Tq, _ = q.shape
+    Bk, Hkv, Tk, _ = k.shape
+    Dv = v.shape[3]
+    slopes = alibi_slopes(Hq, max_bias)
+    sc = scale / logit_softcap if logit_softcap != 0.0 else scale
+    out = np.zeros((B, Tq, Hq, Dv), np.float64)
+    for b in range(B):
+        kb = b // (B // Bk)
+        for h in range(Hq):
+            kh = h // (Hq // Hkv)
+            s = (q[b, h] @ k[kb, kh].T) * sc
+            if logit_softcap != 0.0:
+                s = logit_softcap * np.tanh(s)
+            if mask is not None:
+                mv = np.asarray(mask[b % mask.shape[0], h % mask.shape[1], :Tq, :Tk], np.float64)
+                s = np.where(np.isneginf(mv), -np.inf, s + slopes[h] * mv)
+            m = s.max(axis=1, keepdims=True)
+            live = np.isfinite(m)
+            p = np.where(live, np.exp(s - np.where(live, m, 0.0)), 0.0)
+            den = p.sum(axis=1, keepdims=True)
+            o = p @ v[kb, kh]
+            out[b, :, h] = np.where(den > 0, o / np.where(den > 0, den, 1.0), 0.0)
+    return out

@@ -1,0 +1,270 @@
+"""ekv_flash_attn_ext: GGML_OP_FLASH_ATTN_EXT on ggml-strided device tensors.
+
+CPU: the float64 oracle is pinned to the LingBot known-answer vectors and to the pinned
+attention oracle; the C-ABI rejects malformed tensors before any CUDA call (no kernel runs).
+GPU: parity with the oracle on the reference's call shapes (models/hy_vla.cpp:376-378 permuted
+self-attention, :439-441 time attention under hy_mem_causal_mask, :859 GQA with a mask;
+models/lingbot_va.cpp:1263-1266), plus softcap, ALiBi, f16/bf16 inputs, batch broadcast, the
+largest head dims, fully masked rows and strided outputs. Tolerance: max-abs 2e-4 (f32 arithmetic
+against float64; inputs are rounded to their storage type before the oracle sees them).
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+import ekv
+import oracle
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TOL = 2e-4
+
+
+# ---------------------------------------------------------------- oracle pins (CPU)
+
+def test_oracle_matches_lingbot_known_answer():
+    g = np.load(os.path.join(GOLD, "lingbot_smoke.npz"))
+    S, H, D = g["q"].shape
+    dense = np.where(g["mask"].astype(bool), 0.0, -np.inf)[None, None]
+    t = lambda a: np.transpose(a, (1, 0, 2))[None]  # [S, H, D] -> [1, H, S, D]
+    out = oracle.flash_attn_ext(t(g["q"]), t(g["k"]), t(g["v"]), dense, scale=float(g["scale"]))
+    assert np.abs(out[0] - g["ref"]).max() < 1e-12
+
+
+def test_oracle_matches_attention_oracle_gqa_mask():
+    rng = np.random.default_rng(3)
+    B, Tq, Hq, Hkv, D, Lk = 2, 6, 4, 2, 32, 23
+    q, k, v = (rng.standard_normal(sh).astype(np.float32) for sh in
+               ((B, Tq, Hq, D), (B, Lk, Hkv, D), (B, Lk, Hkv, D)))
+    dense = np.where(rng.random((B, Tq, Lk)) < 0.3, -np.inf, 0.0)
+    dense[:, :, 0] = 0.0
+    seqs = oracle.make_seqs([Lk] * B, n_suffix=0)
+    want = oracle.attention(q, k, v, seqs, oracle.make_mask(), 0.25, dense_mask=dense, precision="f64")
+    got = oracle.flash_attn_ext(q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3),
+                                dense[:, None], scale=0.25)
+    assert np.abs(got - want).max() < 1e-12
+
+
+def test_oracle_alibi_and_softcap_rules():
+    s = oracle.alibi_slopes(12, 8.0)
+    np.testing.assert_allclose(s[[0, 7, 8, 11]], [0.5, 2.0 ** -8, 2.0 ** -0.5, 2.0 ** -3.5], rtol=1e-14)
+    assert np.all(oracle.alibi_slopes(5, 0.0) == 1.0)
+    rng = np.random.default_rng(4)
+    q, k, v = (rng.standard_normal((1, 1, 3, 8)) for _ in range(3))
+    got = oracle.flash_attn_ext(q, k, v, scale=0.7, logit_softcap=2.0)
+    s = 2.0 * np.tanh(0.7 / 2.0 * (q[0, 0] @ k[0, 0].T))
+    p = np.exp(s - s.max(1, keepdims=True))
+    assert np.abs(got[0, :, 0] - (p / p.sum(1, keepdims=True)) @ v[0, 0]).max() < 1e-12
+
+
+# ---------------------------------------------------------------- C-ABI validation (CPU)
+
+def fake(ne, type=ekv.DTYPE_F32, nb=None, data=1 << 20):
+    es = 4 if type == ekv.DTYPE_F32 else 2
+    if nb is None:
+        nb = [es]
+        for i in range(3):
+            nb.append(nb[-1] * ne[i])
+    t = ekv.Tensor()
+    t.data, t.type = data, type
+    for i in range(4):
+        t.ne[i], t.nb[i] = ne[i], nb[i]
+    return t
+
+
+def call(q, k, v, m, dst, scale=0.125, max_bias=0.0, softcap=0.0):
+    r = lambda t: None if t is None else C.byref(t)
+    return ekv.lib.ekv_flash_attn_ext(r(q), r(k), r(v), r(m), scale, max_bias, softcap, r(dst), None)
+
+
+def good():
+    return dict(q=fake([64, 5, 8, 2]), k=fake([64, 9, 2, 1]), v=fake([32, 9, 2, 1]),
+                m=fake([16, 8, 1, 1], ekv.DTYPE_F16), dst=fake([32, 8, 5, 2]))
+
+
+@pytest.mark.parametrize("name,patch,code", [
+    ("k head dim", dict(k=fake([48, 9, 2, 1])), ekv.ERR_INVALID_ARG),
+    ("v length", dict(v=fake([32, 8, 2, 1])), ekv.ERR_INVALID_ARG),
+    ("gqa ratio", dict(k=fake([64, 9, 3, 1]), v=fake([32, 9, 3, 1])), ekv.ERR_INVALID_ARG),
+    ("batch ratio", dict(q=fake([64, 5, 8, 3]), dst=fake([32, 8, 5, 3]), k=fake([64, 9, 2, 2]),
+                         v=fake([32, 9, 2, 2])), ekv.ERR_INVALID_ARG),
+    ("dst shape", dict(dst=fake([32, 5, 8, 2])), ekv.ERR_INVALID_ARG),
+    ("dst type", dict(dst=fake([32, 8, 5, 2], ekv.DTYPE_F16)), ekv.ERR_INVALID_ARG),
+    ("mask short", dict(m=fake([8, 8, 1, 1], ekv.DTYPE_F16)), ekv.ERR_INVALID_ARG),
+    ("mask rows", dict(m=fake([16, 4, 1, 1], ekv.DTYPE_F16)), ekv.ERR_INVALID_ARG),
+    ("mask heads", dict(m=fake([16, 8, 3, 1], ekv.DTYPE_F16)), ekv.ERR_INVALID_ARG),
+    ("mask bf16", dict(m=fake([16, 8, 1, 1], ekv.DTYPE_BF16)), ekv.ERR_INVALID_ARG),
+    ("q type", dict(q=fake([64, 5, 8, 2], ekv.DTYPE_Q8_0)), ekv.ERR_INVALID_ARG),
+    ("odd stride", dict(q=fake([64, 5, 8, 2], nb=[4, 258, 1290, 10320])), ekv.ERR_INVALID_ARG),
+    ("misaligned", dict(q=fake([64, 5, 8, 2], data=(1 << 20) + 2)), ekv.ERR_INVALID_ARG),
+    ("null data", dict(k=fake([64, 9, 2, 1], data=0)), ekv.ERR_INVALID_ARG),
+    ("null dst", dict(dst=None), ekv.ERR_INVALID_ARG),
+    ("empty", dict(q=fake([64, 0, 8, 2])), ekv.ERR_INVALID_ARG),
+    ("D too large", dict(q=fake([640, 5, 8, 2]), k=fake([640, 9, 2, 1])), ekv.ERR_UNSUPPORTED),
+    ("Dv too large", dict(v=fake([320, 9, 2, 1]), dst=fake([320, 8, 5, 2])), ekv.ERR_UNSUPPORTED),
+])
+def test_capi_rejects(name, patch, code):
+    a = good()
+    a.update(patch)
+    assert call(a["q"], a["k"], a["v"], a["m"], a["dst"]) == code, name
+
+
+def test_capi_rejects_scalars():
+    a = good()
+    args = (a["q"], a["k"], a["v"], a["m"], a["dst"])
+    assert call(*args, scale=float("nan")) == ekv.ERR_INVALID_ARG
+    assert call(*args, max_bias=-1.0) == ekv.ERR_INVALID_ARG
+    assert call(*args, softcap=float("inf")) == ekv.ERR_INVALID_ARG
+    assert call(a["q"], a["k"], a["v"], None, a["dst"], max_bias=8.0) == ekv.ERR_INVALID_ARG
+
+
+# ---------------------------------------------------------------- GPU parity
+
+def _np(t):
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def run(q, k, v, mask, *, scale, max_bias=0.0, softcap=0.0, dst=None):
+    import torch
+    B, Hq, Tq, _ = q.shape
+    Dv = v.shape[3]
+    if dst is None:
+        dst = torch.full((B, Tq, Hq, Dv), float("nan"), dtype=torch.float32, device="cuda")
+    ekv.flash_attn_ext(q, k, v, mask, dst, scale=scale, max_bias=max_bias, logit_softcap=softcap)
+    torch.cuda.synchronize()
+    want = oracle.flash_attn_ext(_np(q), _np(k), _np(v), None if mask is None else _np(mask),
+                                 scale=scale, max_bias=max_bias, logit_softcap=softcap)
+    return dst, want
+
+
+def causal_f16(n, device):
+    import torch
+    r = torch.arange(n, device=device)
+    return torch.where(r[None, :] <= r[:, None], 0.0, float("-inf")).to(torch.float16)
+
+
+@pytest.mark.gpu
+def test_hy_self_attention_permuted_views():
+    """models/hy_vla.cpp:365-378: q/k/v are column slices of one fused qkv row-major buffer,
+    reshaped to heads and permuted, so every operand is non-contiguous."""
+    import torch
+    torch.manual_seed(0)
+    seq, H, D = 77, 6, 64
+    qkv = torch.randn(seq, 3 * H * D, device="cuda")
+    views = [qkv[:, i * H * D:(i + 1) * H * D].view(seq, H, D).permute(1, 0, 2)[None] for i in range(3)]
+    dst, want = run(*views, None, scale=D ** -0.5)
+    assert np.abs(_np(dst) - want).max() < TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("frames", [1, 3, 9])
+def test_hy_time_attention_causal_mask(frames):
+    """models/hy_vla.cpp:430-441: patches batched in ne[3], a [T, T] F16 causal mask
+    (hy_mem_causal_mask) broadcast over heads and patches."""
+    import torch
+    torch.manual_seed(frames)
+    P, H, D = 20, 4, 64
+    q4, k4, v4 = (torch.randn(frames, P, H, D, device="cuda") for _ in range(3))
+    Q, K, V = (t.permute(1, 2, 0, 3) for t in (q4, k4, v4))  # [P, H, T, D] views
+    mask = causal_f16(frames, "cuda")[None, None]
+    dst, want = run(Q, K, V, mask, scale=D ** -0.5)
+    assert np.abs(_np(dst) - want).max() < TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("hq,hkv", [(8, 1), (8, 2), (16, 16)])
+def test_hy_expert_gqa_mask(hq, hkv):
+    """models/hy_vla.cpp:845-859: GQA heads with an additive F16 mask over the suffix."""
+    import torch
+    torch.manual_seed(hq + hkv)
+    seq, D = 51, 128
+    q = torch.randn(seq, hq, D, device="cuda").permute(1, 0, 2)[None]
+    k = torch.randn(seq, hkv, D, device="cuda").permute(1, 0, 2)[None]
+    v = torch.randn(seq, hkv, D, device="cuda").permute(1, 0, 2)[None]
+    pad = 64  # ggml pads the mask's rows and columns; extra entries are ignored
+    m = torch.zeros(pad, pad, device="cuda")
+    m[:seq, :seq] = torch.where(torch.rand(seq, seq, device="cuda") < 0.25, float("-inf"), 0.0)
+    m[:, 0] = 0.0
+    mask = m.to(torch.float16)[None, None]
+    dst, want = run(q, k, v, mask, scale=D ** -0.5)
+    assert np.abs(_np(dst) - want).max() < TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_half_inputs_and_f32_mask_per_head(dtype):
+    import torch
+    torch.manual_seed(7)
+    dt = torch.float16 if dtype == "f16" else torch.bfloat16
+    B, Hq, Hkv, Tq, Tk, D = 2, 4, 2, 33, 70, 96
+    q = torch.randn(B, Hq, Tq, D, device="cuda").to(dt)
+    k = torch.randn(B, Hkv, Tk, D, device="cuda").to(dt)
+    v = torch.randn(B, Hkv, Tk, D, device="cuda").to(dt)
+    mask = torch.randn(B, Hq, Tq, Tk, device="cuda")
+    mask[..., 5:9] = float("-inf")
+    dst, want = run(q, k, v, mask, scale=0.1)
+    assert np.abs(_np(dst) - want).max() < TOL
+
+
+@pytest.mark.gpu
+def test_softcap_alibi_and_batch_broadcast():
+    import torch
+    torch.manual_seed(11)
+    B, Bk, Hq, Hkv, Tq, Tk, D = 4, 2, 12, 3, 17, 45, 64
+    q = torch.randn(B, Hq, Tq, D, device="cuda")
+    k = torch.randn(Bk, Hkv, Tk, D, device="cuda")
+    v = torch.randn(Bk, Hkv, Tk, D, device="cuda")
+    mask = (-torch.arange(Tk, device="cuda").float().abs()).expand(1, 1, Tq, Tk).contiguous()
+    dst, want = run(q, k, v, mask, scale=0.125, max_bias=8.0, softcap=20.0)
+    assert np.abs(_np(dst) - want).max() < TOL
+    dst, want = run(q, k, v, None, scale=0.125, softcap=5.0)
+    assert np.abs(_np(dst) - want).max() < TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("d,dv,tk", [(512, 256, 33), (256, 256, 1), (40, 24, 31), (64, 128, 300)])
+def test_head_dims_and_key_counts(d, dv, tk):
+    import torch
+    torch.manual_seed(d + dv + tk)
+    q = torch.randn(1, 2, 9, d, device="cuda") * 0.2
+    k = torch.randn(1, 2, tk, d, device="cuda") * 0.2
+    v = torch.randn(1, 2, tk, dv, device="cuda")
+    dst, want = run(q, k, v, None, scale=1.0)
+    assert np.abs(_np(dst) - want).max() < TOL
+
+
+@pytest.mark.gpu
+def test_fully_masked_rows_and_strided_dst():
+    """Rows whose every key is -inf give 0 (the op's S == 0 rule); dst may be a strided view
+    inside a larger buffer, and nothing outside it is written."""
+    import torch
+    torch.manual_seed(5)
+    B, H, Tq, Tk, D = 1, 2, 8, 40, 64
+    q, k, v = (torch.randn(B, H, n, D, device="cuda") for n in (Tq, Tk, Tk))
+    mask = torch.zeros(1, 1, Tq, Tk, device="cuda", dtype=torch.float16)
+    mask[0, 0, 3] = float("-inf")
+    mask[0, 0, 6, :35] = float("-inf")
+    big = torch.full((B, Tq, H + 1, D + 16), 7.0, device="cuda")
+    dst = big[:, :, 1:, 8:8 + D]
+    dst, want = run(q, k, v, mask, scale=0.125, dst=dst)
+    got = _np(dst)
+    assert np.all(got[:, 3] == 0.0)
+    assert np.abs(got - want).max() < TOL
+    rest = big.clone()
+    rest[:, :, 1:, 8:8 + D] = 7.0
+    assert torch.all(rest == 7.0)
+
+
+@pytest.mark.gpu
+def test_lingbot_known_answer_on_gpu():
+    """models/lingbot_va.cpp:1263-1266 shapes from the LingBot smoke vectors, through the op."""
+    import torch
+    g = np.load(os.path.join(GOLD, "lingbot_smoke.npz"))
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda().permute(1, 0, 2)[None]
+    mask = torch.from_numpy(np.where(g["mask"].astype(bool), 0.0, -np.inf).astype(np.float16)).cuda()[None, None]
+    S, H, D = g["q"].shape
+    dst = torch.empty(1, S, H, D, device="cuda")
+    ekv.flash_attn_ext(t(g["q"]), t(g["k"]), t(g["v"]), mask, dst, scale=float(g["scale"]))
+    torch.cuda.synchronize()
+    assert np.abs(dst[0].cpu().numpy() - g["ref"]).max() < float(g["tol"])
