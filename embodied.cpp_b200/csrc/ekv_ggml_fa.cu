@@ -2,8 +2,9 @@
 //
 // The reference builds ggml_flash_attn_ext(Q, K, V, mask, scale, 0, 0) over permuted f32 views
 // (models/hy_vla.cpp:376-378, :439-441, :492, and :859 with GQA and a mask; the causal F16 mask of
-// hy_mem_causal_mask, :627 and :739; models/lingbot_va.cpp:1263-1266). A ggml backend that routes that op to this library passes the
-// tensors as they are: data pointer, type, ggml ne[4] (ne[0] fastest) and byte strides nb[4].
+// hy_mem_causal_mask, :627 and :739; models/lingbot_va.cpp:1263-1266). A ggml backend that
+// routes that op to this library passes the tensors as they are: data pointer, type, ggml ne[4]
+// (ne[0] fastest) and byte strides nb[4].
 // Semantics follow the op: GQA by head (h / (Hq / Hkv)) and batch broadcast, an additive mask
 // broadcast over heads and batch, score = scale * q.k with the optional tanh softcap, the ALiBi
 // slope when max_bias > 0, softmax in f32, and the result laid out as {Dv, Hq, Tq, B}.
@@ -189,7 +190,7 @@ extern "C" int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, cons
     a.has_mask = mask != nullptr;
     if (mask) a.m = fa_view(mask);
     else a.m = FaTensor{};
-    // the op divides the scale by the softcap at creation and multiplies the tanh by it
+    // as the op's compute kernel does: scale / softcap inside the tanh, softcap outside it
     a.softcap = logit_softcap;
     a.scale = logit_softcap != 0.0f ? scale / logit_softcap : scale;
     a.alibi = max_bias > 0.0f;
