@@ -9,6 +9,10 @@
 // broadcast over heads and batch, score = scale * q.k with the optional tanh softcap, the ALiBi
 // slope when max_bias > 0, softmax in f32, and the result laid out as {Dv, Hq, Tq, B}.
 //
+// The pi0.5 expert layer builds the same computation as three ggml ops (models/pi05.cpp:414-418:
+// mul_mat, soft_max_ext, mul_mat over permuted copies); ekv_mul_mat_soft_max_mul_mat takes that triple's
+// operands and result in their own layouts.
+//
 // One warp per query row: the row's q is staged in shared memory as f32, each lane scores one
 // key of a 32-key chunk (reading its K row), the chunk's running max / sum update is a warp
 // reduction, and each lane accumulates Dv/32 output columns over the chunk's V rows. This is the
@@ -161,10 +165,12 @@ FaTensor fa_view(const ekv_tensor *t) {
 }  // namespace
 }  // namespace ekv
 
-extern "C" int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask,
-                                  float scale, float max_bias, float logit_softcap, const ekv_tensor *dst,
-                                  ekv_stream_t stream) {
-    using namespace ekv;
+namespace ekv {
+namespace {
+
+// The op on validated-type tensors in flash_attn_ext order: v {Dv, Tk, Hkv, Bk}, dst {Dv, Hq, Tq, B}.
+int run_flash_attn(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask, float scale,
+                   float max_bias, float logit_softcap, const ekv_tensor *dst, cudaStream_t stream) {
     if (!tensor_ok(q, false) || !tensor_ok(k, false) || !tensor_ok(v, false) || !tensor_ok(dst, true))
         return EKV_ERR_INVALID_ARG;
     if (mask && (!tensor_ok(mask, false) || mask->type == EKV_DTYPE_BF16)) return EKV_ERR_INVALID_ARG;
@@ -201,6 +207,42 @@ extern "C" int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, cons
     a.dst = (uint8_t *)dst->data;
     for (int i = 0; i < 4; ++i) a.dnb[i] = dst->nb[i];
     const dim3 grid((unsigned)((q->ne[1] + kFaWarps - 1) / kFaWarps), (unsigned)q->ne[2], (unsigned)q->ne[3]);
-    flash_attn_ext_kernel<<<grid, kFaWarps * 32, 0, (cudaStream_t)stream>>>(a);
+    flash_attn_ext_kernel<<<grid, kFaWarps * 32, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? EKV_OK : EKV_ERR_CUDA;
+}
+
+// `t` with dimensions i and j exchanged (a permuted view of the same bytes).
+ekv_tensor swap_dims(const ekv_tensor &t, int i, int j) {
+    ekv_tensor r = t;
+    r.ne[i] = t.ne[j];
+    r.ne[j] = t.ne[i];
+    r.nb[i] = t.nb[j];
+    r.nb[j] = t.nb[i];
+    return r;
+}
+
+}  // namespace
+}  // namespace ekv
+
+extern "C" int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask,
+                                  float scale, float max_bias, float logit_softcap, const ekv_tensor *dst,
+                                  ekv_stream_t stream) {
+    return ekv::run_flash_attn(q, k, v, mask, scale, max_bias, logit_softcap, dst, (cudaStream_t)stream);
+}
+
+// mul_mat(K, Q) -> soft_max_ext(kq, mask, scale, max_bias) -> mul_mat(V, attn) of models/pi05.cpp:414-418:
+// the same computation as the fused op with V given keys-fastest ({Tk, Dv, ...}, the permute(1, 2, 0, 3)
+// of :412) and the result in mul_mat order {Dv, Tq, Hq, B} (before the permute of :419-420). Both are
+// views of the caller's bytes with two dimensions exchanged.
+extern "C" int ekv_mul_mat_soft_max_mul_mat(const ekv_tensor *k, const ekv_tensor *q, const ekv_tensor *v,
+                                            const ekv_tensor *mask, float scale, float max_bias, const ekv_tensor *dst,
+                                            ekv_stream_t stream) {
+    using namespace ekv;
+    if (!k || !q || !v || !dst) return EKV_ERR_INVALID_ARG;
+    // mul_mat(V, attn) contracts V's ne[0] with attn's ne[0] = keys; V's heads and batch are K's
+    if (v->ne[0] != k->ne[1] || v->ne[2] != k->ne[2] || v->ne[3] != k->ne[3]) return EKV_ERR_INVALID_ARG;
+    if (dst->ne[0] != v->ne[1] || dst->ne[1] != q->ne[1] || dst->ne[2] != q->ne[2] || dst->ne[3] != q->ne[3])
+        return EKV_ERR_INVALID_ARG;
+    const ekv_tensor vt = swap_dims(*v, 0, 1), dt = swap_dims(*dst, 1, 2);
+    return run_flash_attn(q, k, &vt, mask, scale, max_bias, 0.0f, &dt, (cudaStream_t)stream);
 }

@@ -71,6 +71,7 @@ EXPORTED = [
     "ekv_seq_get", "ekv_append", "ekv_append_suffix", "ekv_gather", "ekv_gather_suffix",
     "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
     "ekv_strerror", "ekv_attention_noalloc", "ekv_flash_attn_ext",
+    "ekv_mul_mat_soft_max_mul_mat",
 ]
 NOALLOC_SCRATCH_BYTES = 16 << 20  # EKV_NOALLOC_SCRATCH_BYTES
 
@@ -102,6 +103,8 @@ def _load():
         "ekv_attention_algo": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, i32, vp], C.c_int),
         "ekv_attention_noalloc": ([vp, C.POINTER(AttnParams), vp, vp, vp], C.c_int),
         "ekv_flash_attn_ext": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 3 + [C.POINTER(Tensor), vp], C.c_int),
+        "ekv_mul_mat_soft_max_mul_mat": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 2 + [C.POINTER(Tensor), vp],
+                                         C.c_int),
         "ekv_version": ([], C.c_char_p),
         "ekv_strerror": ([C.c_int], C.c_char_p),
     }
@@ -277,6 +280,16 @@ def flash_attn_ext(q, k, v, mask, dst, *, scale, max_bias=0.0, logit_softcap=0.0
     check(lib.ekv_flash_attn_ext(C.byref(ggml_view(q)), C.byref(ggml_view(k)), C.byref(ggml_view(v)), gm,
                                  scale, max_bias, logit_softcap, C.byref(ggml_view(dst)), _stream(stream)),
           "ekv_flash_attn_ext")
+
+
+def mul_mat_soft_max_mul_mat(k, q, v, mask, dst, *, scale, max_bias=0.0, stream=None):
+    """The ggml triple mul_mat(K, Q) -> soft_max_ext -> mul_mat(V, .) on torch tensors in reversed ggml
+    order: k [Bk, Hkv, Tk, D], q [B, Hq, Tq, D], v [Bk, Hkv, Dv, Tk] (keys fastest), mask
+    [Mb, Mh, >=Tq, >=Tk] or None, f32 dst [B, Hq, Tq, Dv]."""
+    gm = None if mask is None else C.byref(ggml_view(mask))
+    check(lib.ekv_mul_mat_soft_max_mul_mat(C.byref(ggml_view(k)), C.byref(ggml_view(q)), C.byref(ggml_view(v)), gm,
+                                           scale, max_bias, C.byref(ggml_view(dst)), _stream(stream)),
+          "ekv_mul_mat_soft_max_mul_mat")
 
 
 def version() -> str:

@@ -236,6 +236,19 @@ int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, const ekv_tenso
                        float scale, float max_bias, float logit_softcap, const ekv_tensor *dst,
                        ekv_stream_t stream);
 
+/* The ggml triple of models/pi05.cpp:414-418 (also models/smolvla.cpp and models/hy_vla.cpp expert
+ * layers): kq = mul_mat(K, Q) at F32 precision, attn = soft_max_ext(kq, mask, scale, max_bias),
+ * kqv = mul_mat(V, attn), fused into one call for a backend that recognises the pattern:
+ *   k    {D,  Tk, Hkv, Bk}   q {D, Tq, Hq, B}   (head h reads K/V head h / (Hq / Hkv))
+ *   v    {Tk, Dv, Hkv, Bk}   keys fastest: the ggml_permute(V, 1, 2, 0, 3) of :412
+ *   mask {>= Tk, >= Tq, Mh, Mb} or NULL (F16 or F32), as for ekv_flash_attn_ext
+ *   dst  {Dv, Tq, Hq, B}     EKV_DTYPE_F32, any strides: kqv before the permute of :419-420
+ * Types, strides and limits as ekv_flash_attn_ext (no softcap). Rows whose every key is masked give
+ * 0 (ggml's soft_max would give NaN there; the reference masks never produce such rows). */
+int ekv_mul_mat_soft_max_mul_mat(const ekv_tensor *k, const ekv_tensor *q, const ekv_tensor *v,
+                                 const ekv_tensor *mask, float scale, float max_bias, const ekv_tensor *dst,
+                                 ekv_stream_t stream);
+
 const char *ekv_version(void);
 const char *ekv_strerror(int code);
 

@@ -268,3 +268,57 @@ def test_lingbot_known_answer_on_gpu():
     ekv.flash_attn_ext(t(g["q"]), t(g["k"]), t(g["v"]), mask, dst, scale=float(g["scale"]))
     torch.cuda.synchronize()
     assert np.abs(dst[0].cpu().numpy() - g["ref"]).max() < float(g["tol"])
+
+
+# ---------------------------------------------------------------- the mul_mat / soft_max_ext / mul_mat triple
+
+def call_triple(k, q, v, m, dst, scale=0.0625, max_bias=0.0):
+    r = lambda t: None if t is None else C.byref(t)
+    return ekv.lib.ekv_mul_mat_soft_max_mul_mat(r(k), r(q), r(v), r(m), scale, max_bias, r(dst), None)
+
+
+def good_triple():
+    # pi0.5 shapes (models/pi05.cpp:410-418): K {256, 866, 1}, Q {256, 50, 8}, V {866, 256, 1}
+    return dict(k=fake([256, 866, 1, 1]), q=fake([256, 50, 8, 1]), v=fake([866, 256, 1, 1]),
+                m=fake([866, 50, 1, 1]), dst=fake([256, 50, 8, 1]))
+
+
+@pytest.mark.parametrize("name,patch", [
+    ("v keys", dict(v=fake([865, 256, 1, 1]))),
+    ("v heads", dict(v=fake([866, 256, 2, 1]))),
+    ("dst order", dict(dst=fake([256, 8, 50, 1]))),
+    ("dst dv", dict(dst=fake([128, 50, 8, 1]))),
+    ("k dim", dict(k=fake([128, 866, 1, 1]))),
+    ("mask short", dict(m=fake([800, 50, 1, 1]))),
+    ("null v", dict(v=None)),
+])
+def test_triple_capi_rejects(name, patch):
+    a = good_triple()
+    a.update(patch)
+    assert call_triple(a["k"], a["q"], a["v"], a["m"], a["dst"]) == ekv.ERR_INVALID_ARG, name
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("contig_v", [True, False])
+@pytest.mark.parametrize("masked", [False, True])
+def test_triple_pi05_layer(contig_v, masked):
+    """models/pi05.cpp:404-418 on one layer-step: K/V = concat(cached prefix, 50 new rows), Q 50 x 8
+    heads over 1 KV head, D = 256, scale 1/16; V keys-fastest as the permute of :412 makes it (a
+    contiguous copy) or as a strided view; the f32 mask of :815 (zeros) or SmolVLA-style padding."""
+    import torch
+    torch.manual_seed(21 + contig_v + 2 * masked)
+    Tq, Hq, D, Lp = 50, 8, 256, 816
+    Tk = Lp + Tq
+    kf = (torch.randn(Tk, D, device="cuda") * 0.5).to(torch.bfloat16).float()
+    vf = (torch.randn(Tk, D, device="cuda") * 0.5).to(torch.bfloat16).float()
+    q = (torch.randn(1, Hq, Tq, D, device="cuda") * 0.5).to(torch.bfloat16).float()
+    k = kf[None, None]                                         # ggml {D, Tk, 1, 1}
+    v = vf.t().contiguous()[None, None] if contig_v else vf.t()[None, None]  # ggml {Tk, D, 1, 1}
+    mask = torch.zeros(1, 1, Tq, Tk, device="cuda")
+    if masked:
+        mask[..., 790:Lp] = float("-inf")                      # padded text positions
+    dst = torch.full((1, Hq, Tq, D), float("nan"), device="cuda")
+    ekv.mul_mat_soft_max_mul_mat(k, q, v, mask, dst, scale=1.0 / 16)
+    torch.cuda.synchronize()
+    want = oracle.flash_attn_ext(_np(q), _np(k), _np(vf)[None, None], _np(mask), scale=1.0 / 16)
+    assert np.abs(_np(dst) - want.transpose(0, 2, 1, 3)).max() < TOL
