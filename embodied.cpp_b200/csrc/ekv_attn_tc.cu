@@ -72,8 +72,11 @@ struct TcCfg {
     static constexpr int OFF_RAW = 2 * NSTAGE * KV_BYTES;
     static constexpr int OFF_RAW_V = OFF_RAW + NRAW_K * RAW_HALF;
     static constexpr int OFF_BAR = OFF_RAW_V + NRAW_V * RAW_HALF;
-    static constexpr int OFF_XCH = OFF_BAR + 256;  // softmax pair exchange: row maxima [2][2][128], sums [2][128]
-    static constexpr int OFF_TBL = OFF_XCH + 6 * kBM * 4;
+    // softmax warps per TMEM lane quarter, each owning 32 columns of a tile (1: one thread per row,
+    // all BN columns; Q8_0 at BN = 128 keeps that form, its dequantisers use the threads)
+    static constexpr int SPLIT_H = BN == 64 ? 2 : (Q8 ? 1 : 4);
+    static constexpr int OFF_XCH = OFF_BAR + 256;  // softmax exchange: row maxima [2][H][128], sums [H][128]
+    static constexpr int OFF_TBL = OFF_XCH + 3 * (SPLIT_H > 2 ? SPLIT_H : 2) * kBM * 4;
     // tile base pointers of the split's block-table entries (whatever fits, at most 512)
     static constexpr int TBL_ROOM = (232448 - 1024 - OFF_TBL) / 8;
     static constexpr int TBL = TBL_ROOM > 512 ? 512 : TBL_ROOM;
@@ -81,9 +84,8 @@ struct TcCfg {
     // Q staging: rows of D*2 bytes whose 16-byte units are XOR-swizzled by the row (q_stage_off), so
     // both the row-major stores and the per-row reads of a warp hit distinct bank groups
     static constexpr int QSTR = D * 2;
-    // BN = 64: two softmax warps per TMEM lane quarter, each owning half of the tile's columns
-    static constexpr bool SPLIT = BN == 64;
-    static constexpr int SMW = SPLIT ? 8 : 4;  // softmax warps
+    static constexpr bool SPLIT = SPLIT_H > 1;
+    static constexpr int SMW = 4 * SPLIT_H;  // softmax warps
     static constexpr int MMA_WARP = SMW;
     static constexpr int TMA_WARP = SMW + 1;  // K feeder; TMA_WARP + 1 feeds V
     static constexpr int DQ_WARP0 = SMW + 3;
@@ -499,18 +501,18 @@ __device__ __forceinline__ bool pair_sync(uint32_t xbar, int use, volatile int *
     return mbar_wait(xbar, (uint32_t)use & 1u, abort, kWaitBudget);
 }
 
-// ---- softmax / epilogue with two warps per TMEM lane quarter (BN = 64): warp w owns query row
-// (w & 3) * 32 + lane and S columns [h * 32, h * 32 + 32) of every tile, h = w >> 2. Per tile the
-// two warps swap their masked chunk maxima through shared memory; P for the 32 keys goes back as
-// 16 packed columns [h * 16, h * 16 + 16) of the tile's S buffer (both warps have read S by then).
-// The O rescale and the epilogue split O's columns the same way. ----
+// ---- softmax / epilogue with H = BN / 32 warps per TMEM lane quarter (2 at BN = 64, 4 at BN = 128):
+// warp w owns query row (w & 3) * 32 + lane and S columns [h * 32, h * 32 + 32) of every tile,
+// h = w >> 2. Per tile the H warps of a quarter swap their masked chunk maxima through shared memory;
+// P for the 32 keys goes back as 16 packed columns [h * 16, h * 16 + 16) of the tile's S buffer (all
+// H warps have read S by then). The O rescale and the epilogue split O's columns among them. ----
 template <int D, bool Q8>
 __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan &pl, uint8_t *smem, uint32_t bar0,
                                                    volatile int *abort, uint32_t tmem, uint32_t lane_base, int n,
                                                    int n_qtiles, const void *omap, int omode) {
     using C = TcCfg<D, Q8>;
-    constexpr int BN = C::BN, DH = D / 2;
-    static_assert(BN == 64, "split softmax: 32 columns per warp");
+    constexpr int BN = C::BN, H = C::SPLIT_H;
+    static_assert(BN == 32 * H, "split softmax: 32 columns per warp");
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int h = warp >> 2, quarter = warp & 3;
@@ -520,8 +522,8 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
     const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
     const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
     const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
-    float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][2 half][128 rows]
-    float *xl = xmax + 4 * kBM;                   // [2 half][128 rows]
+    float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][H][128 rows]
+    float *xl = xmax + 2 * H * kBM;               // [H][128 rows]
     const uint32_t xbar = bar(BAR_XCH + quarter);
     int uses = 0;
     float m_used = -INFINITY, l = 0.0f;
@@ -555,11 +557,14 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
             for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], ((vb >> i) & 1u) ? __uint_as_float(rr[i]) : -INFINITY);
         }
         const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-        xmax[((jj & 1) * 2 + h) * kBM + r] = cm;
+        xmax[((jj & 1) * H + h) * kBM + r] = cm;
         if (!(ok = pair_sync(xbar, uses++, abort))) break;
-        const float rmax = fmaxf(cm, xmax[((jj & 1) * 2 + (h ^ 1)) * kBM + r]);  // raw scores (scale > 0)
-        // a new maximum more than 2^8 above the one in use: rescale l and O (both warps of the pair
-        // see the same row maxima, so they take this branch together)
+        float rmax = cm;  // raw scores (scale > 0)
+#pragma unroll
+        for (int o = 0; o < H; ++o)
+            if (o != h) rmax = fmaxf(rmax, xmax[((jj & 1) * H + o) * kBM + r]);
+        // a new maximum more than 2^8 above the one in use: rescale l and O (the H warps of a
+        // quarter see the same row maxima, so they take this branch together)
         if (__any_sync(0xffffffffu, rmax > (m_used + 8.0f) * inv_scale_log2)) {
             const float m_tile = rmax * a.scale_log2;
             float alpha = 1.0f;
@@ -580,7 +585,7 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
                     break;
                 tc_fence_after();
 #pragma unroll 1
-                for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 16) {
+                for (int c0 = h * 16; c0 < D; c0 += 16 * H) {
                     uint32_t o16[16];
                     tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), o16);
 #pragma unroll
@@ -627,14 +632,18 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
         if (!ok) fail_timeout(a, abort, 4);
         tc_fence_after();
     }
-    // ---- epilogue: row sum over both halves, then this warp's D/2 columns of O ----
+    // ---- epilogue: row sum over the H warps, then this warp's columns of O ----
     if (r == 0 && h == 0) TRACE(10);
     xl[h * kBM + r] = l;
     if (ok && !pair_sync(xbar, uses++, abort)) {
         ok = false;
         fail_timeout(a, abort, 7);
     }
-    const float l_row = ok ? xl[r] + xl[kBM + r] : 0.0f;  // same order in both warps
+    float l_row = 0.0f;  // same order in every warp
+    if (ok) {
+#pragma unroll
+        for (int o = 0; o < H; ++o) l_row += xl[o * kBM + r];
+    }
     const bool have_o = ok && n > 0;
     // O -> shared staging row r -> the softmax warps write whole rows with consecutive 16-byte lanes
     // (the K/V stages are idle once the last P.V has landed). Without key splits: O / l as bf16 or
@@ -653,30 +662,42 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
         }
     }
     if (omode != OUT_THREADS) {
-        // this warp's columns [h * D/2, (h + 1) * D/2) of its lane quarter -> swizzled boxes -> copy engine
-        epilogue_o_tma(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem + C::OFF_K, quarter, lane,
-                       tmem + lane_base + (uint32_t)C::O_COL, h * DH, (h + 1) * DH, have_o, inv, f32, unit, 2 + h);
+        // the host picks a copy-engine route only for head dims that are whole 64-column blocks:
+        // EH column ranges of D / EH (a multiple of 64), one per group of four quarter warps
+        constexpr int EH = (D % 64 == 0) ? (D / 64 < H ? D / 64 : H) : 1;
+        if constexpr (D % 64 == 0) {
+            if (h < EH)
+                epilogue_o_tma(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem + C::OFF_K, quarter, lane,
+                               tmem + lane_base + (uint32_t)C::O_COL, h * (D / EH), (h + 1) * (D / EH), have_o, inv,
+                               f32, unit, 2 + h);
+        }
         return;
     }
     uint8_t *orow = (smem + C::OFF_K) + r * C::OSTR;
+    constexpr int EC = (D % 32 == 0) ? 32 : 16;  // columns per TMEM load
 #pragma unroll 1
-    for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
+    for (int c0 = h * EC; c0 < D; c0 += EC * H) {
         uint32_t o32[32];
         if (have_o) {
-            tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
+            if constexpr (EC == 32) {
+                tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
+            } else {
+                uint32_t (&o16)[16] = *reinterpret_cast<uint32_t (*)[16]>(o32);
+                tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), o16);
+            }
         } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o32[i] = 0u;
+            for (int i = 0; i < EC; ++i) o32[i] = 0u;
         }
         if (f32) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
+            for (int i = 0; i < EC; i += 4)
                 *(float4 *)(orow + (c0 + i) * 4) =
                     make_float4(__uint_as_float(o32[i]) * inv, __uint_as_float(o32[i + 1]) * inv,
                                 __uint_as_float(o32[i + 2]) * inv, __uint_as_float(o32[i + 3]) * inv);
         } else {
 #pragma unroll
-            for (int i0 = 0; i0 < 32; i0 += 8) {
+            for (int i0 = 0; i0 < EC; i0 += 8) {
                 uint32_t w[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -750,7 +771,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
             mbar_init(bar(BAR_P_FULL + s), C::SMW);
         }
         mbar_init(bar(BAR_DONE), 1);
-        for (int q = 0; q < 4; ++q) mbar_init(bar(BAR_XCH + q), 2);
+        for (int q = 0; q < 4; ++q) mbar_init(bar(BAR_XCH + q), C::SPLIT_H);
         mbar_init(bar(BAR_Q_READY), C::SMW);
         *abort = 0;
         mbar_init_fence();
@@ -775,8 +796,8 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
     const uint32_t tmem = *tmem_holder;
     const uint32_t lane_base = ((uint32_t)((warp & 3) * 32)) << 16;
     if (warp < C::SMW) {
-        // row (warp & 3) * 32 + lane; with SPLIT the two warps of a lane quarter take half the columns each
-        const int h = C::SPLIT ? warp >> 2 : 0, nh = C::SPLIT ? 2 : 1;
+        // row (warp & 3) * 32 + lane; with SPLIT the H warps of a lane quarter share its column blocks
+        const int h = C::SPLIT ? warp >> 2 : 0, nh = C::SPLIT_H;
         q_to_tmem<D, Q8>(smem + C::OFF_V, (warp & 3) * 32 + lane, tmem + lane_base + C::Q_COL, h * (D / 16) / nh,
                          (h + 1) * (D / 16) / nh);
         tmem_wait_st();
