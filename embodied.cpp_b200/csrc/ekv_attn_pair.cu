@@ -189,6 +189,48 @@ __device__ __forceinline__ const uint8_t *pair_ptr_of(const AttnArgs &a, const P
     return blk < 0 ? nullptr : a.pool.prefix + prefix_tile_index(a.pool, a.layer, blk, 0, pl.g) * a.pool.tile_bytes;
 }
 
+// This CTA's part of suffix tile j read straight from the caller's row-major bf16 K/V
+// ([n_batch][suffix_len][kv_heads][256]) into the swizzled operand stage: K rows [32r, 32r + 32) of
+// the tile (kv = 0), or V columns [128r, 128r + 128) of its 64 rows (kv = 1); rows past suffix_len
+// are zero. `nthr` threads (tid < nthr) share the 1024 16-byte units, four loads in flight each;
+// TO_F16 converts to the f16 operands of Q8_0 pools.
+template <bool TO_F16>
+__device__ __forceinline__ void pair_suffix_direct(const AttnArgs &a, const PairPlan &pl, int j, int kv, uint8_t *sDst,
+                                                   int tid, int nthr) {
+    constexpr int BN = 64, D = 256, KH_ROWS = 32, VH_COLS = 128, W = 128;
+    const int s_base = (j - pl.np_tiles) * BN;
+    const int upr = kv == 0 ? D / 8 : VH_COLS / 8;
+    const int row_base = kv == 0 ? pl.rank * KH_ROWS : 0;
+    const int col_base = kv == 0 ? 0 : pl.rank * VH_COLS;
+    const int dD = kv == 0 ? D : VH_COLS;
+    const int64_t row_stride = (int64_t)a.pool.kv_heads * D;
+    const uint16_t *src = (kv ? a.v_sfx : a.k_sfx) + ((int64_t)pl.b * a.suffix_len * a.pool.kv_heads + pl.g) * D +
+                          col_base;
+    constexpr int UNITS = 1024;  // 32 rows x 32 units (K) = 64 rows x 16 units (V)
+#pragma unroll 1
+    for (int u0 = tid; u0 < UNITS; u0 += 4 * nthr) {
+        uint4 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int u = u0 + i * nthr;
+            const int row = u / upr, dl = (u - row * upr) * 8;
+            const int srow = s_base + row_base + row;
+            v[i] = make_uint4(0, 0, 0, 0);
+            if (u < UNITS && srow < a.suffix_len) v[i] = __ldg((const uint4 *)(src + srow * row_stride + dl));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int u = u0 + i * nthr;
+            if (u >= UNITS) break;
+            const int row = u / upr, dl = (u - row * upr) * 8;
+            uint4 w = v[i];
+            if (TO_F16)
+                w = make_uint4(bf16x2_to_f16x2(w.x), bf16x2_to_f16x2(w.y), bf16x2_to_f16x2(w.z), bf16x2_to_f16x2(w.w));
+            *(uint4 *)(sDst + tile_elem_off(row, dl, dD, W)) = w;
+        }
+    }
+}
+
 // ---- bf16 feeder. K half (kv = 0): tile rows [32r, 32r + 32), in runs of whole blocks (or of 32
 // rows of a larger block), one copy per run into the K stage. V half (kv = 1): the two 1 KB column
 // chunks [2r, 2r + 2) of each of the tile's 8 row groups, one 2 KB copy per row group into the V
@@ -199,6 +241,14 @@ __device__ __forceinline__ void pair_produce_bf16(const AttnArgs &a, const PairP
     constexpr int BN = C::BN, RB = C::D * 2;
     const PoolView &p = a.pool;
     const bool suffix = j >= pl.np_tiles;
+    if (suffix && a.k_sfx) {
+        // the caller's row-major suffix: loaded and swizzled by the warp, then one plain arrival
+        pair_suffix_direct<false>(a, pl, j, kv, sDst, lane, 32);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_full);
+        return;
+    }
     const int key0 = suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN;  // tile's first key / suffix row
     // copy `lane`: source row range (8-row groups) and destination offset
     int n_cp;        // copies this part needs
@@ -384,6 +434,10 @@ __device__ __forceinline__ void pair_convert_suffix(const AttnArgs &a, const Pai
                                                     uint8_t *sDst, int dtid) {
     using C = PairCfg<true>;
     constexpr int BN = C::BN, D = C::D;
+    if (a.k_sfx) {
+        pair_suffix_direct<true>(a, pl, j, kv, sDst, dtid, kDq);
+        return;
+    }
     const PoolView &p = a.pool;
     const int s_base = (j - pl.np_tiles) * BN;
     const uint8_t *src = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, kv, pl.g) * p.suffix_tile_bytes;
@@ -998,6 +1052,7 @@ int launch_attention_pair(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms) 
     const cudaError_t e = q8 ? cudaLaunchKernelEx(&cfg, attn_pair_kernel<true>, a, n_qtiles, omap, omode)
                              : cudaLaunchKernelEx(&cfg, attn_pair_kernel<false>, a, n_qtiles, omap, omode);
     if (e != cudaSuccess) return EKV_ERR_CUDA;
+    note_launches(1);
     if (a.n_splits > 1) return launch_merge_splits(a, n_qtiles, s);
     return EKV_OK;
 }

@@ -128,7 +128,9 @@ int launch_attention_simt(const AttnArgs &a, cudaStream_t s) {
     const int64_t grid = (n_rows + kWarps - 1) / kWarps;
     if (grid > 0x7fffffff) return EKV_ERR_INVALID_ARG;
     attn_simt_kernel<<<(unsigned)grid, kWarps * 32, 0, s>>>(a);
-    return cudaGetLastError() == cudaSuccess ? EKV_OK : EKV_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
+    note_launches(1);
+    return EKV_OK;
 }
 
 }  // namespace ekv

@@ -1331,10 +1331,12 @@ int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
     const int omode = make_out_map(a, D, units, &omap);
     attn_tc_kernel<D, Q8><<<grid, C::THREADS, C::SMEM, s>>>(a, n_qtiles, omap, omode);
     if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
+    note_launches(1);
     if (a.n_splits > 1) {
         merge_splits_kernel<D><<<dim3(n_qtiles * (kBM / kMergeWarps), a.pool.kv_heads, a.n_batch), kMergeWarps * 32, 0, s>>>(
             a, n_qtiles);
         if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
+        note_launches(1);
     }
     return EKV_OK;
 }
@@ -1389,7 +1391,9 @@ int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s) {
         case 256: merge_splits_kernel<256><<<grid, kMergeWarps * 32, 0, s>>>(a, n_qtiles); break;
         default: return EKV_ERR_UNSUPPORTED;
     }
-    return cudaGetLastError() == cudaSuccess ? EKV_OK : EKV_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
+    note_launches(1);
+    return EKV_OK;
 }
 
 int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k) {

@@ -246,6 +246,7 @@ int launch_append(const PoolView &p, int layer, int n_batch, const int32_t *seq_
         append_q8_kernel<<<dim3(grid_for(units), n_batch), kThreads, 0, s>>>(
             p, layer, seq_ids, dst_pos, n_rows, src_row, max_rows, (const uint4 *)k, (const uint4 *)v);
     }
+    note_launches(1);
     return launch_status();
 }
 
@@ -256,6 +257,7 @@ int launch_append_suffix(const PoolView &p, int layer, int n_batch, const int32_
     const int64_t units = (int64_t)n_rows * 2 * p.kv_heads * (p.head_dim / 8);
     append_suffix_kernel<<<dim3(grid_for(units), n_batch), kThreads, 0, s>>>(p, layer, seq_ids, n_rows,
                                                                              (const uint4 *)k, (const uint4 *)v);
+    note_launches(1);
     return launch_status();
 }
 
@@ -272,6 +274,7 @@ int launch_gather(const PoolView &p, int layer, int seq, int pos0, int n_rows, i
         gather_q8_kernel<<<grid_for(units), kThreads, 0, s>>>(p, layer, seq, pos0, n_rows,
                                                              format == EKV_GATHER_F32, k_out, v_out);
     }
+    note_launches(1);
     return launch_status();
 }
 
@@ -282,6 +285,7 @@ int launch_gather_suffix(const PoolView &p, int layer, int seq, int n_rows, int 
     const int64_t units = (int64_t)n_rows * 2 * p.kv_heads * (p.head_dim / 8);
     gather_bf16_kernel<<<grid_for(units), kThreads, 0, s>>>(p, layer, seq, 0, n_rows, 1,
                                                            format == EKV_GATHER_F32, k_out, v_out);
+    note_launches(1);
     return launch_status();
 }
 

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -38,9 +39,16 @@ int set_device(const ekv_pool *p) {
 
 }  // namespace
 
+namespace ekv {
+static std::atomic<unsigned long long> g_launches{0};
+void note_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+}  // namespace ekv
+
 extern "C" {
 
 const char *ekv_version(void) { return "ekv 0.1 (sm_100a)"; }
+
+uint64_t ekv_launch_count(void) { return ekv::g_launches.load(std::memory_order_relaxed); }
 
 const char *ekv_strerror(int code) {
     switch (code) {
@@ -432,6 +440,37 @@ int ekv_attention_algo(ekv_pool *p, const ekv_attn_params *prm, const void *q, v
 int ekv_attention(ekv_pool *p, const ekv_attn_params *prm, const void *q, void *out, void *workspace,
                   size_t workspace_bytes, ekv_stream_t stream) {
     return ekv_attention_algo(p, prm, q, out, workspace, workspace_bytes, EKV_ALGO_TC, stream);
+}
+
+int ekv_append_suffix_attention(ekv_pool *p, const ekv_attn_params *prm, const void *k_suffix,
+                                const void *v_suffix, const void *q, void *out, void *workspace,
+                                size_t workspace_bytes, ekv_stream_t stream) {
+    if (!p || !prm || !k_suffix || !v_suffix) return EKV_ERR_INVALID_ARG;
+    if (prm->layer < 0 || prm->layer >= p->cfg.n_layers || prm->n_batch < 0 || prm->suffix_len < 0)
+        return EKV_ERR_INVALID_ARG;
+    if (prm->suffix_len > p->cfg.suffix_tokens) return EKV_ERR_RANGE;
+    if (((uintptr_t)k_suffix | (uintptr_t)v_suffix) & 15) return EKV_ERR_INVALID_ARG;
+    if (p->cfg.suffix_tokens == 0) return EKV_ERR_INVALID_ARG;
+    ekv::AttnArgs a;
+    if (const int rc = fill_attn_args(p, prm, q, out, a)) return rc;
+    if (workspace && ((uintptr_t)workspace & 15)) return EKV_ERR_INVALID_ARG;
+    if (const int e = set_device(p)) return e;
+    const cudaStream_t s = (cudaStream_t)stream;
+    if (p->cfg.head_dim == 256) {
+        // the CTA-pair kernel reads the suffix from the caller's buffers; the slot is not written
+        a.k_sfx = (const uint16_t *)k_suffix;
+        a.v_sfx = (const uint16_t *)v_suffix;
+    } else if (prm->suffix_len > 0) {
+        const int rc = ekv::launch_append_suffix(p->view, prm->layer, prm->n_batch, prm->seq_ids, prm->suffix_len,
+                                                 k_suffix, v_suffix, s);
+        if (rc) return rc;
+    }
+    const size_t need = ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens);
+    if (workspace && need && workspace_bytes >= need) {
+        a.ws_o = (float *)workspace;
+        a.n_splits = 0;
+    }
+    return ekv::launch_attention_tc(a, s, ekv::TcKernel::Auto);
 }
 
 }  // extern "C"

@@ -25,6 +25,7 @@
 
 #include "../../include/ekv.h"
 #include "ekv_device.cuh"
+#include "ekv_internal.h"
 
 namespace ekv {
 namespace {
@@ -208,7 +209,9 @@ int run_flash_attn(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v
     for (int i = 0; i < 4; ++i) a.dnb[i] = dst->nb[i];
     const dim3 grid((unsigned)((q->ne[1] + kFaWarps - 1) / kFaWarps), (unsigned)q->ne[2], (unsigned)q->ne[3]);
     flash_attn_ext_kernel<<<grid, kFaWarps * 32, 0, stream>>>(a);
-    return cudaGetLastError() == cudaSuccess ? EKV_OK : EKV_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
+    note_launches(1);
+    return EKV_OK;
 }
 
 // `t` with dimensions i and j exchanged (a permuted view of the same bytes).

@@ -43,7 +43,14 @@ struct AttnArgs {
     int32_t n_splits;
     float *ws_o;      // [units][128][D] unnormalised partial outputs
     float *ws_ml;     // [units][128][2] running max (log2 domain) and sum
+    // this layer-step's suffix K/V read straight from the caller's [n_batch][suffix_len][kv_heads]
+    // [head_dim] bf16 buffers instead of the pool's suffix slot (CTA-pair kernel only), or null
+    const uint16_t *k_sfx, *v_sfx;
 };
+
+// Kernels launched by this library in this process (ekv_launch_count); every launch site adds its
+// launches after cudaLaunch* returned.
+void note_launches(int n);
 
 int launch_append(const PoolView &p, int layer, int n_batch, const int32_t *seq_ids,
                   const int32_t *dst_pos, const int32_t *n_rows, const int32_t *src_row,

@@ -71,7 +71,7 @@ EXPORTED = [
     "ekv_seq_get", "ekv_append", "ekv_append_suffix", "ekv_gather", "ekv_gather_suffix",
     "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
     "ekv_strerror", "ekv_attention_noalloc", "ekv_flash_attn_ext",
-    "ekv_mul_mat_soft_max_mul_mat",
+    "ekv_mul_mat_soft_max_mul_mat", "ekv_append_suffix_attention", "ekv_launch_count",
 ]
 NOALLOC_SCRATCH_BYTES = 16 << 20  # EKV_NOALLOC_SCRATCH_BYTES
 
@@ -102,10 +102,12 @@ def _load():
         "ekv_attention": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, vp], C.c_int),
         "ekv_attention_algo": ([vp, C.POINTER(AttnParams), vp, vp, vp, C.c_size_t, i32, vp], C.c_int),
         "ekv_attention_noalloc": ([vp, C.POINTER(AttnParams), vp, vp, vp], C.c_int),
+        "ekv_append_suffix_attention": ([vp, C.POINTER(AttnParams), vp, vp, vp, vp, vp, C.c_size_t, vp], C.c_int),
         "ekv_flash_attn_ext": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 3 + [C.POINTER(Tensor), vp], C.c_int),
         "ekv_mul_mat_soft_max_mul_mat": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 2 + [C.POINTER(Tensor), vp],
                                          C.c_int),
         "ekv_version": ([], C.c_char_p),
+        "ekv_launch_count": ([], C.c_uint64),
         "ekv_strerror": ([C.c_int], C.c_char_p),
     }
     for name, (args, res) in sig.items():
@@ -247,6 +249,14 @@ class Pool:
         ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
         check(lib.ekv_attention_algo(self.h, C.byref(params), _ptr(q), _ptr(out), _ptr(workspace),
                                      ws_bytes, algo, _stream(stream)), "ekv_attention")
+
+    def append_suffix_attention(self, params: AttnParams, k_suffix, v_suffix, q, out, workspace=None, stream=None):
+        """ekv_append_suffix_attention: this layer-step's suffix K/V ([n_batch][suffix_len][kv_heads]
+        [head_dim] bf16) into the slots, then attention, in one call."""
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        check(lib.ekv_append_suffix_attention(self.h, C.byref(params), _ptr(k_suffix), _ptr(v_suffix), _ptr(q),
+                                              _ptr(out), _ptr(workspace), ws_bytes, _stream(stream)),
+              "ekv_append_suffix_attention")
 
 
 _TORCH_DTYPES = {"torch.float32": DTYPE_F32, "torch.float16": DTYPE_F16, "torch.bfloat16": DTYPE_BF16}

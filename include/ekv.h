@@ -212,6 +212,18 @@ int ekv_attention_algo(ekv_pool *pool, const ekv_attn_params *p, const void *q, 
                        void *workspace, size_t workspace_bytes, int32_t algo,
                        ekv_stream_t stream);
 
+/* One layer-step of the denoise loop: attention whose suffix keys are this step's k_suffix /
+ * v_suffix ([n_batch][suffix_len][kv_heads][head_dim] bf16, 16-byte aligned) -- the concat of
+ * models/pi05.cpp:406-407 and the attention of :410-421 in one call. Same output as
+ * ekv_append_suffix(pool, p->layer, p->n_batch, p->seq_ids, p->suffix_len, k_suffix, v_suffix)
+ * followed by ekv_attention(pool, p, q, out, ...). At head_dim 256 the attention reads the suffix
+ * straight from k_suffix / v_suffix and the pool's suffix slot is left as it was; at other head dims
+ * the two calls run (the slot then holds this suffix). Use ekv_append_suffix where the slot must
+ * hold it (ekv_gather_suffix). Nothing is enqueued when the arguments are invalid. */
+int ekv_append_suffix_attention(ekv_pool *pool, const ekv_attn_params *p, const void *k_suffix,
+                                const void *v_suffix, const void *q, void *out, void *workspace,
+                                size_t workspace_bytes, ekv_stream_t stream);
+
 /* ---- ggml op surface: GGML_OP_FLASH_ATTN_EXT on strided device tensors ----
  * Replaces ggml_flash_attn_ext (models/hy_vla.cpp:376-378, :439-441, :460, :492, :859 (GQA, mask);
  * models/lingbot_va.cpp:1263-1266) for a ggml backend that routes the op here: the tensors keep
@@ -250,6 +262,9 @@ int ekv_mul_mat_soft_max_mul_mat(const ekv_tensor *k, const ekv_tensor *q, const
                                  ekv_stream_t stream);
 
 const char *ekv_version(void);
+/* Kernels this library has launched in this process, on every device (a diagnostic: the difference
+ * across a region of calls is the launches they made). */
+uint64_t ekv_launch_count(void);
 const char *ekv_strerror(int code);
 
 #ifdef __cplusplus

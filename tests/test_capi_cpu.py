@@ -117,3 +117,22 @@ def test_data_ops_refuse_host_only_pool():
     pool.seq_resize(s, 32)
     rc = ekv.lib.ekv_gather(pool.h, 0, s, 0, 4, 0, C.c_void_p(16), C.c_void_p(16), None)
     assert rc == ekv.ERR_UNSUPPORTED
+
+
+def test_append_suffix_attention_validates_before_enqueueing():
+    pool = host_pool()
+    s = pool.seq_create()
+    pool.seq_resize(s, 32)
+    ids = C.c_void_p(16)
+    prm = ekv.AttnParams(0, 1, 50, 8, 0.0625, 0, 0, 0, 0, 0, 50, ekv.DTYPE_BF16, 1, 0, ids.value,
+                         None, None, None, None)
+    f = ekv.lib.ekv_append_suffix_attention
+    buf = C.c_void_p(1 << 20)
+    assert f(pool.h, C.byref(prm), None, buf, buf, buf, None, 0, None) == ekv.ERR_INVALID_ARG
+    assert f(pool.h, C.byref(prm), C.c_void_p((1 << 20) + 8), buf, buf, buf, None, 0, None) == ekv.ERR_INVALID_ARG
+    prm.suffix_len = 51
+    assert f(pool.h, C.byref(prm), buf, buf, buf, buf, None, 0, None) == ekv.ERR_RANGE
+    prm.suffix_len, prm.layer = 50, 7
+    assert f(pool.h, C.byref(prm), buf, buf, buf, buf, None, 0, None) == ekv.ERR_INVALID_ARG
+    prm.layer, prm.q_heads = 0, 0
+    assert f(pool.h, C.byref(prm), buf, buf, buf, buf, None, 0, None) == ekv.ERR_INVALID_ARG

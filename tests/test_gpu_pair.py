@@ -101,3 +101,48 @@ def test_pair_bf16_output_pi05_batch():
     want = oracle_attention(f, 0, q, scale=1 / 16)
     check(got, want, TOL[ekv.DTYPE_Q8_0])
     assert np.abs(got - single).max() <= 2e-2
+
+
+@pytest.mark.parametrize("dtype", [ekv.DTYPE_BF16, ekv.DTYPE_Q8_0])
+@pytest.mark.parametrize("B,ws,d", [(6, False, 256), (2, True, 256), (3, False, 128)])
+def test_append_suffix_attention_matches_two_calls(dtype, B, ws, d):
+    """ekv_append_suffix_attention gives the same output, bit for bit, as ekv_append_suffix followed
+    by ekv_attention, over several layer-steps with a fresh suffix each time, with and without key
+    splits. At head_dim 256 the pair kernel reads the suffix from the caller's buffers (the slot,
+    clobbered beforehand, stays as it was); at head_dim 128 the call appends into the slot first."""
+    gen = torch.Generator().manual_seed(40 + B)
+    plens = [int(x) for x in np.random.default_rng(B).integers(200, 820, size=B)]
+    T, Hq = 50, 8
+    f = Filled(dtype=dtype, B=B, prefix_lens=plens, Hkv=1, D=d, suffix_len=T, n_layers=2, seed=40 + B)
+    prm = [f.pool.attention_params(layer=l, seq_ids=f.seq_ids, q_tokens=T, q_heads=Hq, scale=d ** -0.5,
+                                   suffix_len=T, out_dtype=ekv.DTYPE_F32) for l in range(2)]
+    wsb = None
+    if ws:
+        n = f.pool.workspace_size(prm[0])
+        wsb = torch.empty(max(n, 16), dtype=torch.uint8, device="cuda")
+    for step in range(3):
+        for l in range(2):
+            sk = bf16_randn(gen, (B, T, 1, d)).cuda()
+            sv = bf16_randn(gen, (B, T, 1, d)).cuda()
+            q = bf16_randn(gen, (B, T, Hq, d)).cuda()
+            two = torch.empty((B, T, Hq, d), dtype=torch.float32, device="cuda")
+            one = torch.empty_like(two)
+            f.pool.append_suffix(l, f.seq_ids, sk, sv)
+            f.pool.attention(prm[l], q, two, workspace=wsb)
+            ks_two = torch.empty((T, 1, d), dtype=torch.bfloat16, device="cuda")
+            vs_two = torch.empty_like(ks_two)
+            f.pool.gather_suffix(l, f.seqs[0], T, ekv.GATHER_NATIVE, ks_two, vs_two)
+            # clobber the slot so that the fused call must write it again
+            f.pool.append_suffix(l, f.seq_ids, torch.zeros_like(sk), torch.zeros_like(sv))
+            f.pool.append_suffix_attention(prm[l], sk, sv, q, one, workspace=wsb)
+            ks_one = torch.empty_like(ks_two)
+            vs_one = torch.empty_like(ks_two)
+            f.pool.gather_suffix(l, f.seqs[0], T, ekv.GATHER_NATIVE, ks_one, vs_one)
+            torch.cuda.synchronize()
+            assert f.pool.status() == 0
+            assert torch.equal(one, two), (step, l)
+            if d == 256:
+                assert not torch.any(ks_one.view(torch.int16)) and not torch.any(vs_one.view(torch.int16))
+            else:
+                assert torch.equal(ks_one.view(torch.int16), ks_two.view(torch.int16))
+                assert torch.equal(vs_one.view(torch.int16), vs_two.view(torch.int16))
