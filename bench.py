@@ -455,7 +455,9 @@ def main():
 def run_e2e(wl, args, world, barrier):
     """Same metric through the C-ABI with host buffers: every step copies its inputs from
     pinned host memory (prefix K/V of all layers, per-call suffix K/V and Q) and reads every
-    call's output back, on separate copy streams overlapped with compute per layer-call."""
+    call's output back. Per-call inputs and outputs move in chunks of one denoise step's 18
+    layer-calls (one copy per tensor and chunk), double-buffered on separate copy streams so that
+    the copies overlap the compute of the neighbouring chunk."""
     import torch
     dev = wl.q.device
     hp = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
@@ -465,13 +467,14 @@ def run_e2e(wl, args, world, barrier):
     h_sk.copy_(wl.sk)
     h_sv.copy_(wl.sv)
     h_q.copy_(wl.q)
-    # device staging: two slots per per-call tensor
+    N, G = wl.n_calls, N_LAYERS
+    assert N % G == 0
+    # device staging: two chunk slots per per-call tensor
     d_pk, d_pv = torch.empty_like(wl.pk), torch.empty_like(wl.pv)
-    slot = lambda t: torch.empty((2,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
+    slot = lambda t: torch.empty((2, G) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
     d_sk, d_sv, d_q, d_out = slot(wl.sk), slot(wl.sv), slot(wl.q), slot(wl.out)
     s_c = torch.cuda.current_stream()
     s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    N = wl.n_calls
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_done = [torch.cuda.Event() for _ in range(2)]
     ev_out = [torch.cuda.Event() for _ in range(2)]
@@ -489,29 +492,31 @@ def run_e2e(wl, args, world, barrier):
             wl.pool.append(l, wl.seq_ids, wl.zeros, wl.n_rows, wl.src_row, int(wl.plen.max()), d_pk[l], d_pv[l],
                            stream=s_c)
 
-        def stage(c):
-            i = c & 1
+        def stage(k):  # chunk k = calls [k * G, (k + 1) * G)
+            i, cs = k & 1, slice(k * G, (k + 1) * G)
             with torch.cuda.stream(s_h2d):
-                s_h2d.wait_event(ev_done[i])  # slot free once call c-2 finished reading it
-                d_sk[i].copy_(h_sk[c], non_blocking=True)
-                d_sv[i].copy_(h_sv[c], non_blocking=True)
-                d_q[i].copy_(h_q[c], non_blocking=True)
+                s_h2d.wait_event(ev_done[i])  # slot free once chunk k-2 finished reading it
+                d_sk[i].copy_(h_sk[cs], non_blocking=True)
+                d_sv[i].copy_(h_sv[cs], non_blocking=True)
+                d_q[i].copy_(h_q[cs], non_blocking=True)
                 ev_in[i].record(s_h2d)
 
+        n_chunks = N // G
         stage(0)
-        for c in range(N):
-            i = c & 1
-            if c + 1 < N:
-                stage(c + 1)
+        for k in range(n_chunks):
+            i = k & 1
+            if k + 1 < n_chunks:
+                stage(k + 1)
             s_c.wait_event(ev_in[i])
-            s_c.wait_event(ev_out[i])  # output slot drained (call c-2)
-            l = c % N_LAYERS
-            wl.pool.append_suffix_attention(wl.params[l], d_sk[i], d_sv[i], d_q[i], d_out[i], workspace=wl.ws,
-                                            stream=s_c)
+            s_c.wait_event(ev_out[i])  # output slot drained (chunk k-2)
+            for g in range(G):
+                l = (k * G + g) % N_LAYERS
+                wl.pool.append_suffix_attention(wl.params[l], d_sk[i, g], d_sv[i, g], d_q[i, g], d_out[i, g],
+                                                workspace=wl.ws, stream=s_c)
             ev_done[i].record(s_c)
             with torch.cuda.stream(s_d2h):
                 s_d2h.wait_event(ev_done[i])
-                h_out[c].copy_(d_out[i], non_blocking=True)
+                h_out[k * G:(k + 1) * G].copy_(d_out[i], non_blocking=True)
                 ev_out[i].record(s_d2h)
 
     for _ in range(args.warmup):
