@@ -50,6 +50,18 @@ CONFIGS = {
                                "18 layers x 10 steps, 50 suffix, 8q/1kv x 256"),
 }
 
+# BASELINE configs 3 and 4 (parity shapes; measured by `--config groot_b128` / `lingbot_b1`)
+OTHER_CONFIGS = {
+    "groot_b128": dict(kind="groot", batch=128,
+                       desc="GR00T-N1.7 DiT action head: 16 layers (even: cross-attention of 17 queries to a cached "
+                            "300-token backbone K/V, image span [0,256) and text [256,300) masks alternating; odd: "
+                            "self-attention among the 17), 4 denoise steps, 32 heads x 48 (MHA), bf16, batch 128"),
+    "lingbot_b1": dict(kind="lingbot", batch=1,
+                       desc="LingBot-VA rollout: 30 layers, 24 heads x 128 (MHA), 16 chunks of 1560 video tokens "
+                            "appended to a paged bf16 cache (64-token blocks, chunk stride 1600), block-causal "
+                            "window of 8 chunks with oldest-chunk eviction, one episode per GPU"),
+}
+
 N_LAYERS, N_STEPS, TQ, HQ, HKV, D, BT = 18, 10, 50, 8, 1, 256, 16
 SCALE = 1.0 / 16.0
 
@@ -206,6 +218,225 @@ class Pi05Workload:
 
 
 # ------------------------------------------------------------------------------------------
+# BASELINE configs 3 (GR00T) and 4 (LingBot): parity shapes, timed with the same contract
+# ------------------------------------------------------------------------------------------
+class GrootWorkload:
+    """GR00T DiT action head over a cached backbone: per step, 16 layer-calls x 4 denoise steps;
+    even layers cross-attend 17 queries to the layer's 300-token backbone K/V (image span or text
+    mask, alternating), odd layers self-attend among the 17 (their K/V passed with the call)."""
+    L, STEPS, T, H, DH, P, IMG = 16, 4, 17, 32, 48, 300, 256
+    graphable = True
+
+    def __init__(self, B, device):
+        import torch
+        import ekv
+        self.ekv, self.B = ekv, B
+        self.dtype = ekv.DTYPE_BF16
+        L, T, H, DH, P = self.L, self.T, self.H, self.DH, self.P
+        need = (P + 15) // 16
+        self.pool = ekv.Pool(device=device, dtype=self.dtype, block_tokens=16, n_blocks=B * need, kv_heads=H,
+                             head_dim=DH, n_layers=L, max_seqs=B, max_blocks_per_seq=need, suffix_tokens=T)
+        self.seqs = []
+        for _ in range(B):
+            s = self.pool.seq_create()
+            self.pool.seq_resize(s, P)
+            self.seqs.append(s)
+        self.pool.sync()
+        dev = f"cuda:{device}"
+        t = lambda a: torch.tensor(np.asarray(a, np.int32), device=dev)
+        self.seq_ids = t(self.seqs)
+        self.zeros, self.n_rows = t(np.zeros(B)), t(np.full(B, P))
+        self.src_row = t(np.arange(B) * P)
+        g = torch.Generator(device=dev).manual_seed(3)
+        rn = lambda *shape: (torch.randn(shape, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        self.n_calls = L * self.STEPS
+        self.pk, self.pv = rn(L // 2, B * P, H, DH), rn(L // 2, B * P, H, DH)
+        self.sk, self.sv = rn(self.n_calls, B, T, H, DH), rn(self.n_calls, B, T, H, DH)
+        self.q = rn(self.n_calls, B, T, H, DH)
+        self.out = torch.empty((self.n_calls, B, T, H, DH), dtype=torch.bfloat16, device=dev)
+        span_b, span_e = t(np.zeros(B)), t(np.full(B, self.IMG))
+        self.params = []
+        flop = byts = 0.0
+        for l in range(L):
+            if l % 2 == 0:
+                flag = ekv.MASK_SPAN_ONLY if l % 4 == 0 else ekv.MASK_SPAN_EXCLUDE
+                keys = self.IMG if flag == ekv.MASK_SPAN_ONLY else P - self.IMG
+                self.params.append(self.pool.attention_params(layer=l, seq_ids=self.seq_ids, q_tokens=T, q_heads=H,
+                                                              scale=DH ** -0.5, mask_flags=flag, span_begin=span_b,
+                                                              span_end=span_e, out_dtype=ekv.DTYPE_BF16))
+            else:
+                keys = T
+                self.params.append(self.pool.attention_params(layer=l, seq_ids=self.seq_ids, q_tokens=T, q_heads=H,
+                                                              scale=DH ** -0.5, suffix_len=T, use_prefix=False,
+                                                              out_dtype=ekv.DTYPE_BF16))
+            flop += 4.0 * B * T * H * keys * DH
+            byts += B * (2 * T * H * DH * 2 + 2 * keys * H * DH * 2)  # Q + O, visible K/V
+        self.flop_per_call = flop / L
+        self.bytes_per_call = byts / L
+        self.qtok_per_step = B * T * self.n_calls
+        self.ws = None
+
+    def step_prefix(self, stream):
+        for c in range(self.L // 2):  # the cross layers' backbone K/V
+            self.pool.append(2 * c, self.seq_ids, self.zeros, self.n_rows, self.src_row, self.P, self.pk[c],
+                             self.pv[c], stream=stream)
+
+    def step_calls(self, stream):
+        for c in range(self.n_calls):
+            l = c % self.L
+            if l % 2 == 0:
+                self.pool.attention(self.params[l], self.q[c], self.out[c], stream=stream)
+            else:
+                self.pool.append_suffix_attention(self.params[l], self.sk[c], self.sv[c], self.q[c], self.out[c],
+                                                  stream=stream)
+
+
+class LingbotWorkload:
+    """LingBot-VA world-action rollout for one episode: per step, 16 chunks; per chunk the window
+    slides (oldest chunk evicted once 8 are held), then each of 30 layers appends the chunk's 1560
+    K/V rows and attends the chunk's queries over the window (block-causal)."""
+    L, CHUNKS, CT, STRIDE, WIN, H, DH = 30, 16, 1560, 1600, 8, 24, 128
+    graphable = False  # the window moves on the host between chunks
+
+    def __init__(self, B, device):
+        import torch
+        import ekv
+        assert B == 1, "one episode per GPU"
+        self.ekv, self.B = ekv, B
+        self.dtype = ekv.DTYPE_BF16
+        blocks_per_chunk = self.STRIDE // 64
+        self.bpc = blocks_per_chunk
+        self.pool = ekv.Pool(device=device, dtype=self.dtype, block_tokens=64,
+                             n_blocks=(self.WIN + 1) * blocks_per_chunk, kv_heads=self.H, head_dim=self.DH,
+                             n_layers=self.L, max_seqs=1, max_blocks_per_seq=(self.WIN + 1) * blocks_per_chunk,
+                             suffix_tokens=0)
+        self.seq = self.pool.seq_create()
+        dev = f"cuda:{device}"
+        t = lambda a: torch.tensor(np.asarray(a, np.int32), device=dev)
+        self.seq_ids = t([self.seq])
+        self.n_rows, self.src_row = t([self.CT]), t([0])
+        self.dst = [t([w * self.STRIDE]) for w in range(self.WIN)]
+        g = torch.Generator(device=dev).manual_seed(4)
+        rn = lambda *shape: (torch.randn(shape, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        # per (chunk, layer) K/V and Q would be 16 x 30 x 3 x 9.6 MB; 4 distinct sets cycle (> L2)
+        self.NSET = 4
+        self.k = rn(self.NSET, self.L, self.CT, self.H, self.DH)
+        self.v = rn(self.NSET, self.L, self.CT, self.H, self.DH)
+        self.q = rn(self.NSET, self.L, self.CT, self.H, self.DH)
+        self.out = torch.empty((self.NSET, self.L, self.CT, self.H, self.DH), dtype=torch.bfloat16, device=dev)
+        self.params = [[self.pool.attention_params(layer=l, seq_ids=self.seq_ids, q_tokens=self.CT, q_heads=self.H,
+                                                   scale=self.DH ** -0.5, mask_flags=ekv.MASK_BLOCK_CAUSAL,
+                                                   chunk_tokens=self.CT, chunk_stride=self.STRIDE,
+                                                   window_chunks=self.WIN, q_chunk0=w, out_dtype=ekv.DTYPE_BF16)
+                        for l in range(self.L)] for w in range(self.WIN)]
+        ws = max(self.pool.workspace_size(p) for p in self.params[self.WIN - 1])
+        self.ws = torch.empty(ws, dtype=torch.uint8, device=dev) if ws else None
+        self.n_calls = self.CHUNKS * self.L
+        flop = 0.0
+        for c in range(self.CHUNKS):
+            held = min(c, self.WIN - 1) + 1
+            flop += self.L * 4.0 * self.CT * self.H * (held * self.CT) * self.DH
+        self.flop_per_call = flop / self.n_calls
+        self.bytes_per_call = 0.0
+        for c in range(self.CHUNKS):
+            held = min(c, self.WIN - 1) + 1
+            self.bytes_per_call += self.L * (2 * self.CT * self.H * self.DH * 2 + 2 * held * self.CT * self.H * self.DH * 2)
+        self.bytes_per_call /= self.n_calls
+        self.qtok_per_step = self.CT * self.n_calls
+
+    def step_prefix(self, stream):
+        self.pool.seq_resize(self.seq, 0)  # a fresh episode
+        self.pool.sync(stream)
+
+    def step_calls(self, stream):
+        for c in range(self.CHUNKS):
+            held = min(c, self.WIN - 1) + 1
+            if c >= self.WIN:
+                self.pool.seq_evict_front(self.seq, self.bpc)
+            self.pool.seq_resize(self.seq, held * self.STRIDE)
+            self.pool.sync(stream)
+            w = held - 1
+            for l in range(self.L):
+                i = (c * self.L + l) % self.NSET
+                self.pool.append(l, self.seq_ids, self.dst[w], self.n_rows, self.src_row, self.CT, self.k[i, l],
+                                 self.v[i, l], stream=stream)
+                self.pool.attention(self.params[w][l], self.q[i, l], self.out[i, l], workspace=self.ws, stream=stream)
+
+
+def run_other(args, cfg):
+    """Configs 3 and 4 on one GPU: the same JSON contract as the default config, without the
+    end-to-end and CPU legs (the headline metric is config 2's)."""
+    import torch
+    torch.cuda.set_device(0)
+    cls = GrootWorkload if cfg["kind"] == "groot" else LingbotWorkload
+    wl = cls(cfg["batch"], 0)
+    stream = torch.cuda.current_stream()
+    wl.step_prefix(stream)
+    wl.step_calls(stream)
+    torch.cuda.synchronize()
+    if wl.graphable:
+        g_pre, g_calls = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        n0 = wl.ekv.lib.ekv_launch_count()
+        with torch.cuda.graph(g_pre):
+            wl.step_prefix(torch.cuda.current_stream())
+        with torch.cuda.graph(g_calls):
+            wl.step_calls(torch.cuda.current_stream())
+        per_step = wl.ekv.lib.ekv_launch_count() - n0
+        run_pre, run_calls = g_pre.replay, g_calls.replay
+    else:
+        run_pre = lambda: wl.step_prefix(torch.cuda.current_stream())
+        run_calls = lambda: wl.step_calls(torch.cuda.current_stream())
+        per_step = None
+    for _ in range(args.warmup):
+        run_pre()
+        run_calls()
+    torch.cuda.synchronize()
+    if wl.pool.status() != 0:
+        raise RuntimeError("device status word set during warm-up")
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    uuid = str(torch.cuda.get_device_properties(0).uuid)
+    clocks = Clocks(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+    clocks.start()
+    time.sleep(0.3)
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = wl.ekv.lib.ekv_launch_count()
+    t_start.record(stream)
+    for k in range(args.steps):
+        run_pre()
+        starts[k].record(stream)
+        run_calls()
+        ends[k].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = per_step * args.steps if per_step is not None else wl.ekv.lib.ekv_launch_count() - n0
+    ms = t_start.elapsed_time(t_end)
+    call_s = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3 / wl.n_calls
+    peaks = load_peaks()
+    bound = "tensor" if wl.flop_per_call / (peaks["tc"] * 1e12) >= wl.bytes_per_call / (peaks["hbm"] * 1e9) else "hbm"
+    if bound == "tensor":
+        ach = wl.flop_per_call / call_s / 1e12
+        roof = {"bound": bound, "achieved": ach, "peak": peaks["tc"], "unit": "TFLOP/s", "frac": ach / peaks["tc"]}
+    else:
+        ach = wl.bytes_per_call / call_s / 1e9
+        roof = {"bound": bound, "achieved": ach, "peak": peaks["hbm"], "unit": "GB/s", "frac": ach / peaks["hbm"]}
+    roof.update({"traffic": None, "peak_source": peaks["source"], "avg_launch_us": call_s * 1e6,
+                 "kernel": "attn_tc_kernel (one CTA per 128 query rows" +
+                           (", packed units)" if cfg["kind"] == "groot" else ")"),
+                 "algorithmic_per_launch": {"flop": wl.flop_per_call, "bytes": wl.bytes_per_call},
+                 "timed": "CUDA events around each step's layer-calls, divided by the calls (appends included "
+                          "for the LingBot chunks)"})
+    line = {"metric": METRIC, "value": wl.qtok_per_step * args.steps / (ms / 1e3), "unit": "query-tok/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 MMA, f32 accumulate",
+            "data": "synthetic", "config": {"workload": args.config, "description": cfg["desc"],
+                                            "batch_per_gpu": wl.B, "parallelism": "x1"},
+            "roofline": roof, "clocks": clk, "gpu_launches": int(launches), "device_status": wl.pool.status()}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------
 # CPU baseline: the oracle (C restatement of the reference's per-call work), all host cores
 # ------------------------------------------------------------------------------------------
 def cpu_baseline(wl: Pi05Workload, n_req: int, n_layers: int, threads: int):
@@ -324,12 +555,18 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ekv", choices=["ekv", "reference"])
-    ap.add_argument("--config", default="pi05_q8_b64", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="pi05_q8_b64", choices=sorted(CONFIGS) + sorted(OTHER_CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the requests per GPU (profiling cases)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.config in OTHER_CONFIGS:
+        if args.impl == "reference" or args.gpus != 1:
+            print(json.dumps({"impl": args.impl, "unavailable": f"{args.config} is measured on one GPU, ekv arm only"}))
+            return
+        run_other(args, OTHER_CONFIGS[args.config])
+        return
     cfg = dict(CONFIGS[args.config])
     args.workload = args.config
     if args.batch:

@@ -142,14 +142,14 @@ struct Plan {
     int tbl_n;      // entries cached (table indices [tbl_lo, tbl_lo + tbl_n))
 };
 
+// Plan of query tile qt (split `split` of n_splits) of request b, KV head g.
 template <int BN>
-__device__ __forceinline__ Plan make_plan(const AttnArgs &a, int n_qtiles) {
+__device__ __forceinline__ Plan make_plan_at(const AttnArgs &a, int b, int g, int qt, int split, int n_splits) {
     Plan pl;
-    const int n_splits = a.n_splits > 1 ? a.n_splits : 1;
-    pl.qt = blockIdx.x / n_splits;
-    pl.split = blockIdx.x - pl.qt * n_splits;
-    pl.g = blockIdx.y;
-    pl.b = blockIdx.z;
+    pl.qt = qt;
+    pl.split = split;
+    pl.g = g;
+    pl.b = b;
     pl.qrow0 = pl.qt * kBM;
     const int rows_total = a.q_tokens * a.group;
     pl.rows_valid = min(kBM, rows_total - pl.qrow0);
@@ -195,9 +195,27 @@ __device__ __forceinline__ Plan make_plan(const AttnArgs &a, int n_qtiles) {
             pl.tbl_n = (k_hi + bt - 1) / bt - pl.tbl_lo;
         }
     }
-    (void)n_qtiles;
     return pl;
 }
+
+template <int BN>
+__device__ __forceinline__ Plan make_plan(const AttnArgs &a, int n_qtiles) {
+    const int n_splits = a.n_splits > 1 ? a.n_splits : 1;
+    const int qt = blockIdx.x / n_splits;
+    (void)n_qtiles;
+    return make_plan_at<BN>(a, blockIdx.z, blockIdx.y, qt, blockIdx.x - qt * n_splits, n_splits);
+}
+
+// ---- packed units (a.pack > 0): CTA x holds the units u = x * pack + s, s < pack, unit u being
+// request u / kv_heads, KV head u % kv_heads, all its rows_per_unit = q_tokens * group query rows
+// (CTA rows [s * rpu, (s + 1) * rpu)). Its key tiles are unit 0's, then unit 1's, ...; a row sees
+// only its own unit's tiles. The per-unit plans and the first tile of each unit live in shared
+// memory (the block-table cache is not used: tbl_n = 0). ----
+constexpr int kMaxPack = 8;
+struct PackTable {
+    Plan unit[kMaxPack];
+};
+
 
 
 // K tile base (head g, this layer) of block-table entry `idx`: shared-memory copy when cached,
@@ -231,12 +249,21 @@ __device__ __forceinline__ void stage_q_load(const AttnArgs &a, const Plan &pl, 
         const int u = threadIdx.x + i * TcCfg<D, Q8>::THREADS;
         const int r = u / Q::UPR;
         qs.val[i] = make_uint4(0, 0, 0, 0);
-        if (u < Q::UNITS && r < pl.rows_valid) {
+        int b = pl.b, g = pl.g, qr = pl.qrow0 + r;
+        bool ok = r < pl.rows_valid;
+        if (a.pack) {  // packed units: row r is row r % rpu of unit r / rpu
+            const int rpu = a.q_tokens * a.group, s = r / rpu;
+            const int unit = blockIdx.x * a.pack + s;
+            b = unit / a.pool.kv_heads;
+            g = unit - b * a.pool.kv_heads;
+            qr = r - s * rpu;
+            ok = s < a.pack && b < a.n_batch;
+        }
+        if (u < Q::UNITS && ok) {
             const int d0 = (u - r * Q::UPR) * 8;
-            const int qr = pl.qrow0 + r;
             const int t = qr / a.group;
-            const int h = pl.g * a.group + (qr - t * a.group);
-            qs.val[i] = __ldg((const uint4 *)(a.q + (((int64_t)pl.b * a.q_tokens + t) * a.q_heads + h) * D + d0));
+            const int h = g * a.group + (qr - t * a.group);
+            qs.val[i] = __ldg((const uint4 *)(a.q + (((int64_t)b * a.q_tokens + t) * a.q_heads + h) * D + d0));
         }
     }
 }
@@ -506,7 +533,7 @@ __device__ __forceinline__ bool pair_sync(uint32_t xbar, int use, volatile int *
 // h = w >> 2. Per tile the H warps of a quarter swap their masked chunk maxima through shared memory;
 // P for the 32 keys goes back as 16 packed columns [h * 16, h * 16 + 16) of the tile's S buffer (all
 // H warps have read S by then). The O rescale and the epilogue split O's columns among them. ----
-template <int D, bool Q8>
+template <int D, bool Q8, bool PACK>
 __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan &pl, uint8_t *smem, uint32_t bar0,
                                                    volatile int *abort, uint32_t tmem, uint32_t lane_base, int n,
                                                    int n_qtiles, const void *omap, int omode) {
@@ -517,8 +544,13 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int h = warp >> 2, quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const bool row_ok = r < pl.rows_valid;
-    const int t = (pl.qrow0 + r) / a.group;
+    // packed units: row r belongs to unit r / rpu and sees only that unit's tiles
+    const PackTable *pt = (const PackTable *)(smem + C::OFF_TBL);
+    const int rpu = a.q_tokens * a.group;
+    const int s_row = PACK ? r / rpu : 0;
+    const bool row_ok = PACK ? (s_row < a.pack && pt->unit[s_row].rows_valid > 0) : r < pl.rows_valid;
+    const int t = PACK ? (r - s_row * rpu) / a.group : (pl.qrow0 + r) / a.group;
+    int s_tile = 0, first_tile = 0;  // unit of the current tile, and that unit's first CTA tile
     const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
     const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
     const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
@@ -535,16 +567,33 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
         if (!(ok = mbar_wait(bar(BAR_K_EMPTY + jj % C::NSTAGE), s_done_parity(jj, C::NSTAGE), abort, kWaitBudget))) break;
         tc_fence_after();
         if (r == 0 && h == 0 && jj < 50) TRACE(300 + jj);
-        const bool suffix = j >= pl.np_tiles;
-        const int key0 = (suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN) + h * 32;  // this warp's 32 keys
-        // all 32 keys visible to every row (uniform over the CTA; rows past rows_valid score zero
-        // queries and are never written)
-        const bool all_vis = suffix ? (suffix_simple && key0 + 32 <= a.suffix_len)
-                                    : (prefix_simple && key0 + 32 <= pl.sk.prefix_valid);
-        const uint32_t vb = all_vis ? 0xffffffffu
-                                    : (row_ok ? vis_word(m, suffix, key0, t, pl.sk.prefix_valid, pl.sk.span_b,
-                                                         pl.sk.span_e, a.suffix_len)
-                                              : 0u);
+        uint32_t vb;
+        bool all_vis = false;
+        if constexpr (PACK) {
+            // the tile's unit (tiles run unit by unit); rows of other units see none of its keys
+            while (s_tile + 1 < a.pack && jj >= first_tile + (pt->unit[s_tile].j1 - pt->unit[s_tile].j0)) {
+                first_tile += pt->unit[s_tile].j1 - pt->unit[s_tile].j0;
+                ++s_tile;
+            }
+            const int jt = jj - first_tile;
+            const Plan &up = pt->unit[s_tile];
+            const bool suffix = jt >= up.np_tiles;
+            const int key0 = (suffix ? (jt - up.np_tiles) * BN : up.kbeg + jt * BN) + h * 32;
+            vb = (row_ok && s_row == s_tile)
+                     ? vis_word(m, suffix, key0, t, up.sk.prefix_valid, up.sk.span_b, up.sk.span_e, a.suffix_len)
+                     : 0u;
+        } else {
+            const bool suffix = j >= pl.np_tiles;
+            const int key0 = (suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN) + h * 32;  // this warp's 32 keys
+            // all 32 keys visible to every row (uniform over the CTA; rows past rows_valid score zero
+            // queries and are never written)
+            all_vis = suffix ? (suffix_simple && key0 + 32 <= a.suffix_len)
+                             : (prefix_simple && key0 + 32 <= pl.sk.prefix_valid);
+            vb = all_vis ? 0xffffffffu
+                         : (row_ok ? vis_word(m, suffix, key0, t, pl.sk.prefix_valid, pl.sk.span_b, pl.sk.span_e,
+                                              a.suffix_len)
+                                   : 0u);
+        }
         const uint32_t s_buf = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
         uint32_t rr[32];
         tmem_load32(s_buf + h * 32, rr);
@@ -715,6 +764,14 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
         uint8_t *dst;
         if (split) {
             dst = (uint8_t *)(a.ws_o + (unit * kBM + rw) * D);
+        } else if (PACK) {
+            const int s = rw / rpu;
+            const Plan &up = pt->unit[s];
+            if (up.rows_valid == 0) continue;  // past the last unit
+            const int qrw = rw - s * rpu;
+            const int tw = qrw / a.group;
+            const int hw = up.g * a.group + (qrw - tw * a.group);
+            dst = (uint8_t *)a.out + ((((int64_t)up.b * a.q_tokens + tw) * a.q_heads + hw) * D) * (f32 ? 4 : 2);
         } else {
             const int qrw = pl.qrow0 + rw;
             const int tw = qrw / a.group;
@@ -726,7 +783,7 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
     }
 }
 
-template <int D, bool Q8>
+template <int D, bool Q8, bool PACK = false>
 __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
     attn_tc_kernel(const AttnArgs a, int n_qtiles, const __grid_constant__ CUtensorMap omap, int omode) {
     using C = TcCfg<D, Q8>;
@@ -750,9 +807,31 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
         TRACE(0);
         TRACE_CLK(20);
     }
-    const Plan pl = make_plan<BN>(a, n_qtiles);
+    Plan pl = make_plan<BN>(a, n_qtiles);
+    PackTable *pt = (PackTable *)(smem + C::OFF_TBL);  // packed units only (no block-table cache then)
+    const int rpu = a.q_tokens * a.group;
+    if constexpr (PACK) {
+        static_assert(!Q8 && BN == 128, "packed units: bf16 pools at 128-key tiles");
+        {
+            static_assert(sizeof(PackTable) <= C::TBL * 8, "pack table fits the block-table cache");
+            if (threadIdx.x < a.pack) {
+                const int unit = blockIdx.x * a.pack + threadIdx.x;
+                const int b = unit / a.pool.kv_heads;
+                Plan up{};
+                if (b < a.n_batch) {
+                    up = make_plan_at<BN>(a, b, unit - b * a.pool.kv_heads, 0, 0, 1);
+                    if (!up.sk.ok) report_error(a.pool.status, DEV_ERR_BAD_SEQ, b, a.seq_ids[b], 3);
+                }
+                up.tbl_n = 0;
+                pt->unit[threadIdx.x] = up;
+            }
+        }
+        pl.tbl_n = 0;
+        pl.qrow0 = 0;
+        pl.rows_valid = a.pack * rpu;
+    }
     if (threadIdx.x == 0) TRACE(1);
-    if (threadIdx.x == 0 && !pl.sk.ok) report_error(a.pool.status, DEV_ERR_BAD_SEQ, pl.b, a.seq_ids[pl.b], 3);
+    if (threadIdx.x == 0 && !PACK && !pl.sk.ok) report_error(a.pool.status, DEV_ERR_BAD_SEQ, pl.b, a.seq_ids[pl.b], 3);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -807,6 +886,13 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
         if (lane == 0) mbar_arrive(bar(BAR_Q_READY));
     }
     if (threadIdx.x == 0) TRACE(3);
+    if constexpr (PACK) {  // the CTA's tiles: every unit's, in unit order (plans published by the barrier above)
+        int total = 0;
+        for (int s = 0; s < a.pack; ++s) total += pt->unit[s].j1 - pt->unit[s].j0;
+        pl.j0 = 0;
+        pl.j1 = total;
+        pl.np_tiles = total;
+    }
     const int n = pl.j1 - pl.j0;
 
     if (warp == C::MMA_WARP) {
@@ -926,6 +1012,15 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
                     break;
                 }
                 if (lane == 0 && it < 50) TRACE((kv ? 150 : 450) + it);
+                if constexpr (PACK) {  // tile `it` of the CTA = tile it - first(s) of unit s
+                    int s = 0, first = 0;
+                    while (s + 1 < a.pack && it >= first + (pt->unit[s].j1 - pt->unit[s].j0)) {
+                        first += pt->unit[s].j1 - pt->unit[s].j0;
+                        ++s;
+                    }
+                    produce_bf16_part<D>(a, pt->unit[s], (const uint8_t *const *)sPtr, it - first, kv,
+                                         stages + st * C::KV_BYTES, bar(b_full + st), lane);
+                } else
                 produce_bf16_part<D>(a, pl, (const uint8_t *const *)sPtr, pl.j0 + it, kv, stages + st * C::KV_BYTES,
                                      bar(b_full + st), lane);
                 issued = it + 1;
@@ -983,7 +1078,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
         }
     } else if (warp < C::SMW && C::SPLIT) {
         if constexpr (C::SPLIT)
-            softmax_split_role<D, Q8>(a, pl, smem, bar0, abort, tmem, lane_base, n, n_qtiles, &omap, omode);
+            softmax_split_role<D, Q8, PACK>(a, pl, smem, bar0, abort, tmem, lane_base, n, n_qtiles, &omap, omode);
     } else if (warp < 4) {
         // ---- softmax / epilogue: thread = query row = TMEM lane ----
         const int r = threadIdx.x;
@@ -1310,6 +1405,32 @@ int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
     }
     const int bt = a.pool.block_tokens;
     if (C::BN % bt != 0 && bt % C::BN != 0) return EKV_ERR_UNSUPPORTED;  // blocks must tile key tiles
+    if constexpr (!Q8 && C::BN == 128) {
+        // Units of at most 64 query rows (GR00T's 17 queries x 1 head): several per CTA, so that a
+        // call of thousands of small (request, head) units runs a few CTAs per SM instead of one CTA
+        // (and its set-up) per unit. Only when the units outnumber the SMs; no key splits.
+        const int rpu = a.q_tokens * a.group;
+        const int64_t n_units = (int64_t)a.n_batch * a.pool.kv_heads;
+        if (2 * rpu <= kBM && n_units > sm_count()) {
+            a.pack = std::min(kMaxPack, kBM / rpu);
+            a.n_splits = 1;
+            const int64_t ctas = (n_units + a.pack - 1) / a.pack;
+            if (ctas > 0x7fffffff) return EKV_ERR_INVALID_ARG;
+            CUtensorMap omap;
+            std::memset(&omap, 0, sizeof(omap));
+            static int pack_attr_done[64] = {0};
+            if (dev < 64 && !pack_attr_done[dev]) {
+                if (cudaFuncSetAttribute(attn_tc_kernel<D, Q8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM) != cudaSuccess)
+                    return EKV_ERR_CUDA;
+                pack_attr_done[dev] = 1;
+            }
+            attn_tc_kernel<D, Q8, true><<<dim3((unsigned)ctas, 1, 1), C::THREADS, C::SMEM, s>>>(a, 1, omap, OUT_THREADS);
+            if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
+            note_launches(1);
+            return EKV_OK;
+        }
+    }
     const int n_qtiles = (a.q_tokens * a.group + kBM - 1) / kBM;
     const int64_t units = (int64_t)a.n_batch * a.pool.kv_heads * n_qtiles;
     if (a.n_splits == 0) {

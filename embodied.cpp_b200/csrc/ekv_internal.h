@@ -46,6 +46,10 @@ struct AttnArgs {
     // this layer-step's suffix K/V read straight from the caller's [n_batch][suffix_len][kv_heads]
     // [head_dim] bf16 buffers instead of the pool's suffix slot (CTA-pair kernel only), or null
     const uint16_t *k_sfx, *v_sfx;
+    // one-CTA kernel, bf16 at 128-key tiles: (request, KV head) units per CTA when a unit has at
+    // most 64 query rows (the CTA's 128 rows hold several units, each seeing only its own keys);
+    // 0 = one unit's 128-row tile per CTA
+    int32_t pack;
 };
 
 // Kernels launched by this library in this process (ekv_launch_count); every launch site adds its

@@ -316,3 +316,35 @@ def test_kernel_reports_bad_block_table():
         f.pool.attention(prm, q.cuda(), out, algo=algo)
         torch.cuda.synchronize()
         assert f.pool.status() == ekv.DEV_ERR_BAD_BLOCK
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,T,B", [(48, 32, 32, 17, 6), (64, 16, 8, 17, 24), (128, 8, 8, 9, 30)])
+@pytest.mark.parametrize("flag", [0, ekv.MASK_SPAN_EXCLUDE, ekv.MASK_SPAN_ONLY])
+def test_attention_packed_units(D, Hq, Hkv, T, B, flag):
+    """More (request, KV head) units of at most 64 query rows than SMs (GR00T's 17 queries x 32
+    heads at batch 6 and up): the one-CTA kernel packs several units into one CTA's 128 rows, each
+    row seeing only its unit's keys. Ragged prefixes, padding, spans, GQA, bf16 and f32 output, and
+    the suffix-only self layer."""
+    gen = torch.Generator().manual_seed(D + B)
+    rng = np.random.default_rng(D + B)
+    plens = [int(x) for x in rng.integers(1, 400, size=B)]
+    f = Filled(dtype=ekv.DTYPE_BF16, B=B, prefix_lens=plens, Hkv=Hkv, D=D, suffix_len=T, seed=D + B,
+               block_tokens=16)
+    q = bf16_randn(gen, (B, T, Hq, D))
+    valid = [max(1, p - int(rng.integers(0, 20))) for p in plens]
+    span = ([int(rng.integers(0, v)) for v in valid], [v for v in valid])
+    scale = 1 / np.sqrt(D)
+    f.suffix_len = 0
+    kw = dict(mask_flags=flag, prefix_valid=valid)
+    if flag:
+        kw["span"] = span
+    got = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC, **kw)
+    want = oracle_attention(f, 0, q, scale=scale, **kw)
+    check(got, want, 2e-2)
+    f.suffix_len = T
+    got = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC, use_prefix=False)
+    want = oracle_attention(f, 0, q, scale=scale, use_prefix=False)
+    check(got, want, 2e-2)
+    got = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC, out_dtype=ekv.DTYPE_BF16)
+    want = oracle_attention(f, 0, q, scale=scale)
+    check(got, want, 2e-2)
