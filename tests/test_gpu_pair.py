@@ -146,3 +146,41 @@ def test_append_suffix_attention_matches_two_calls(dtype, B, ws, d):
             else:
                 assert torch.equal(ks_one.view(torch.int16), ks_two.view(torch.int16))
                 assert torch.equal(vs_one.view(torch.int16), vs_two.view(torch.int16))
+
+
+@pytest.mark.parametrize("dtype", [ekv.DTYPE_BF16, ekv.DTYPE_Q8_0])
+@pytest.mark.parametrize("flag,T,hkv", [(ekv.MASK_SUFFIX_CAUSAL, 50, 1), (ekv.MASK_SUFFIX_PREFIX_LM, 51, 1),
+                                        (ekv.MASK_SPAN_EXCLUDE, 100, 2), (0, 1, 1), (0, 64, 2), (0, 128, 1)])
+def test_direct_suffix_masks_and_lengths(dtype, flag, T, hkv):
+    """The pair kernel's direct suffix read against the oracle and against append + attention,
+    bit for bit: causal and prefix-LM suffix masks, spans, GQA, suffix lengths of 1, 51, 64, 100 and
+    128 rows (one, two and exactly two full suffix tiles), ragged prefixes with padding."""
+    gen = torch.Generator().manual_seed(60 + T)
+    B, Hq = 3, 4 * hkv
+    plens = [517, 64, 300]
+    f = Filled(dtype=dtype, B=B, prefix_lens=plens, Hkv=hkv, D=D, suffix_len=T, seed=60 + T)
+    valid = [500, 60, 290]
+    span = ([20, 0, 10], [400, 64, 200])
+    dev = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")
+    kw = dict(mask_flags=flag, suffix_len=T, out_dtype=ekv.DTYPE_F32, prefix_valid=dev(valid))
+    if flag == ekv.MASK_SPAN_EXCLUDE:
+        kw.update(span_begin=dev(span[0]), span_end=dev(span[1]))
+    prm = f.pool.attention_params(layer=0, seq_ids=f.seq_ids, q_tokens=T, q_heads=Hq, scale=1 / 16, **kw)
+    sk = bf16_randn(gen, (B, T, hkv, D))
+    sv = bf16_randn(gen, (B, T, hkv, D))
+    q = bf16_randn(gen, (B, T, Hq, D)).cuda()
+    fused = torch.empty((B, T, Hq, D), dtype=torch.float32, device="cuda")
+    f.pool.append_suffix(0, f.seq_ids, torch.zeros_like(sk).cuda(), torch.zeros_like(sv).cuda())
+    f.pool.append_suffix_attention(prm, sk.cuda(), sv.cuda(), q, fused)
+    two = torch.empty_like(fused)
+    f.pool.append_suffix(0, f.seq_ids, sk.cuda(), sv.cuda())
+    f.pool.attention(prm, q, two)
+    torch.cuda.synchronize()
+    assert f.pool.status() == 0
+    assert torch.equal(fused, two)
+    f.sk[0], f.sv[0] = sk, sv  # the oracle reads this layer's suffix from the builder
+    okw = dict(mask_flags=flag, prefix_valid=valid)
+    if flag == ekv.MASK_SPAN_EXCLUDE:
+        okw["span"] = span
+    want = oracle_attention(f, 0, q.cpu(), scale=1 / 16, **okw)
+    check(fused.cpu().numpy(), want, TOL[dtype])
