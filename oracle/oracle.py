@@ -243,3 +243,32 @@ def flash_attn_ext(q, k, v, mask=None, *, scale, max_bias=0.0, logit_softcap=0.0
             o = p @ v[kb, kh]
             out[b, :, h] = np.where(den > 0, o / np.where(den > 0, den, 1.0), 0.0)
     return out
+
+
+def attention_ggml_q8_0(q, k, v, n_prefix, scale):
+    """The pi0.5 attention as ggml's CPU backend would compute it over a Q8_0 key/value cache
+    (models/pi05.cpp:406-418 with the cached tensors stored as GGML_TYPE_Q8_0), float64.
+
+    ggml's Q8_0 mul_mat converts src1 to the type's dot-product partner, Q8_0 itself (llama.cpp
+    b9016, ggml-cpu: the vec_dot_type of Q8_0), so S = dot(q8(Q), q8(K)): every 32-value block of each
+    query row is quantised with the same gguf rule as the keys. The 50 suffix keys joined by the
+    concat of :406 are quantised with the prefix (the concat writes into the Q8_0 tensor). V is read
+    dequantised (a permuted Q8_0 tensor is made contiguous as float). Softmax in float.
+    q [B, Tq, Hq, D], k/v [B, Lk, Hkv, D] f32 (pre-quantisation values: prefix, then suffix);
+    n_prefix is unused by the arithmetic (all keys are cached the same way) and kept for symmetry
+    with `attention`. Returns [B, Tq, Hq, D]. Used to bound the difference between a Q8_0 ggml path
+    and this library's f16 MMAs over exactly dequantised keys (both within the 5e-2 tolerance)."""
+    q = np.asarray(q, np.float32)
+    B, Tq, Hq, D = q.shape
+    Lk, Hkv = k.shape[1], k.shape[2]
+    rt = lambda x: dequantize_q8_0(quantize_q8_0(np.ascontiguousarray(x, np.float32).reshape(-1, D))).reshape(x.shape)
+    qh, kh, vh = rt(q).astype(np.float64), rt(k).astype(np.float64), rt(v).astype(np.float64)
+    g = Hq // Hkv
+    out = np.zeros((B, Tq, Hq, D), np.float64)
+    for b in range(B):
+        for h in range(Hq):
+            s = (qh[b, :, h] @ kh[b, :, h // g].T) * scale
+            p = np.exp(s - s.max(axis=1, keepdims=True))
+            out[b, :, h] = (p / p.sum(axis=1, keepdims=True)) @ vh[b, :, h // g]
+    del n_prefix
+    return out

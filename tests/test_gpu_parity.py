@@ -348,3 +348,18 @@ def test_attention_packed_units(D, Hq, Hkv, T, B, flag):
     got = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC, out_dtype=ekv.DTYPE_BF16)
     want = oracle_attention(f, 0, q, scale=scale)
     check(got, want, 2e-2)
+
+
+def test_q8_0_attention_against_ggml_q8_0_path():
+    """The tcgen05 Q8_0 path against the emulated ggml CPU Q8_0 path (queries and suffix keys
+    quantised for the dot products as ggml's Q8_0 mul_mat does) within the Q8_0 tolerance."""
+    gen = torch.Generator().manual_seed(12)
+    plens = [300, 517]
+    f = Filled(dtype=ekv.DTYPE_Q8_0, B=2, prefix_lens=plens, Hkv=1, D=256, suffix_len=50, seed=12)
+    q = bf16_randn(gen, (2, 50, 8, 256))
+    got = run_attention(f, 0, q, Hq=8, scale=1 / 16, algo=ekv.ALGO_TC)
+    for b, n in enumerate(plens):
+        k = np.concatenate([to_f32_np(f.pk[0][b, :n]), to_f32_np(f.sk[0][b, :50])])[None]
+        v = np.concatenate([to_f32_np(f.pv[0][b, :n]), to_f32_np(f.sv[0][b, :50])])[None]
+        want = oracle.attention_ggml_q8_0(to_f32_np(q[b:b + 1]), k, v, n, 1 / 16)
+        check(got[b:b + 1], want, TOL[ekv.DTYPE_Q8_0])

@@ -108,3 +108,24 @@ def test_f32_vs_f64_pi05_small():
     a = oracle.attention(q, k, v, seqs, m, 1 / 8.0)
     b = oracle.attention(q, k, v, seqs, m, 1 / 8.0, precision="f64")
     assert np.abs(a - b).max() < 1e-5
+
+
+def test_ggml_q8_0_path_within_tolerance_of_exact_dequant():
+    """A Q8_0 ggml CPU path (queries quantised to Q8_0 for the dot products) differs from the
+    exactly dequantised f32 attention of the pinned oracle by well under the Q8_0 tolerance (5e-2)
+    on pi0.5 shapes, so either reading of 'the reference's result' passes the same check."""
+    rng = np.random.default_rng(11)
+    to_bf = lambda a: oracle.bf16_to_f32(oracle.f32_to_bf16(a))
+    B, Tq, Hq, Hkv, D, Lp, Ls = 2, 50, 8, 1, 256, 300, 50
+    q = to_bf(rng.standard_normal((B, Tq, Hq, D)).astype(np.float32) * 0.5)
+    k = to_bf(rng.standard_normal((B, Lp + Ls, Hkv, D)).astype(np.float32) * 0.5)
+    v = to_bf(rng.standard_normal((B, Lp + Ls, Hkv, D)).astype(np.float32) * 0.5)
+    kq = k.copy()
+    vq = v.copy()
+    for x in (kq, vq):  # the library's Q8_0 pool: prefix quantised, suffix bf16
+        x[:, :Lp] = oracle.dequantize_q8_0(oracle.quantize_q8_0(x[:, :Lp].reshape(-1, D))).reshape(x[:, :Lp].shape)
+    seqs = oracle.make_seqs([Lp] * B, n_suffix=Ls)
+    exact = oracle.attention(q, kq, vq, seqs, oracle.make_mask(), 1 / 16.0, precision="f64")
+    ggml = oracle.attention_ggml_q8_0(q, k, v, Lp, 1 / 16.0)
+    d = np.abs(exact - ggml).max()
+    assert d < 1e-2, d
