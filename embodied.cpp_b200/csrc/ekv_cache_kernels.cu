@@ -74,14 +74,19 @@ __global__ void append_q8_kernel(PoolView p, int layer, const int32_t *__restric
     const int rem = u - kv * (p.kv_heads * groups);
     const int h = rem / groups;
     const int g = rem - h * groups;
-    int blk, rib;
-    if (!prefix_dest(p, layer, seq_ids[b], dst_pos[b] + r, blk, rib)) return;
+    // the group's 64 source bytes are requested before the destination is resolved (block table
+    // lookups), so the two memory latencies overlap instead of adding up
     const int64_t src = (((int64_t)src_row[b] + r) * p.kv_heads + h) * p.head_dim + g * 32;
     const uint4 *s = (kv ? v : k) + src / 8;
+    uint4 raw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) raw[i] = __ldg(s + i);
+    int blk, rib;
+    if (!prefix_dest(p, layer, seq_ids[b], dst_pos[b] + r, blk, rib)) return;
     float x[32];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const uint4 w = s[i];
+        const uint4 w = raw[i];
         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
