@@ -595,6 +595,23 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
                                    : 0u);
         }
         const uint32_t s_buf = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
+        if constexpr (PACK) {
+            // No row of this lane quarter belongs to the tile's unit (a 17-row unit touches one or two
+            // quarters): its P is zero and its scores need not be read. The four warps of the quarter
+            // decide alike, so they skip the maxima exchange together.
+            const int lo = s_tile * rpu;
+            if (!(lo < quarter * 32 + 32 && lo + rpu > quarter * 32)) {
+                uint32_t pz[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) pz[i] = 0u;
+                tmem_st16(s_buf + h * 16, pz);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(BAR_P_FULL + sb));
+                continue;
+            }
+        }
         uint32_t rr[32];
         tmem_load32(s_buf + h * 32, rr);
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -606,12 +623,15 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
             for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], ((vb >> i) & 1u) ? __uint_as_float(rr[i]) : -INFINITY);
         }
         const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-        xmax[((jj & 1) * H + h) * kBM + r] = cm;
+        // exchange slots alternate by use (a slot is rewritten only after the next exchange, which
+        // every warp of the quarter reaches after reading this one)
+        const int xp = uses & 1;
+        xmax[(xp * H + h) * kBM + r] = cm;
         if (!(ok = pair_sync(xbar, uses++, abort))) break;
         float rmax = cm;  // raw scores (scale > 0)
 #pragma unroll
         for (int o = 0; o < H; ++o)
-            if (o != h) rmax = fmaxf(rmax, xmax[((jj & 1) * H + o) * kBM + r]);
+            if (o != h) rmax = fmaxf(rmax, xmax[(xp * H + o) * kBM + r]);
         // a new maximum more than 2^8 above the one in use: rescale l and O (the H warps of a
         // quarter see the same row maxima, so they take this branch together)
         if (__any_sync(0xffffffffu, rmax > (m_used + 8.0f) * inv_scale_log2)) {
