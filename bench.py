@@ -377,9 +377,9 @@ def run_other(args, cfg):
     if wl.graphable:
         g_pre, g_calls = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
         n0 = wl.ekv.lib.ekv_launch_count()
-        with torch.cuda.graph(g_pre):
+        with torch.cuda.graph(g_pre, capture_error_mode="thread_local"):
             wl.step_prefix(torch.cuda.current_stream())
-        with torch.cuda.graph(g_calls):
+        with torch.cuda.graph(g_calls, capture_error_mode="thread_local"):
             wl.step_calls(torch.cuda.current_stream())
         per_step = wl.ekv.lib.ekv_launch_count() - n0
         run_pre, run_calls = g_pre.replay, g_calls.replay
@@ -602,13 +602,15 @@ def main():
     # One eager step (first-call set-up: kernel attributes, tensor-map encoder), then the step
     # captured as two CUDA graphs -- the 18 prefix appends, and the 180 layer-step calls -- the
     # way the reference runs its denoise loop as one ggml graph. Launches are counted at capture.
+    # Thread-local capture: CUDA calls of other threads (the NCCL watchdog under torchrun) do not
+    # invalidate it.
     wl.step(stream)
     torch.cuda.synchronize()
     g_pre, g_calls = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     n0 = wl.ekv.lib.ekv_launch_count()
-    with torch.cuda.graph(g_pre):
+    with torch.cuda.graph(g_pre, capture_error_mode="thread_local"):
         wl.step_prefix(torch.cuda.current_stream())
-    with torch.cuda.graph(g_calls):
+    with torch.cuda.graph(g_calls, capture_error_mode="thread_local"):
         wl.step_calls(torch.cuda.current_stream())
     launches_per_step = wl.ekv.lib.ekv_launch_count() - n0
     torch.cuda.synchronize()
