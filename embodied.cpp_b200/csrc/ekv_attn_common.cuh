@@ -63,8 +63,7 @@ constexpr int kDq = 256;  // dequantising threads (Q8_0): 8 warps, two per SM su
 // `max_tiles` key tiles per unit: minimises waves x (per-unit fixed cost + tiles per split x tile
 // cost) + a merge pass when split. The costs are in tile-times, measured on B200: a unit's set-up
 // and epilogue (Q load, table, O write) take about five tile-times, the merge about two.
-inline int choose_split_count(int64_t units, int max_tiles, int slots) {
-    constexpr double kFixed = 5.0, kMerge = 2.0;
+inline int choose_split_count_cost(int64_t units, int max_tiles, int slots, double kFixed, double kMerge) {
     slots = slots > 0 ? slots : 1;
     int best = 1;
     double best_cost = 1e30;
@@ -79,6 +78,10 @@ inline int choose_split_count(int64_t units, int max_tiles, int slots) {
         }
     }
     return best;
+}
+
+inline int choose_split_count(int64_t units, int max_tiles, int slots) {
+    return choose_split_count_cost(units, max_tiles, slots, 5.0, 2.0);
 }
 
 // Bits of the keys [lo, hi) inside the 32-key word starting at key w0.
@@ -150,6 +153,16 @@ __device__ __forceinline__ void dequant16(const uint4 q, uint32_t dbits, uint4 &
     }
     lo = make_uint4(o[0], o[1], o[2], o[3]);
     hi = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// Any of the eight f16 values with an all-ones exponent (a bf16 value beyond the f16 range became
+// inf, or the input was inf / NaN).
+__device__ __forceinline__ bool f16x8_has_inf(uint4 v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) bad |= ((w[i] & 0x7C00u) == 0x7C00u) | ((w[i] & 0x7C000000u) == 0x7C000000u);
+    return bad;
 }
 
 [[maybe_unused]] __device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {

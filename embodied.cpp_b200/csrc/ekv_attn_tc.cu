@@ -1500,7 +1500,8 @@ int dispatch(const AttnArgs &a, cudaStream_t s, size_t ws) {
 }  // namespace ekv
 extern "C" int ekv_debug_set_trace(unsigned long long *buf) {
     if (cudaMemcpyToSymbol(ekv::c_trace, &buf, sizeof(buf)) != cudaSuccess) return -2;
-    return ekv::pair_debug_set_trace(buf);
+    if (ekv::pair_debug_set_trace(buf)) return -2;
+    return ekv::pair128_debug_set_trace(buf);
 }
 namespace ekv {
 #endif
@@ -1519,6 +1520,11 @@ size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int
         const int64_t pair_units = (int64_t)prm.n_batch * p.kv_heads * n_pairs;
         const int psp = pair_choose_splits(pair_units, max_tiles, sm_count());
         if (psp > 1) need = std::max(need, (size_t)pair_units * 2 * psp * kBM * (p.head_dim + 2) * sizeof(float));
+        // the 128-key pair kernel's choice
+        const int max_tiles128 = (max_prefix + 127) / 128 + (prm.suffix_len + 127) / 128;
+        const int psp128 = pair128_choose_splits(pair_units, max_tiles128, sm_count());
+        if (psp128 > 1)
+            need = std::max(need, (size_t)pair_units * 2 * psp128 * kBM * (p.head_dim + 2) * sizeof(float));
     }
     return need;
 }
@@ -1544,6 +1550,7 @@ int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k) {
     // head_dim 256: each SM of a pair copies (bf16) or dequantises (Q8_0) half of every tile, and
     // each K/V byte crosses L2 -> SM twice per request instead of four times
     const bool pair = a.pool.head_dim == 256 && k != TcKernel::OneCta;
+    if (pair && k == TcKernel::Pair) return launch_attention_pair128(a, s, ws, sm_count());
     if (pair) return launch_attention_pair(a, s, ws, sm_count());
     return a.pool.dtype == EKV_DTYPE_Q8_0 ? dispatch<true>(a, s, ws) : dispatch<false>(a, s, ws);
 }

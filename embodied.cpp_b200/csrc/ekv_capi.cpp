@@ -423,7 +423,8 @@ int ekv_attention_algo(ekv_pool *p, const ekv_attn_params *prm, const void *q, v
     if (rc) return rc;
     if (const int e = set_device(p)) return e;
     if (algo == EKV_ALGO_SIMT) return ekv::launch_attention_simt(a, (cudaStream_t)stream);
-    if (algo != EKV_ALGO_TC && algo != EKV_ALGO_TC_PAIR && algo != EKV_ALGO_TC_CTA) return EKV_ERR_INVALID_ARG;
+    if (algo != EKV_ALGO_TC && algo != EKV_ALGO_TC_PAIR && algo != EKV_ALGO_TC_CTA && algo != EKV_ALGO_TC_PAIR64)
+        return EKV_ERR_INVALID_ARG;
     const size_t need = ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens);
     if (workspace && ((uintptr_t)workspace & 15)) return EKV_ERR_INVALID_ARG;
     if (workspace && need && workspace_bytes >= need) {
@@ -431,9 +432,10 @@ int ekv_attention_algo(ekv_pool *p, const ekv_attn_params *prm, const void *q, v
         a.ws_o = (float *)workspace;
         a.n_splits = 0;  // 0 = let the launcher choose from the workspace it was given
     }
-    const ekv::TcKernel k = algo == EKV_ALGO_TC_PAIR  ? ekv::TcKernel::Pair
-                            : algo == EKV_ALGO_TC_CTA ? ekv::TcKernel::OneCta
-                                                      : ekv::TcKernel::Auto;
+    const ekv::TcKernel k = algo == EKV_ALGO_TC_PAIR     ? ekv::TcKernel::Pair
+                            : algo == EKV_ALGO_TC_CTA    ? ekv::TcKernel::OneCta
+                            : algo == EKV_ALGO_TC_PAIR64 ? ekv::TcKernel::Pair64
+                                                         : ekv::TcKernel::Auto;
     return ekv::launch_attention_tc(a, (cudaStream_t)stream, k);
 }
 

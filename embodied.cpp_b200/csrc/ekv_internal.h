@@ -66,18 +66,25 @@ int launch_gather(const PoolView &p, int layer, int seq, int pos0, int n_rows, i
 int launch_gather_suffix(const PoolView &p, int layer, int seq, int n_rows, int format,
                          void *k_out, void *v_out, cudaStream_t s);
 int launch_attention_simt(const AttnArgs &a, cudaStream_t s);
-// Which tcgen05 kernel runs a call: Auto and Pair = the CTA-pair kernel (ekv_attn_pair.cu) for
-// head_dim 256, one CTA per 128 query rows otherwise; OneCta = one CTA per 128 query rows always.
-enum class TcKernel { Auto, Pair, OneCta };
+// Which tcgen05 kernel runs a call at head_dim 256: Auto and Pair64 = the 64-key CTA-pair kernel
+// (ekv_attn_pair.cu); Pair = the 128-key CTA-pair kernel (ekv_attn_pair128.cu) where the call's
+// shape allows it (query group dividing 128, power-of-two blocks), else EKV_ERR_UNSUPPORTED;
+// OneCta = one CTA per 128 query rows. Other head dims always run one CTA per 128 query rows.
+enum class TcKernel { Auto, Pair, OneCta, Pair64 };
 int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k);
 size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix);
 // CTA-pair kernel (head_dim 256); n_splits == 0 in `a` = choose from the workspace at a.ws_o
 int launch_attention_pair(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms);
 int pair_choose_splits(int64_t pair_units, int max_tiles, int sms);
+// 128-key CTA-pair kernel (head_dim 256): EKV_ERR_UNSUPPORTED, with nothing enqueued, where the
+// call's shape needs the 64-key pair kernel
+int launch_attention_pair128(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms);
+int pair128_choose_splits(int64_t pair_units, int max_tiles, int sms);
 // combine key-split partial outputs (head_dim of the pool) into a.out
 int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s);
 #ifdef EKV_TRACE
 int pair_debug_set_trace(unsigned long long *buf);
+int pair128_debug_set_trace(unsigned long long *buf);
 #endif
 
 }  // namespace ekv

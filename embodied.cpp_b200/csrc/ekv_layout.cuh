@@ -47,6 +47,7 @@ enum : int32_t {
     DEV_ERR_BAD_SEQ = 2,       // sequence id outside [0, max_seqs)
     DEV_ERR_BAD_POS = 3,       // position outside the sequence's blocks
     DEV_ERR_TIMEOUT = 4,       // bounded mbarrier wait ran out
+    DEV_ERR_F16_RANGE = 5,     // a value beyond the f16 range met an f16 operand (Q8_0 pools)
 };
 
 __host__ __device__ inline int swizzle_bytes_for(int head_dim) {

@@ -360,6 +360,75 @@ __device__ __forceinline__ void mma_ts_x4(uint32_t d_tmem, const uint32_t (&a)[4
     }
 }
 
+// Four tcgen05.mma back to back with both operands in shared memory (descriptors a[0..3], b[0..3]);
+// the first accumulates into D only when acc0 != 0, the others always.
+template <bool PAIR>
+__device__ __forceinline__ void mma_ss_x4(uint32_t d_tmem, const uint64_t (&a)[4], const uint64_t (&b)[4], uint32_t idesc,
+                                          uint32_t acc0) {
+    if constexpr (PAIR) {
+        asm volatile(
+            "{\n\t.reg .pred p, t;\n\t"
+            "setp.ne.b32 p, %10, 0;\n\t"
+            "setp.eq.b32 t, %10, %10;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %5, %9, p;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %2, %6, %9, t;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %3, %7, %9, t;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %8, %9, t;\n\t}" ::"r"(d_tmem),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc), "r"(acc0)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p, t;\n\t"
+            "setp.ne.b32 p, %10, 0;\n\t"
+            "setp.eq.b32 t, %10, %10;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %9, p;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %9, t;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %9, t;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %9, t;\n\t}" ::"r"(d_tmem),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc), "r"(acc0)
+            : "memory");
+    }
+}
+
+// Tiled tensor load global -> this CTA's shared memory through a tensor map (no multicast),
+// completion counted in bytes on a local mbarrier. `map` is the generic address of a
+// __grid_constant__ CUtensorMap kernel parameter.
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const void *map, int c0, int c1, int c2, int c3, int c4,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+        "%6}], [%7];" ::"r"(dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+        : "memory");
+}
+
+// 16-byte global load through the non-coherent path without allocating in L1 (data read once per SM).
+__device__ __forceinline__ uint4 ldg_nc_16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_nc_u16(const void *p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return (uint32_t)v;
+}
+
+// Per-warpgroup register budget (all four warps of a warpgroup execute it). The increases of a
+// block draw on the registers it was launched with (threads x registers at launch) that decreases
+// released, so the budgets of all warpgroups must sum to at most the launch total.
+template <uint32_t N>
+__device__ __forceinline__ void warpgroup_reg_alloc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void warpgroup_reg_dealloc() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                  : "memory");

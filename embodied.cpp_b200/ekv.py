@@ -28,7 +28,7 @@ MASK_SUFFIX_PREFIX_LM = 1 << 1
 MASK_SPAN_ONLY = 1 << 2
 MASK_SPAN_EXCLUDE = 1 << 3
 MASK_BLOCK_CAUSAL = 1 << 4
-ALGO_TC, ALGO_SIMT, ALGO_TC_PAIR, ALGO_TC_CTA = 0, 1, 2, 3
+ALGO_TC, ALGO_SIMT, ALGO_TC_PAIR, ALGO_TC_CTA, ALGO_TC_PAIR64 = 0, 1, 2, 3, 4
 
 # Device-side error codes written into the pool status word by kernels.
 DEV_ERR_BAD_BLOCK, DEV_ERR_BAD_SEQ, DEV_ERR_BAD_POS, DEV_ERR_TIMEOUT = 1, 2, 3, 4

@@ -20,8 +20,13 @@ D = 256
 
 
 def both(f, q, *, Hq, scale, **kw):
+    """The CTA-pair kernel (128-key tiles where the shape allows, as the default runs it) and the
+    one-CTA kernel; the 64-key pair kernel is checked against the one-CTA kernel on the way."""
     got = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC_PAIR, **kw)
     single = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC_CTA, **kw)
+    pair64 = run_attention(f, 0, q, Hq=Hq, scale=scale, algo=ekv.ALGO_TC_PAIR64, **kw)
+    tol = TOL[f.dtype]
+    assert np.abs(pair64 - single).max() <= tol
     return got, single
 
 
@@ -83,11 +88,12 @@ def test_pair_split_keys(dtype):
     prm = f.pool.attention_params(layer=0, seq_ids=f.seq_ids, q_tokens=10, q_heads=8, scale=1 / 16,
                                   suffix_len=f.suffix_len, out_dtype=ekv.DTYPE_F32)
     assert f.pool.workspace_size(prm) > 0  # the splitter engages for this shape
-    a = run_attention(f, 0, q, Hq=8, scale=1 / 16, algo=ekv.ALGO_TC_PAIR)
-    b = run_attention(f, 0, q, Hq=8, scale=1 / 16, algo=ekv.ALGO_TC_PAIR, workspace=True)
     want = oracle_attention(f, 0, q, scale=1 / 16)
-    check(a, want, TOL[dtype])
-    check(b, want, TOL[dtype])
+    for algo in (ekv.ALGO_TC_PAIR, ekv.ALGO_TC_PAIR64):
+        a = run_attention(f, 0, q, Hq=8, scale=1 / 16, algo=algo)
+        b = run_attention(f, 0, q, Hq=8, scale=1 / 16, algo=algo, workspace=True)
+        check(a, want, TOL[dtype])
+        check(b, want, TOL[dtype])
 
 
 def test_pair_bf16_output_pi05_batch():
