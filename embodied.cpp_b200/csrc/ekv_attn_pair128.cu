@@ -22,9 +22,9 @@
 // scale) and store the swizzled operand; Q is converted to f16 in place once it has landed, and
 // the MMAs run in f16 (11 mantissa bits of q * d). bf16 pools: two copy-engine feeder warps move
 // whole pool blocks (pre-swizzled tiles) into the stages and the MMAs run in bf16. Accumulation
-// is f32. Warps: 0-7 softmax and epilogue (two per TMEM lane quarter, 64 columns each), 8 MMA
-// issue (rank 0) and TMEM allocation, 9 Q load and bf16 K feeder, 10 bf16 V feeder, 11 bf16
-// relay of the copies' completion to rank 0, 12-19 Q8_0 dequantisation.
+// is f32. Warps: 0-15 softmax and epilogue (four per TMEM lane quarter, 32 columns each), 16 MMA
+// issue (rank 0) and TMEM allocation, 17 Q load and bf16 K feeder, 18 bf16 V feeder, 19 bf16
+// relay of the copies' completion to rank 0, 20-27 Q8_0 dequantisation.
 //
 // Every wait is bounded; on expiry the CTA records DEV_ERR_TIMEOUT and unwinds through the closing
 // cluster barrier after rank 0's MMAs have finished.
@@ -62,13 +62,26 @@ struct P2Cfg {
     static constexpr int OFF_V = OFF_K + NS * K_BYTES;
     static constexpr int OFF_BAR = OFF_V + NS * V_BYTES;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int OFF_XCH = OFF_BAR + BAR_BYTES;  // max exchange [2 parity][2 half][128] + sums [2][128]
-    static constexpr int OFF_TBL = OFF_XCH + 6 * kBM * 4;
-    static constexpr int TBL_ROOM = (232448 - 1024 - OFF_TBL) / 8;
+    static constexpr int SMH = 4;                      // softmax warps per TMEM lane quarter
+    static constexpr int OFF_XCH = OFF_BAR + BAR_BYTES;  // max exchange [2 parity][SMH][128] + sums [SMH][128]
+    static constexpr int OFF_TBL = OFF_XCH + 3 * SMH * kBM * 4;
+    // block-table cache of the split: tile pointers (8 B) and physical block ids (4 B)
+    static constexpr int TBL_ROOM = (232448 - 1024 - OFF_TBL) / 12;
     static constexpr int TBL = TBL_ROOM > 512 ? 512 : TBL_ROOM;
-    static constexpr int SMEM = OFF_TBL + TBL * 8 + 1024;
-    static constexpr int SMW = 8;                      // softmax warps
-    static constexpr int MMA_WARP = 8, KF_WARP = 9, VF_WARP = 10, RELAY_WARP = 11, DQ_WARP0 = 12;
+    static constexpr int OFF_BLK = OFF_TBL + TBL * 8;
+    static constexpr int SMEM = OFF_BLK + TBL * 4 + 1024;
+    // Q8_0: the raw int8 / fp16-scale bytes of a tile land in the upper part of its own operand stage
+    // (copy engine) and are converted in place: K -- this CTA's 64 rows as segments of
+    // min(block, 64) rows, [qs rows x 256 B][scales rows x 16 B]; V -- this CTA's 128 columns of all
+    // 128 rows as segments of min(block, 128) rows, [qs rows x 128 B][scales rows x 16 B]
+    static constexpr int RAWK_BYTES = KROWS * (D + D / 16);
+    static constexpr int RAWV_BYTES = BN * (VCOLS + D / 16);
+    static constexpr int RAWK_OFF = K_BYTES - RAWK_BYTES;
+    static constexpr int RAWV_OFF = V_BYTES - RAWV_BYTES;
+    static_assert(RAWK_OFF >= 0 && RAWV_OFF >= 0 && RAWK_OFF % 16 == 0 && RAWV_OFF % 128 == 0, "raw staging");
+    static constexpr int SMW = 4 * SMH;                // softmax warps
+    static constexpr int MMA_WARP = SMW, KF_WARP = SMW + 1, VF_WARP = SMW + 2, RELAY_WARP = SMW + 3,
+                         DQ_WARP0 = SMW + 4;
     static constexpr int NDQ = 256;                    // dequantising threads (Q8_0)
     static constexpr int THREADS = Q8 ? (DQ_WARP0 * 32 + NDQ) : (RELAY_WARP + 1) * 32;
     static constexpr int TMEM_COLS = 512;
@@ -88,8 +101,11 @@ enum {
     P2_KFULL = 9,       // [2] local (bf16): this CTA's K half landed
     P2_VFULL = 11,      // [2] local (bf16): this CTA's V half landed
     P2_DONE = 13,       // rank 0: all MMAs finished
-    P2_XCH = 14,        // [4] softmax pair exchange, one per TMEM lane quarter
-    P2_N = 18
+    P2_XCH = 14,        // [4] softmax row-maximum exchange, one per TMEM lane quarter
+    P2_RAWK = 18,       // [2] local (Q8_0): raw K part of tile j landed in K stage j % 2
+    P2_RAWV = 20,       // [2] local (Q8_0): raw V part of tile j landed in V stage j % 2
+    P2_TEAM = 22,       // [2] local (Q8_0): the K (V) dequantising team has read the raw part
+    P2_N = 24
 };
 static_assert(P2_N * 8 + 16 <= 256, "barrier block");
 
@@ -231,74 +247,141 @@ __device__ __forceinline__ void p2_suffix_stage(const AttnArgs &a, const P2Plan 
     (void)abort;
 }
 
-// ---- Q8_0 dequantisation: this thread's 4 K units and 4 V units (16 int8 values each, with their
-// fp16 scales) of one prefix tile, loaded straight from the pool. Lane l of a warp takes physical
-// 16-byte unit 4 (l >> 4) + (l & 3) (plus 8 uh for K, 8r for V) of row 4 rq + ((l >> 2) & 3): a warp
-// pass reads four 128-byte row segments (coalesced), and the eight lanes of each shared-memory
-// store phase (two adjacent rows, four column segments) hit eight distinct bank groups. ----
-struct P2Raw {
-    uint4 q[4];
-    uint32_t d[4];
-};
+// ---- Q8_0 raw staging (copy engine) and in-place dequantisation. The K feeder copies this CTA's
+// 64 K rows (whole blocks: qs plane then scales, contiguous in the pool), the V feeder this CTA's
+// 128 columns of the tile's 128 V rows (a tensor-map load of the qs half of each block, a bulk copy
+// of its scale plane), into the upper part of the tile's own operand stage once the stage is free.
+// Warps DQ_WARP0 .. +3 then convert K, the next four V: each thread reads its eight units (16 int8
+// values and the fp16 scale of their 32-group) from the raw bytes, the team meets at a bounded
+// barrier (every raw byte read before any f16 store overwrites the stage), and the thread stores
+// its units as f16. Eight consecutive lanes take eight consecutive rows of one 16-column segment:
+// the pool's row swizzle of the int8 units (unit ^ (row & 7)) makes their raw loads, and the
+// operand layout's swizzle their stores, hit eight distinct bank groups. ----
+constexpr int kDqUnits = 8;
 
-__device__ __forceinline__ void p2_raw_coords(int dw, int lane, int i, int kv, int rank, int &row, int &pu) {
-    const int p4 = lane & 3, rr = (lane >> 2) & 3, pc = lane >> 4;
-    const int combo = dw * 4 + i;  // 32 warp passes per part
+// Row (of this CTA's K rows or of the tile's V rows) and logical 16-column segment (of the row, or
+// of this CTA's V half) of unit i of team thread ptid.
+__device__ __forceinline__ void p2_dq_coords(int ptid, int i, int kv, int &row, int &seg) {
     if (kv == 0) {
-        row = (combo >> 1) * 4 + rr;                 // K row 0-63 of this CTA
-        pu = (combo & 1) * 8 + pc * 4 + p4;          // physical unit 0-15
+        row = 8 * i + (ptid & 7);
+        seg = ptid >> 3;            // 0-15
     } else {
-        row = combo * 4 + rr;                        // V row 0-127 of the tile
-        pu = rank * 8 + pc * 4 + p4;                 // this CTA's half of the columns
+        row = 16 * i + 8 * (ptid >> 6) + (ptid & 7);
+        seg = (ptid >> 3) & 7;      // 0-7 within this CTA's half
     }
 }
 
-// Issue the loads of this thread's four units of part kv (0: K, 1: V) of prefix tile j.
-template <int TBL>
-__device__ __forceinline__ void p2_load_raw(const AttnArgs &a, const P2Plan &pl, const uint8_t *const *sPtr, int j,
-                                            int kv, int dw, int lane, P2Raw &r) {
-    constexpr int D = 256, BN = 128, KROWS = 64;
+template <bool Q8>
+__device__ __forceinline__ void p2_dequant_part(const uint8_t *raw, int kv, int rank, int bt, uint8_t *sDst, int ptid,
+                                                uint32_t team_bar, int team_use, volatile int *abort, bool &bad,
+                                                bool &ok) {
+    constexpr int D = 256, VCOLS = 128, W = 128;
+    const int ks = kv == 0 ? min(bt, 64) : min(bt, 128);
+    const int rowb = kv == 0 ? D : VCOLS;                 // raw qs bytes per row
+    const int segb = ks * (rowb + D / 16);                // raw bytes per segment
+    uint4 q[kDqUnits];
+    uint32_t d[kDqUnits];
+#pragma unroll
+    for (int i = 0; i < kDqUnits; ++i) {
+        int row, seg;
+        p2_dq_coords(ptid, i, kv, row, seg);
+        const int sg = row / ks, rr = row - sg * ks;
+        const uint8_t *base = raw + sg * segb;
+        const int pu = seg ^ (row & 7);                  // physical unit (of the row, or of its half)
+        const int gs = kv == 0 ? seg : seg + 8 * rank;   // logical segment of the full row
+        q[i] = *(const uint4 *)(base + rr * rowb + pu * 16);
+        d[i] = *(const uint16_t *)(base + ks * rowb + rr * (D / 16) + (gs >> 1) * 2);
+    }
+    // every thread of the team has read its raw units before any stores over them
+    __syncwarp();
+    if (ptid == 0 && kv == 0 && team_use < 30) TRACE(960 + team_use);
+    if ((threadIdx.x & 31) == 0) mbar_arrive(team_bar);
+    if (!mbar_wait(team_bar, (uint32_t)team_use & 1u, abort, kWaitBudget)) {
+        ok = false;
+        return;
+    }
+    if (ptid == 0 && kv == 0 && team_use < 30) TRACE(990 + team_use);
+#pragma unroll
+    for (int i = 0; i < kDqUnits; ++i) {
+        int row, seg;
+        p2_dq_coords(ptid, i, kv, row, seg);
+        uint4 lo, hi;
+        dequant16(q[i], d[i], lo, hi);
+        bad |= f16x8_has_inf(lo) | f16x8_has_inf(hi);
+        const int dD = kv == 0 ? D : VCOLS;
+        *(uint4 *)(sDst + tile_elem_off(row, 16 * seg, dD, W)) = lo;
+        *(uint4 *)(sDst + tile_elem_off(row, 16 * seg + 8, dD, W)) = hi;
+    }
+}
+
+// Raw staging of part kv of prefix tile j into the upper part of the operand stage (one lane per
+// segment), with an L2 prefetch of the blocks of tile j + 2 this part will need. Segments past the
+// prefix, or of an invalid block, are zero-filled by the warp.
+__device__ __forceinline__ void p2_stage_raw(const AttnArgs &a, const P2Plan &pl, const uint8_t *const *sPtr,
+                                             const int32_t *sBlk, const void *vmap, int j, int kv, uint8_t *raw,
+                                             uint32_t bar_raw, int lane) {
+    constexpr int D = 256, BN = 128, KROWS = 64, VCOLS = 128;
     const PoolView &p = a.pool;
     const int bt = p.block_tokens;
-    const int64_t v_off = (int64_t)kv * p.kv_heads * p.tile_bytes;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        int row, pu;
-        p2_raw_coords(dw, lane, i, kv, pl.rank, row, pu);
-        const int key = pl.kbeg + j * BN + (kv == 0 ? pl.rank * KROWS : 0) + row;
-        r.q[i] = make_uint4(0, 0, 0, 0);
-        r.d[i] = 0u;
+    const int ks = kv == 0 ? min(bt, KROWS) : min(bt, BN);
+    const int n_seg = (kv == 0 ? KROWS : BN) / ks;
+    const int rowb = kv == 0 ? D : VCOLS;
+    const uint32_t segb = (uint32_t)ks * (rowb + D / 16);
+    const int key_base = pl.kbeg + j * BN + (kv == 0 ? pl.rank * KROWS : 0);
+    const int rel0 = pl.tbl_lo << p.bt_shift;
+    const uint8_t *t = nullptr;
+    int blk = -1, rib = 0;
+    if (lane < n_seg) {
+        const int key = key_base + lane * ks;
         if (key < pl.sk.n_prefix) {
-            int rib;
-            const int idx = block_index(p, key, rib);
-            const uint8_t *t = p2_ptr_of<TBL>(a, pl, sPtr, idx);
-            if (t) {
-                t += v_off;
-                const int s = pu ^ (rib & 7);  // logical 16-column segment
-                r.q[i] = ldg_nc_16(t + (int64_t)rib * D + pu * 16);
-                r.d[i] = ldg_nc_u16(t + (int64_t)bt * D + (int64_t)rib * (D / 16) + (s >> 1) * 2);
-            }
+            const int rel = key - rel0;
+            t = sPtr[rel >> p.bt_shift];
+            blk = sBlk[rel >> p.bt_shift];
+            rib = rel & (bt - 1);
         }
     }
-}
-
-// Dequantise the four units of part kv into the K half [64 rows x 256] or V half [128 rows x 128]
-// operand stage.
-__device__ __forceinline__ void p2_store_dq(const P2Raw &r, int kv, uint8_t *sDst, int dw, int lane, int rank,
-                                            bool &bad) {
-    constexpr int D = 256, VCOLS = 128, W = 128;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        int row, pu;
-        p2_raw_coords(dw, lane, i, kv, rank, row, pu);
-        const int s = pu ^ (row & 7);  // rows of a tile start on 8-row boundaries of their block
-        uint4 lo, hi;
-        dequant16(r.q[i], r.d[i], lo, hi);
-        bad |= f16x8_has_inf(lo) | f16x8_has_inf(hi);
-        const int col = kv == 0 ? 16 * s : 16 * (s - 8 * rank);
-        const int dD = kv == 0 ? D : VCOLS;
-        *(uint4 *)(sDst + tile_elem_off(row, col, dD, W)) = lo;
-        *(uint4 *)(sDst + tile_elem_off(row, col + 8, dD, W)) = hi;
+    const uint32_t segmask = n_seg >= 32 ? 0xffffffffu : ((1u << n_seg) - 1u);
+    const uint32_t valid = __ballot_sync(0xffffffffu, t != nullptr) & segmask;
+    const uint32_t missing = ~valid & segmask;
+    if (missing) {
+        for (uint32_t m = missing; m; m &= m - 1) {
+            uint8_t *z = raw + (__ffs(m) - 1) * segb;
+            for (uint32_t o = lane * 16; o < segb; o += 32 * 16) *(uint4 *)(z + o) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+    }
+    if (lane == 0) mbar_arrive_expect_tx(bar_raw, (uint32_t)__popc(valid) * segb);
+    __syncwarp();
+    if (t) {
+        uint8_t *dst = raw + lane * segb;
+        if (kv == 0) {
+            if (ks == bt) {
+                bulk_g2s(smem_addr(dst), t, segb, bar_raw);  // the whole K tile: qs plane, then scales
+            } else {
+                bulk_g2s(smem_addr(dst), t + (int64_t)rib * D, (uint32_t)ks * D, bar_raw);
+                bulk_g2s(smem_addr(dst + ks * D), t + (int64_t)bt * D + rib * (D / 16), (uint32_t)ks * (D / 16), bar_raw);
+            }
+        } else {
+            const uint8_t *tv = t + (int64_t)p.kv_heads * p.tile_bytes;
+            tma_load_4d(smem_addr(dst), vmap, pl.rank * VCOLS, rib, pl.g, a.layer * p.n_blocks + blk, bar_raw);
+            bulk_g2s(smem_addr(dst + ks * VCOLS), tv + (int64_t)bt * D + rib * (D / 16), (uint32_t)ks * (D / 16), bar_raw);
+        }
+    }
+    // the blocks of tile j + 2 (this CTA's K rows: K and V tiles; the peer prefetches the rest)
+    if (kv == 0 && j + 2 < pl.np_tiles && lane < n_seg) {
+        const int key = key_base + 2 * BN + lane * ks;
+        const int rel = key - rel0;
+        if (key < pl.sk.n_prefix && (rel >> p.bt_shift) < pl.tbl_n) {
+            const uint8_t *tp = sPtr[rel >> p.bt_shift];
+            if (tp) {
+                const uint32_t tb = (uint32_t)p.tile_bytes;
+                if (p.kv_heads == 1) bulk_prefetch_l2(tp, 2 * tb);
+                else {
+                    bulk_prefetch_l2(tp, tb);
+                    bulk_prefetch_l2(tp + (int64_t)p.kv_heads * p.tile_bytes, tb);
+                }
+            }
+        }
     }
 }
 
@@ -362,22 +445,98 @@ __device__ __forceinline__ void p2_produce_bf16(const AttnArgs &a, const P2Plan 
     if (src) bulk_g2s(smem_addr(sDst + dst), src, bytes, bar_full);
 }
 
+// ---- bf16 suffix tile j into this CTA's K half (kv = 0) or V half (kv = 1). From the pool's suffix
+// slot (pre-swizzled rows, as the prefix blocks): one copy of up to 64 K rows, or one 2 KB copy per
+// 8-row group of V, zero-filling rows past the slot. From the caller's row-major buffers: tensor-map
+// loads of 64-column boxes (K: 4 boxes of 64 rows; V: this CTA's 2 boxes of 128 rows), 128-byte
+// swizzled, rows past suffix_len read as zeros; these land chunk-major ([64-column chunk][rows]
+// [128 B]), which the MMA reads with its own descriptors (sfx_desc). ----
+__device__ __forceinline__ void p2_produce_bf16_suffix(const AttnArgs &a, const P2Plan &pl, int j, int kv,
+                                                       uint8_t *sDst, uint32_t bar_full, const void *ksmap,
+                                                       const void *vsmap, int lane) {
+    constexpr int BN = 128, KROWS = 64, RB = 512;
+    const PoolView &p = a.pool;
+    const int s_base = (j - pl.np_tiles) * BN;
+    if (a.k_sfx) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(bar_full, 32768u);
+            if (kv == 0) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tma_load_4d(smem_addr(sDst + c * 8192), ksmap, 64 * c, pl.g, s_base + pl.rank * KROWS, pl.b, bar_full);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+                    tma_load_4d(smem_addr(sDst + c * 16384), vsmap, pl.rank * 128 + 64 * c, pl.g, s_base, pl.b, bar_full);
+            }
+        }
+        __syncwarp();
+        return;
+    }
+    const uint8_t *slot = p.suffix + suffix_tile_index(p, a.layer, pl.sk.seq, kv, pl.g) * p.suffix_tile_bytes;
+    const int n_cp = kv == 0 ? 1 : BN / 8;
+    const uint32_t cp_full = kv == 0 ? (uint32_t)KROWS * RB : 2048u;
+    const uint8_t *src = nullptr;
+    uint32_t bytes = 0;
+    if (lane < n_cp) {
+        const int srow = s_base + (kv == 0 ? pl.rank * KROWS : lane * 8);
+        if (srow < p.suffix_rows) {
+            const int rows = kv == 0 ? min(KROWS, p.suffix_rows - srow) : 8;
+            src = kv == 0 ? slot + (int64_t)srow * RB : slot + (int64_t)(srow >> 3) * 4096 + (int64_t)pl.rank * 2048;
+            bytes = kv == 0 ? (uint32_t)rows * RB : 2048u;
+        }
+    }
+    const uint32_t dst = (uint32_t)lane * cp_full;
+    const uint32_t zlo = dst + bytes, zhi = lane < n_cp ? dst + cp_full : zlo;
+    const uint32_t need_zero = __ballot_sync(0xffffffffu, zhi > zlo);
+    const uint32_t total = __reduce_add_sync(0xffffffffu, src ? bytes : 0u);
+    if (need_zero) {
+        for (uint32_t m = need_zero; m; m &= m - 1) {
+            const int s = __ffs(m) - 1;
+            const uint32_t z0 = __shfl_sync(0xffffffffu, zlo, s), z1 = __shfl_sync(0xffffffffu, zhi, s);
+            for (uint32_t o = z0 + lane * 16; o < z1; o += 32 * 16) *(uint4 *)(sDst + o) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async();
+        __syncwarp();
+    }
+    if (lane == 0) {
+        if (total) mbar_arrive_expect_tx(bar_full, total);
+        else mbar_arrive(bar_full);
+    }
+    __syncwarp();
+    if (src) bulk_g2s(smem_addr(sDst + dst), src, bytes, bar_full);
+}
+
 __device__ __forceinline__ bool p2_xsync(uint32_t xbar, int use, volatile int *abort) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(xbar);
     return mbar_wait(xbar, (uint32_t)use & 1u, abort, kWaitBudget);
 }
 
-// ---- softmax / epilogue (warps 0-7): warp w owns query row (w & 3) * 32 + lane and S columns
-// [64h, 64h + 64), h = w >> 2; the two warps of a lane quarter swap row maxima per tile. P(j) goes
-// back as 16-bit pairs over columns [32h, 32h + 32) of the tile's S buffer; "P(j) written" is one
+// 2^x on the FMA pipe, for part of the softmax's exponentials (the MUFU unit delivers 16 ex2 per
+// clock per SM, the FMA pipe 128 operations): x = n + f with n the nearest integer (the
+// 1.5 * 2^23 rounding constant) and f in [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here
+// for minimum maximum relative error on that interval (Lawson-weighted least squares over
+// Chebyshev nodes; max relative error 7.5e-5, below half an f16 ulp); 2^n added to the exponent
+// field. x is clamped at -125 so that the exponent stays normal; the result there is about 2e-38.
+__device__ __forceinline__ float exp2_fma(float x) {
+    x = fmaxf(x, -125.0f);
+    const float t = x + 12582912.0f;
+    const float f = x - (t - 12582912.0f);
+    const float p = fmaf(fmaf(fmaf(0.0551716648f, f, 0.242611125f), f, 0.693260968f), f, 0.999928057f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// ---- softmax / epilogue (warps 0-15): warp w owns query row (w & 3) * 32 + lane and S columns
+// [32h, 32h + 32), h = w >> 2; the four warps of a lane quarter swap row maxima per tile. P(j) goes
+// back as 16-bit pairs over columns [16h, 16h + 16) of the tile's S buffer; "P(j) written" is one
 // arrival per warp on rank 0's PVK barrier. ----
 template <bool Q8>
 __device__ __forceinline__ void p2_softmax(const AttnArgs &a, const P2Plan &pl, uint8_t *smem, uint32_t bar0,
                                            uint32_t bar0_r0, volatile int *abort, uint32_t tmem, int n, int n_qtiles,
                                            const void *omap, int omode) {
     using C = P2Cfg<Q8>;
-    constexpr int BN = C::BN, D = C::D, DH = D / 2;
+    constexpr int BN = C::BN, D = C::D, SMH = C::SMH, DH = D / SMH;
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int h = warp >> 2, quarter = warp & 3;
@@ -388,26 +547,26 @@ __device__ __forceinline__ void p2_softmax(const AttnArgs &a, const P2Plan &pl, 
     const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
     const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
     const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
-    float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][2 half][128 rows]
-    float *xl = xmax + 4 * kBM;                   // [2 half][128 rows]
+    float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][SMH][128 rows]
+    float *xl = xmax + 2 * SMH * kBM;             // [SMH][128 rows]
     const uint32_t xbar = bar(P2_XCH + quarter);
     int uses = 0;
     float m_used = -INFINITY, l = 0.0f;
     const float inv_scale_log2 = 1.0f / a.scale_log2;
     bool ok = true;
 
-    // Q landed: Q8_0 pools convert this warp's eighth of it to f16 in place; then Q is announced
-    // to rank 0 (K(0)'s barrier also counts the eight softmax warps of each CTA)
+    // Q landed: Q8_0 pools convert this warp's share of it to f16 in place; then Q is announced
+    // to rank 0 (K(0)'s barrier also counts the softmax warps of each CTA)
     ok = mbar_wait(bar(P2_QFULL), 0u, abort, kWaitBudget);
     if (!ok) p2_fail(a, abort, 20);
     if (threadIdx.x == 0) TRACE(2);
     if (ok && Q8) {
         bool bad = false;
         uint8_t *q = smem + C::OFF_Q;
-        const int tid = threadIdx.x;  // 0-255
+        const int tid = threadIdx.x;  // 0 .. 32 * SMW - 1
 #pragma unroll 4
-        for (int i = 0; i < C::Q_BYTES / 16 / 256; ++i) {
-            uint4 *pu = (uint4 *)(q + (size_t)(i * 256 + tid) * 16);
+        for (int i = 0; i < C::Q_BYTES / 16 / (32 * C::SMW); ++i) {
+            uint4 *pu = (uint4 *)(q + (size_t)(i * 32 * C::SMW + tid) * 16);
             uint4 w = *pu;
             w = make_uint4(bf16x2_to_f16x2(w.x), bf16x2_to_f16x2(w.y), bf16x2_to_f16x2(w.z), bf16x2_to_f16x2(w.w));
             bad |= f16x8_has_inf(w);
@@ -426,36 +585,31 @@ __device__ __forceinline__ void p2_softmax(const AttnArgs &a, const P2Plan &pl, 
         tc_fence_after();
         if (r == 0 && h == 0 && jj < 64) TRACE(400 + jj);
         const bool suffix = j >= pl.np_tiles;
-        const int key0 = (suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN) + h * 64;
-        const bool all_vis = suffix ? (suffix_simple && key0 + 64 <= a.suffix_len)
-                                    : (prefix_simple && key0 + 64 <= pl.sk.prefix_valid);
-        uint32_t vb0 = 0xffffffffu, vb1 = 0xffffffffu;
-        if (!all_vis) {
-            vb0 = row_ok ? vis_word(m, suffix, key0, t, pl.sk.prefix_valid, pl.sk.span_b, pl.sk.span_e, a.suffix_len) : 0u;
-            vb1 = row_ok ? vis_word(m, suffix, key0 + 32, t, pl.sk.prefix_valid, pl.sk.span_b, pl.sk.span_e, a.suffix_len)
-                         : 0u;
-        }
+        const int key0 = (suffix ? (j - pl.np_tiles) * BN : pl.kbeg + j * BN) + h * 32;
+        const bool all_vis = suffix ? (suffix_simple && key0 + 32 <= a.suffix_len)
+                                    : (prefix_simple && key0 + 32 <= pl.sk.prefix_valid);
+        const uint32_t vb = all_vis ? 0xffffffffu
+                                    : (row_ok ? vis_word(m, suffix, key0, t, pl.sk.prefix_valid, pl.sk.span_b,
+                                                         pl.sk.span_e, a.suffix_len)
+                                              : 0u);
         const uint32_t s_buf = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
-        uint32_t ra[32], rb[32];
-        tmem_load32x2(s_buf + h * 64, s_buf + h * 64 + 32, ra, rb);
+        uint32_t rr[32];
+        tmem_load32(s_buf + h * 32, rr);
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (all_vis) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(ra[i]));
-                mx[(i + 2) & 3] = fmaxf(mx[(i + 2) & 3], __uint_as_float(rb[i]));
-            }
+            for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(rr[i]));
         } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                mx[i & 3] = fmaxf(mx[i & 3], ((vb0 >> i) & 1u) ? __uint_as_float(ra[i]) : -INFINITY);
-                mx[(i + 2) & 3] = fmaxf(mx[(i + 2) & 3], ((vb1 >> i) & 1u) ? __uint_as_float(rb[i]) : -INFINITY);
-            }
+            for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], ((vb >> i) & 1u) ? __uint_as_float(rr[i]) : -INFINITY);
         }
         const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-        xmax[((jj & 1) * 2 + h) * kBM + r] = cm;
+        float *xm = xmax + (jj & 1) * SMH * kBM;
+        xm[h * kBM + r] = cm;
         if (!(ok = p2_xsync(xbar, uses++, abort))) break;
-        const float rmax = fmaxf(cm, xmax[((jj & 1) * 2 + (h ^ 1)) * kBM + r]);
+        float rmax = cm;
+#pragma unroll
+        for (int o = 1; o < SMH; ++o) rmax = fmaxf(rmax, xm[((h + o) & (SMH - 1)) * kBM + r]);
         if (__any_sync(0xffffffffu, rmax > (m_used + 8.0f) * inv_scale_log2)) {
             const float m_tile = rmax * a.scale_log2;
             float alpha = 1.0f;
@@ -475,45 +629,41 @@ __device__ __forceinline__ void p2_softmax(const AttnArgs &a, const P2Plan &pl, 
                 if (!(ok = mbar_wait(bar(P2_PVDONE + ((jj - 1) & 1)), par2(jj - 1), abort, kWaitBudget))) break;
                 tc_fence_after();
 #pragma unroll 1
-                for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
-                    uint32_t o32[32];
-                    tmem_load32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
+                for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 16) {
+                    uint32_t o16[16];
+                    tmem_load16(tmem + lane_base + (uint32_t)(C::O_COL + c0), o16);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o32[i] = __float_as_uint(__uint_as_float(o32[i]) * alpha);
-                    tmem_st32(tmem + lane_base + (uint32_t)(C::O_COL + c0), o32);
+                    for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
+                    tmem_st16(tmem + lane_base + (uint32_t)(C::O_COL + c0), o16);
                 }
                 tmem_wait_st();
             }
         }
         const float neg_m = -m_used;
-        const bool live = m_used != -INFINITY;
-        const uint32_t pa = live ? vb0 : 0u, pb = live ? vb1 : 0u;
+        const uint32_t pv_bits = (m_used != -INFINITY) ? vb : 0u;
         float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        uint32_t pw[32];
+        uint32_t pw[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            float pr[2], qr[2];
+            float pr[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int c = 2 * i + e;
-                const float x = ex2(fmaf(__uint_as_float(ra[c]), a.scale_log2, neg_m));
-                const float y = ex2(fmaf(__uint_as_float(rb[c]), a.scale_log2, neg_m));
-                pr[e] = ((pa >> c) & 1u) ? x : 0.0f;
-                qr[e] = ((pb >> c) & 1u) ? y : 0.0f;
+                const float xa = fmaf(__uint_as_float(rr[c]), a.scale_log2, neg_m);
+                // one exponential in four on the FMA pipe, the rest on the MUFU unit
+                const float x = (c & 3) == 3 ? exp2_fma(xa) : ex2(xa);
+                pr[e] = ((pv_bits >> c) & 1u) ? x : 0.0f;
                 ps[c & 3] += pr[e];
-                ps[(c + 2) & 3] += qr[e];
             }
             if (Q8) {
-                const __half2 h0 = __floats2half2_rn(pr[0], pr[1]), h1 = __floats2half2_rn(qr[0], qr[1]);
-                pw[i] = *(const uint32_t *)&h0;
-                pw[16 + i] = *(const uint32_t *)&h1;
+                const __half2 h2 = __floats2half2_rn(pr[0], pr[1]);
+                pw[i] = *(const uint32_t *)&h2;
             } else {
-                const __nv_bfloat162 b0 = __floats2bfloat162_rn(pr[0], pr[1]), b1 = __floats2bfloat162_rn(qr[0], qr[1]);
-                pw[i] = *(const uint32_t *)&b0;
-                pw[16 + i] = *(const uint32_t *)&b1;
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(pr[0], pr[1]);
+                pw[i] = *(const uint32_t *)&b2;
             }
         }
-        tmem_st32(s_buf + h * 32, pw);
+        tmem_st16(s_buf + h * 16, pw);
         l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
         tmem_wait_st();
         tc_fence_before();
@@ -528,13 +678,16 @@ __device__ __forceinline__ void p2_softmax(const AttnArgs &a, const P2Plan &pl, 
         tc_fence_after();
     }
     if (r == 0 && h == 0) TRACE(3);
-    // ---- epilogue: row sum over both halves, then this warp's 128 columns of O ----
+    // ---- epilogue: row sum over the four column groups, then this warp's 64 columns of O ----
     xl[h * kBM + r] = l;
     if (ok && !p2_xsync(xbar, uses++, abort)) {
         ok = false;
         p2_fail(a, abort, 7);
     }
-    const float l_row = ok ? xl[r] + xl[kBM + r] : 0.0f;
+    float l_row = 0.0f;
+    if (ok)
+#pragma unroll
+        for (int o = 0; o < SMH; ++o) l_row += xl[o * kBM + r];
     const bool have_o = ok && n > 0;
     const bool split = a.n_splits > 1;
     const float inv = split ? 1.0f : ((have_o && l_row > 0.0f) ? 1.0f / l_row : 0.0f);
@@ -548,16 +701,51 @@ __device__ __forceinline__ void p2_softmax(const AttnArgs &a, const P2Plan &pl, 
             wml[1] = have_o ? l_row : 0.0f;
         }
     }
-    // the Q area and the K stages are free once the last P.V has finished: they stage the boxes
-    epilogue_o_tma(a, pl.qrow0, pl.rows_valid, pl.g, pl.b, omap, omode, smem, quarter, lane,
-                   tmem + lane_base + (uint32_t)C::O_COL, h * DH, (h + 1) * DH, have_o, inv, f32, unit, 2 + h);
+    // the Q area and the K stages are free once the last P.V has finished: they stage the boxes.
+    // This warp's 64 columns, 32 at a time (one tensor-memory load in flight keeps the registers
+    // within the softmax budget), staged as the 32-row boxes of epilogue_o_tma; the four warps of
+    // the column range meet at named barrier 2 + h and one lane stores each 128-row box.
+    {
+        const int boxc = f32 ? 32 : 64;
+        const uint32_t o_taddr = tmem + lane_base + (uint32_t)C::O_COL;
+#pragma unroll 1
+        for (int c0 = h * DH; c0 < (h + 1) * DH; c0 += 32) {
+            uint32_t o32[32];
+            if (have_o) {
+                tmem_load32(o_taddr + (uint32_t)c0, o32);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o32[i] = 0u;
+            }
+            stage_o_box<32>(smem, quarter, lane, c0, o32, inv, f32);
+        }
+        fence_proxy_async();
+        asm volatile("bar.sync %0, 128;" ::"r"(2 + h) : "memory");
+        bool issued = false;
+        const int c0 = h * DH;
+        const int cb = c0 / boxc + quarter;
+        if (lane == 0 && pl.rows_valid > 0 && cb < (c0 + DH) / boxc) {
+            const uint32_t src = smem_addr(smem + cb * 4 * kOutBox);
+            if (omode == OUT_TMA_ROWS)
+                tma_store_5d(omap, src, cb * boxc, pl.qrow0 % a.group, pl.g, pl.qrow0 / a.group, pl.b);
+            else
+                tma_store_2d(omap, src, cb * boxc, (int)(unit * kBM));
+            issued = true;
+        }
+        if (issued) {
+            bulk_commit_group();
+            bulk_wait_group_read0();
+        }
+        __syncwarp();
+    }
     if (r == 0 && h == 0) TRACE(4);
 }
 
 template <bool Q8>
 __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
     attn_pair128_kernel(const AttnArgs a, int n_qtiles, const __grid_constant__ CUtensorMap qmap,
-                        const __grid_constant__ CUtensorMap omap, int omode) {
+                        const __grid_constant__ CUtensorMap omap, int omode, const __grid_constant__ CUtensorMap vmap,
+                        const __grid_constant__ CUtensorMap ksmap, const __grid_constant__ CUtensorMap vsmap) {
     using C = P2Cfg<Q8>;
     constexpr int D = C::D;
     extern __shared__ uint8_t smem_raw[];
@@ -570,6 +758,7 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
     uint32_t *tmem_holder = (uint32_t *)(bars + P2_N);
     volatile int *abort = (volatile int *)(bars + P2_N + 1);
     const uint8_t **sPtr = (const uint8_t **)(smem + C::OFF_TBL);
+    int32_t *sBlk = (int32_t *)(smem + C::OFF_BLK);
     const uint32_t bar0 = smem_addr(bars);
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -584,8 +773,8 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
     if (threadIdx.x == 0 && !pl.sk.ok) report_error(a.pool.status, DEV_ERR_BAD_SEQ, pl.b, a.seq_ids[pl.b], 3);
 
     if (threadIdx.x == 0) {
-        // producers per CTA of K or V: the eight dequantising warps (Q8_0) or the relay warp (bf16)
-        constexpr uint32_t per_rank = Q8 ? C::NDQ / 32 : 1;
+        // producers per CTA of K or of V: four dequantising warps each (Q8_0) or the relay warp (bf16)
+        constexpr uint32_t per_rank = Q8 ? C::NDQ / 64 : 1;
         mbar_init(bar(P2_QFULL), 1);
         mbar_init(bar(P2_KINIT), 2 * per_rank + 2 * C::SMW);
         mbar_init(bar(P2_KINIT + 1), 2 * per_rank);
@@ -597,7 +786,12 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
             mbar_init(bar(P2_VFULL + s), 1);
         }
         mbar_init(bar(P2_DONE), 1);
-        for (int q = 0; q < 4; ++q) mbar_init(bar(P2_XCH + q), 2);
+        for (int q = 0; q < 4; ++q) mbar_init(bar(P2_XCH + q), C::SMH);
+        for (int s2 = 0; s2 < 2; ++s2) {
+            mbar_init(bar(P2_RAWK + s2), 1);
+            mbar_init(bar(P2_RAWV + s2), 1);
+            mbar_init(bar(P2_TEAM + s2), C::NDQ / 64);  // the four warps of a team
+        }
         *abort = 0;
         mbar_init_fence();
     }
@@ -606,6 +800,7 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
         for (int i = threadIdx.x; i < pl.tbl_n; i += C::THREADS) {
             const int blk = lookup_block(a.pool, pl.sk.seq, pl.tbl_lo + i);
             sPtr[i] = blk < 0 ? nullptr : a.pool.prefix + prefix_tile_index(a.pool, a.layer, blk, 0, pl.g) * a.pool.tile_bytes;
+            sBlk[i] = blk;
         }
     tc_fence_before();
     __syncthreads();
@@ -614,13 +809,13 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
     const uint32_t tmem = *tmem_holder;
     const int n = pl.j1 - pl.j0;
     if (threadIdx.x == 0) TRACE(1);
-    // Q8_0: 640 threads launch at 96 registers (61,440); each warpgroup sets its own budget as it
-    // enters its role -- the softmax warpgroups 120, the dequantisers 88, the MMA / feeder warpgroup
-    // 56: 256 x 120 + 256 x 88 + 128 x 56 = 60,416
-    static_assert(!Q8 || (C::THREADS == 640 && C::SMW == 8 && C::DQ_WARP0 == 12), "warpgroup register split");
+    // Q8_0: 896 threads launch at 72 registers (64,512); each warpgroup sets its own budget as it
+    // enters its role -- softmax 64, MMA / feeders 72, dequantisers 88: 512 x 64 + 128 x 72 + 256 x 88
+    // = 64,512 (the decreases release exactly what the increase takes)
+    static_assert(!Q8 || (C::THREADS == 896 && C::SMW == 16 && C::DQ_WARP0 == 20), "warpgroup register split");
     const int wg = warp >> 2;
-    if (wg == 2) {
-    if constexpr (Q8) warpgroup_reg_dealloc<56>();
+    if (wg == C::SMW / 4) {
+    if constexpr (Q8) warpgroup_reg_dealloc<72>();
     if (warp == C::MMA_WARP) {
         if (pl.rank == 0 && n > 0 && lane == 0) {
             // ---- MMA issue for the pair: S(0), S(1), then P.V(j) and S(j + 2) per tile, one wait ----
@@ -628,17 +823,23 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
             const uint32_t idO = idesc_f16_m(!Q8, true, D, 256);
             const uint32_t q_addr = smem_addr(sQ), k_addr = smem_addr(sK), v_addr = smem_addr(sV);
             const uint64_t qd0 = sdesc(q_addr, 16, C::Q_SBO, C::LAYOUT);
+            // bf16 suffix tiles read from the caller's buffers land chunk-major (tensor-map boxes of
+            // 64 columns): K 8-row groups 1 KB apart and 64-column chunks 8 KB apart; V 8-key groups
+            // 1 KB apart and 64-column chunks 16 KB apart
+            const bool sfx_tma = !Q8 && a.k_sfx != nullptr;
             auto issue_s = [&](int jj) {
                 const int st = jj & 1;
                 const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)(st * C::BN);
-                const uint64_t kd0 = sdesc(k_addr + st * C::K_BYTES, 16, C::K_SBO, C::LAYOUT);
+                const bool chunk_major = sfx_tma && pl.j0 + jj >= pl.np_tiles;
+                const uint64_t kd0 = sdesc(k_addr + st * C::K_BYTES, 16, chunk_major ? 1024u : C::K_SBO, C::LAYOUT);
+                const uint32_t kstep = chunk_major ? 8192u : 1024u;
 #pragma unroll
                 for (int g = 0; g < D / 64; ++g) {
                     uint64_t av[4], bv[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         av[i] = qd0 + (((uint32_t)g * C::Q_CHUNK + (uint32_t)i * 32u) >> 4);
-                        bv[i] = kd0 + (((uint32_t)g * 1024u + (uint32_t)i * 32u) >> 4);
+                        bv[i] = kd0 + (((uint32_t)g * kstep + (uint32_t)i * 32u) >> 4);
                     }
                     mma_ss_x4<true>(d_tmem, av, bv, idS, g > 0 ? 1u : 0u);
                 }
@@ -652,7 +853,9 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
                 if (!mbar_wait(bar(P2_PVK + st), par2(jj), abort, kWaitBudget)) return false;
                 tc_fence_after();
                 if (jj < 64) TRACE(200 + jj);
-                const uint64_t vd0 = sdesc(v_addr + st * C::V_BYTES, C::V_LBO, C::V_SBO, C::LAYOUT);
+                const bool chunk_major = sfx_tma && pl.j0 + jj >= pl.np_tiles;
+                const uint32_t vsbo = chunk_major ? 1024u : C::V_SBO;
+                const uint64_t vd0 = sdesc(v_addr + st * C::V_BYTES, chunk_major ? 16384u : C::V_LBO, vsbo, C::LAYOUT);
 #pragma unroll
                 for (int g = 0; g < 2; ++g) {
                     uint32_t av[4];
@@ -661,7 +864,7 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
                     for (int i = 0; i < 4; ++i) {
                         const int kk = g * 4 + i;
                         av[i] = tmem + C::S_COL + (uint32_t)(st * C::BN + kk * 8);
-                        bv[i] = vd0 + (((uint32_t)kk * 2u * C::V_SBO) >> 4);
+                        bv[i] = vd0 + (((uint32_t)kk * 2u * vsbo) >> 4);
                     }
                     mma_ts_x4<true>(tmem + C::O_COL, av, bv, idO, (jj > 0 || g > 0) ? 1u : 0u);
                 }
@@ -696,7 +899,27 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
                 tma_load_5d(smem_addr(sQ + c * C::Q_CHUNK), &qmap, 64 * c, 0, pl.g, t0, pl.b, bar(P2_QFULL));
         }
         __syncwarp();
-        if constexpr (!Q8) {
+        if constexpr (Q8) {
+            // raw Q8_0 bytes of each prefix tile into the upper part of its stage, once the stage is
+            // free: S(j - 2) (K) or P.V(j - 2) (V) done
+            const int np = min(n, max(0, pl.np_tiles - pl.j0));
+            const int b_free = kv ? P2_PVDONE : P2_SFULL;
+            int issued = 0;
+            for (int it = 0; it < np; ++it) {
+                const int st = it & 1;
+                if (it >= 2 && !mbar_wait(bar(b_free + st), par2(it - 2), abort, kWaitBudget)) {
+                    p2_fail(a, abort, 2);
+                    break;
+                }
+                uint8_t *raw = kv ? sV + st * C::V_BYTES + C::RAWV_OFF : sK + st * C::K_BYTES + C::RAWK_OFF;
+                p2_stage_raw(a, pl, (const uint8_t *const *)sPtr, sBlk, &vmap, pl.j0 + it, kv, raw,
+                             bar((kv ? P2_RAWV : P2_RAWK) + st), lane);
+                issued = it + 1;
+            }
+            if (lane == 0 && *abort)
+                for (int jj = max(0, issued - 2); jj < issued; ++jj)
+                    mbar_wait(bar((kv ? P2_RAWV : P2_RAWK) + (jj & 1)), par2(jj), abort, kWaitBudget / 4);
+        } else {
             uint8_t *stages = kv ? sV : sK;
             const int sbytes = kv ? C::V_BYTES : C::K_BYTES;
             const int b_full = kv ? P2_VFULL : P2_KFULL;
@@ -710,10 +933,7 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
                 }
                 const int j = pl.j0 + it;
                 if (j >= pl.np_tiles) {
-                    p2_suffix_stage<false>(a, pl, j, kv, stages + st * sbytes, lane, 32, abort);
-                    fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(bar(b_full + st));
+                    p2_produce_bf16_suffix(a, pl, j, kv, stages + st * sbytes, bar(b_full + st), &ksmap, &vsmap, lane);
                 } else {
                     p2_produce_bf16<C::TBL>(a, pl, (const uint8_t *const *)sPtr, j, kv, stages + st * sbytes,
                                             bar(b_full + st), lane);
@@ -748,48 +968,51 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
     }
     } else if (warp >= C::DQ_WARP0) {
         if constexpr (Q8) {
-            warpgroup_reg_dealloc<88>();
+            warpgroup_reg_alloc<88>();
             const int dtid = threadIdx.x - C::DQ_WARP0 * 32;
-            const int dw = dtid >> 5;
+            const int kv = dtid >> 7;          // team: 0 = K (warps 0-3), 1 = V (warps 4-7)
+            const int ptid = dtid & 127;
             const int np = min(n, max(0, pl.np_tiles - pl.j0));  // prefix tiles of this split
+            const uint32_t team_bar = bar(P2_TEAM + kv);
             bool bad = false;
-            // one tile ahead: part kv of tile j + 1 is loaded right after part kv of tile j is stored
-            P2Raw rk, rv;
-            if (np > 0) {
-                p2_load_raw<C::TBL>(a, pl, (const uint8_t *const *)sPtr, pl.j0, 0, dw, lane, rk);
-                p2_load_raw<C::TBL>(a, pl, (const uint8_t *const *)sPtr, pl.j0, 1, dw, lane, rv);
-            }
-            auto publish = [&](int rbar) {
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_remote(bar0_r0 + 8u * (uint32_t)rbar);
-            };
             bool ok = true;
             for (int jj = 0; jj < n; ++jj) {
                 const int j = pl.j0 + jj, st = jj & 1;
-                uint8_t *kdst = sK + st * C::K_BYTES, *vdst = sV + st * C::V_BYTES;
-                // K stage j % 2 free once S(j - 2) is done, V stage once P.V(j - 2) is
-                if (jj >= 2 && !(ok = mbar_wait(bar(P2_SFULL + st), par2(jj - 2), abort, kWaitBudget))) break;
-                if (jj < np) p2_store_dq(rk, 0, kdst, dw, lane, pl.rank, bad);
-                else p2_suffix_stage<true>(a, pl, j, 0, kdst, dtid, C::NDQ, abort);
-                publish(p2_k_bar(jj));
-                if (dtid == 0 && jj < 64) TRACE(600 + jj);
-                if (jj + 1 < np) p2_load_raw<C::TBL>(a, pl, (const uint8_t *const *)sPtr, j + 1, 0, dw, lane, rk);
-                if (jj >= 2 && !(ok = mbar_wait(bar(P2_PVDONE + st), par2(jj - 2), abort, kWaitBudget))) break;
-                if (jj < np) p2_store_dq(rv, 1, vdst, dw, lane, pl.rank, bad);
-                else p2_suffix_stage<true>(a, pl, j, 1, vdst, dtid, C::NDQ, abort);
-                publish(P2_PVK + st);
-                if (dtid == 0 && jj < 64) TRACE(700 + jj);
-                if (jj + 1 < np) p2_load_raw<C::TBL>(a, pl, (const uint8_t *const *)sPtr, j + 1, 1, dw, lane, rv);
+                uint8_t *dst = kv == 0 ? sK + st * C::K_BYTES : sV + st * C::V_BYTES;
+                if (jj < np) {
+                    // the raw part landed (its feeder waited for the stage to be free)
+                    if (!(ok = mbar_wait(bar((kv ? P2_RAWV : P2_RAWK) + st), par2(jj), abort, kWaitBudget))) break;
+                    if (ptid == 0 && kv == 0 && jj < 64) TRACE(800 + jj);
+                    p2_dequant_part<Q8>(dst + (kv ? C::RAWV_OFF : C::RAWK_OFF), kv, pl.rank, a.pool.block_tokens, dst,
+                                        ptid, team_bar, jj, abort, bad, ok);
+                    if (!ok) break;
+                } else {
+                    // suffix tile: K stage j % 2 free once S(j - 2) is done, V stage once P.V(j - 2) is
+                    if (jj >= 2 && !(ok = mbar_wait(bar((kv == 0 ? P2_SFULL : P2_PVDONE) + st), par2(jj - 2), abort,
+                                                    kWaitBudget)))
+                        break;
+                    p2_suffix_stage<true>(a, pl, j, kv, dst, ptid, C::NDQ / 2, abort);
+                }
+                if (ptid == 0 && kv == 0 && jj < 64) TRACE(900 + jj);
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(bar0_r0 + 8u * (uint32_t)(kv == 0 ? p2_k_bar(jj) : P2_PVK + st));
+                if (ptid == 0 && jj < 64) TRACE((kv == 0 ? 600 : 700) + jj);
             }
             if (!ok) p2_fail(a, abort, 6);
             if (bad) report_error(a.pool.status, DEV_ERR_F16_RANGE, 2, pl.b, pl.j0);
-            // K of the (up to two) tiles past the end still arrives, so the last PVK phases complete
-            if (ok && lane == 0)
-                for (int t = max(n, 2); t < n + 2; ++t) mbar_arrive_remote(bar0_r0 + 8u * (uint32_t)p2_k_bar(t));
+            // K of the (up to two) tiles past the end still arrives, so the last PVK phases complete;
+            // like a real K(t), only once S(t - 2) is done: that is when the phase of PVK((t - 2) % 2)
+            // it belongs to has begun (PVK(t - 4) completed before S(t - 2) was issued)
+            if (ok && kv == 0)
+                for (int t = max(n, 2); t < n + 2; ++t) {
+                    if (!(ok = mbar_wait(bar(P2_SFULL + (t & 1)), par2(t - 2), abort, kWaitBudget))) break;
+                    if (lane == 0) mbar_arrive_remote(bar0_r0 + 8u * (uint32_t)p2_k_bar(t));
+                }
+            if (!ok) p2_fail(a, abort, 9);
         }
     } else {
-        if constexpr (Q8) warpgroup_reg_alloc<120>();
+        if constexpr (Q8) warpgroup_reg_dealloc<64>();
         p2_softmax<Q8>(a, pl, smem, bar0, bar0_r0, abort, tmem, n, n_qtiles, &omap, omode);
     }
     __syncwarp();
@@ -822,6 +1045,44 @@ bool make_q_map(const AttnArgs &a, CUtensorMap *map) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tensor maps of the caller's bf16 suffix K or V ([n_batch][suffix_len][kv_heads][256]) as (column,
+// KV head, row, request), boxes of 64 columns x `rows` rows, 128-byte swizzled.
+bool make_suffix_map(const AttnArgs &a, const void *base, int rows, CUtensorMap *map) {
+    std::memset(map, 0, sizeof(*map));
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc || !base || ((uintptr_t)base & 15) || a.suffix_len <= 0) return false;
+    constexpr int D = 256, es = 2;
+    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)a.pool.kv_heads, (cuuint64_t)a.suffix_len,
+                                (cuuint64_t)a.n_batch};
+    const cuuint64_t strides[3] = {(cuuint64_t)D * es, (cuuint64_t)a.pool.kv_heads * D * es,
+                                   (cuuint64_t)a.suffix_len * a.pool.kv_heads * D * es};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, (void *)base, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tensor map of the Q8_0 pool's V int8 planes, for copying one CTA's half of the columns of a
+// block's rows: (256 bytes of a row, block rows, KV head, layer * n_blocks + block) over the V tiles
+// of the prefix arena, boxes of 128 bytes x min(block, 128) rows.
+bool make_vraw_map(const AttnArgs &a, CUtensorMap *map) {
+    std::memset(map, 0, sizeof(*map));
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    const PoolView &p = a.pool;
+    if (!enc) return false;
+    const int64_t blocks = (int64_t)p.n_layers * p.n_blocks;
+    if (blocks > 0x7fffffff) return false;
+    const cuuint64_t dims[4] = {256, (cuuint64_t)p.block_tokens, (cuuint64_t)p.kv_heads, (cuuint64_t)blocks};
+    const cuuint64_t strides[3] = {256, (cuuint64_t)p.tile_bytes, (cuuint64_t)(2 * p.kv_heads * p.tile_bytes)};
+    const cuuint32_t box[4] = {128, (cuuint32_t)std::min(p.block_tokens, 128), 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    void *base = p.prefix + (int64_t)p.kv_heads * p.tile_bytes;  // V tile of block 0, head 0, layer 0
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 #ifdef EKV_TRACE
@@ -838,7 +1099,9 @@ int pair128_choose_splits(int64_t pair_units, int max_tiles, int sms) {
 
 bool pair128_supported(const AttnArgs &a) {
     const int bt = a.pool.block_tokens;
+    // power-of-two blocks of at least 8 rows; every block of a split fits the shared pointer table
     return a.pool.head_dim == 256 && a.group > 0 && kBM % a.group == 0 && (bt & (bt - 1)) == 0 && bt >= 8 &&
+           a.pool.max_blocks_per_seq <= P2Cfg<true>::TBL && a.pool.max_blocks_per_seq <= P2Cfg<false>::TBL &&
            !((uintptr_t)a.q & 15) && !((uintptr_t)a.out & 15);
 }
 
@@ -889,11 +1152,20 @@ int launch_attention_pair128(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sm
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CUtensorMap omap;
+    CUtensorMap omap, vmap;
     const int omode = make_out_map(a, 256, (int64_t)a.n_batch * a.pool.kv_heads * n_qtiles, &omap);
     if (omode == OUT_THREADS) return EKV_ERR_UNSUPPORTED;
-    const cudaError_t e = q8 ? cudaLaunchKernelEx(&cfg, attn_pair128_kernel<true>, a, n_qtiles, qmap, omap, omode)
-                             : cudaLaunchKernelEx(&cfg, attn_pair128_kernel<false>, a, n_qtiles, qmap, omap, omode);
+    std::memset(&vmap, 0, sizeof(vmap));
+    if (q8 && !make_vraw_map(a, &vmap)) return EKV_ERR_UNSUPPORTED;
+    CUtensorMap ksmap, vsmap;
+    std::memset(&ksmap, 0, sizeof(ksmap));
+    std::memset(&vsmap, 0, sizeof(vsmap));
+    if (!q8 && a.k_sfx && a.suffix_len > 0 &&
+        (!make_suffix_map(a, a.k_sfx, 64, &ksmap) || !make_suffix_map(a, a.v_sfx, 128, &vsmap)))
+        return EKV_ERR_UNSUPPORTED;
+    const cudaError_t e =
+        q8 ? cudaLaunchKernelEx(&cfg, attn_pair128_kernel<true>, a, n_qtiles, qmap, omap, omode, vmap, ksmap, vsmap)
+           : cudaLaunchKernelEx(&cfg, attn_pair128_kernel<false>, a, n_qtiles, qmap, omap, omode, vmap, ksmap, vsmap);
     if (e != cudaSuccess) return EKV_ERR_CUDA;
     note_launches(1);
     if (a.n_splits > 1) return launch_merge_splits(a, n_qtiles, s);

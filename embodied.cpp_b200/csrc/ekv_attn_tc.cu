@@ -1551,6 +1551,13 @@ int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k) {
     // each K/V byte crosses L2 -> SM twice per request instead of four times
     const bool pair = a.pool.head_dim == 256 && k != TcKernel::OneCta;
     if (pair && k == TcKernel::Pair) return launch_attention_pair128(a, s, ws, sm_count());
+    // bf16 pools: the 128-key pair kernel where the shape allows it. Q8_0 pools keep the 64-key pair
+    // kernel: with Q in shared memory, the N = 128 MMAs' operand reads leave too little shared-memory
+    // bandwidth for the in-place dequantisation of every tile.
+    if (pair && k == TcKernel::Auto && a.pool.dtype == EKV_DTYPE_BF16) {
+        const int rc = launch_attention_pair128(a, s, ws, sm_count());
+        if (rc != EKV_ERR_UNSUPPORTED) return rc;
+    }
     if (pair) return launch_attention_pair(a, s, ws, sm_count());
     return a.pool.dtype == EKV_DTYPE_Q8_0 ? dispatch<true>(a, s, ws) : dispatch<false>(a, s, ws);
 }

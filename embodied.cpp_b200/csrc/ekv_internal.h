@@ -66,10 +66,11 @@ int launch_gather(const PoolView &p, int layer, int seq, int pos0, int n_rows, i
 int launch_gather_suffix(const PoolView &p, int layer, int seq, int n_rows, int format,
                          void *k_out, void *v_out, cudaStream_t s);
 int launch_attention_simt(const AttnArgs &a, cudaStream_t s);
-// Which tcgen05 kernel runs a call at head_dim 256: Auto and Pair64 = the 64-key CTA-pair kernel
-// (ekv_attn_pair.cu); Pair = the 128-key CTA-pair kernel (ekv_attn_pair128.cu) where the call's
-// shape allows it (query group dividing 128, power-of-two blocks), else EKV_ERR_UNSUPPORTED;
-// OneCta = one CTA per 128 query rows. Other head dims always run one CTA per 128 query rows.
+// Which tcgen05 kernel runs a call at head_dim 256: Auto = the 128-key CTA-pair kernel
+// (ekv_attn_pair128.cu) for bf16 pools where the call's shape allows it (query group dividing 128,
+// power-of-two blocks), else the 64-key CTA-pair kernel (ekv_attn_pair.cu); Pair = the 128-key
+// pair kernel or EKV_ERR_UNSUPPORTED; Pair64 = the 64-key pair kernel; OneCta = one CTA per 128
+// query rows. Other head dims always run one CTA per 128 query rows.
 enum class TcKernel { Auto, Pair, OneCta, Pair64 };
 int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k);
 size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix);

@@ -402,6 +402,19 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const void *map, int c
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void *map, int c0, int c1, int c2, int c3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
+
+// Ask the copy engine to bring `bytes` (a multiple of 16) at a 16-byte aligned global address into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // 16-byte global load through the non-coherent path without allocating in L1 (data read once per SM).
 __device__ __forceinline__ uint4 ldg_nc_16(const void *p) {
     uint4 v;

@@ -200,8 +200,9 @@ int ekv_attention(ekv_pool *pool, const ekv_attn_params *p, const void *q, void 
 int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                           ekv_stream_t stream);
 
-#define EKV_ALGO_TC 0      /* tcgen05 tensor cores (default): CTA pairs with 64-key tiles for
-                              head_dim 256, the one-CTA kernel otherwise                      */
+#define EKV_ALGO_TC 0      /* tcgen05 tensor cores (default): CTA pairs for head_dim 256 (128-key
+                              tiles for bf16 pools where EKV_ALGO_TC_PAIR supports the shape,
+                              64-key tiles otherwise), the one-CTA kernel for other head dims  */
 #define EKV_ALGO_SIMT 1    /* one-warp-per-row CUDA-core kernel, kept as a GPU cross-check   */
 #define EKV_ALGO_TC_PAIR 2 /* head_dim 256 on CTA pairs (tcgen05 cta_group::2, 256 query rows
                               per pair, each K/V tile split between the two CTAs) with 128-key
@@ -211,8 +212,8 @@ int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, const void *
 #define EKV_ALGO_TC_CTA 3  /* the one-CTA tcgen05 kernel (128 query rows per CTA) for every
                               head dim                                                        */
 #define EKV_ALGO_TC_PAIR64 4 /* head_dim 256 on CTA pairs with 64-key tiles and Q in tensor
-                              memory (what EKV_ALGO_TC runs at head_dim 256); other head dims
-                              as EKV_ALGO_TC                                                  */
+                              memory (what EKV_ALGO_TC runs for Q8_0 pools at head_dim 256);
+                              other head dims as EKV_ALGO_TC                                  */
 int ekv_attention_algo(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                        void *workspace, size_t workspace_bytes, int32_t algo,
                        ekv_stream_t stream);
