@@ -93,15 +93,31 @@ __device__ __forceinline__ uint32_t range_bits(int lo, int hi, int w0) {
     return upto_b & ~below_a;
 }
 
-// Visibility of keys [w0, w0+32) for query token t, from key ranges (no per-key loop):
-// the predicate of prefix_allowed / suffix_allowed in closed form.
+// FLEX masks: the bits of `bits` (keys key0 + i of the call's key order) that query token t may see;
+// one metadata word per candidate key.
+__device__ __forceinline__ uint32_t flex_word(const MaskDesc &m, int t, int key0, uint32_t bits) {
+    const uint32_t qm = (uint32_t)__ldg(m.flex + m.flex_q0 + t);
+    if ((qm >> 24) == 0u) return 0u;
+    uint32_t out = 0u;
+    for (uint32_t rem = bits; rem; rem &= rem - 1u) {
+        const int i = __ffs(rem) - 1;
+        const uint32_t km = (uint32_t)__ldg(m.flex + m.flex_k0 + key0 + i);
+        if (flex_allowed(m.flags, qm, km, m.flex_window)) out |= 1u << i;
+    }
+    return out;
+}
+
+// Visibility of keys [w0, w0+32) for query token t, from key ranges (no per-key loop except for
+// the FLEX masks' metadata): the predicate of prefix_allowed / suffix_allowed in closed form.
+// n_prefix places suffix keys in the call's key order (FLEX metadata index).
 __device__ __forceinline__ uint32_t vis_word(const MaskDesc &m, bool suffix, int w0, int t, int prefix_valid,
-                                             int span_b, int span_e, int suffix_len) {
+                                             int span_b, int span_e, int suffix_len, int n_prefix = 0) {
     if (suffix) {
         int hi = suffix_len;
         if (m.flags & EKV_MASK_SUFFIX_CAUSAL) hi = min(hi, t + 1);
         if ((m.flags & EKV_MASK_SUFFIX_PREFIX_LM) && t == 0) hi = min(hi, 1);
-        return range_bits(0, hi, w0);
+        const uint32_t sbits = range_bits(0, hi, w0);
+        return (m.flags & kFlexFlags) ? flex_word(m, t, n_prefix + w0, sbits) : sbits;
     }
     uint32_t bits = range_bits(0, prefix_valid, w0);
     if (m.flags & EKV_MASK_SPAN_ONLY) bits &= range_bits(span_b, span_e, w0);
@@ -115,6 +131,7 @@ __device__ __forceinline__ uint32_t vis_word(const MaskDesc &m, bool suffix, int
             win |= range_bits(kc * m.chunk_stride, kc * m.chunk_stride + m.chunk_tokens, w0);
         bits &= win;
     }
+    if (m.flags & kFlexFlags) bits = flex_word(m, t, w0, bits);
     return bits;
 }
 

@@ -492,9 +492,9 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
     const uint32_t lane_base = ((uint32_t)(quarter * 32)) << 16;
     const bool row_ok = r < pl.rows_valid;
     const int t = (pl.qrow0 + r) / a.group;
-    const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
-    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
-    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
+    const MaskDesc m = mask_desc(a, pl.b);
+    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kFlexFlags));
+    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kFlexFlags));
     float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][2 half][128 rows]
     float *xl = xmax + 4 * kBM;                   // [2 half][128 rows]
     const uint32_t xbar = bar(PB_XCH + quarter);
@@ -514,7 +514,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
                                     : (prefix_simple && key0 + 32 <= pl.sk.prefix_valid);
         const uint32_t vb = all_vis ? 0xffffffffu
                                     : (row_ok ? vis_word(m, suffix, key0, t, pl.sk.prefix_valid, pl.sk.span_b,
-                                                         pl.sk.span_e, a.suffix_len)
+                                                         pl.sk.span_e, a.suffix_len, pl.sk.n_prefix)
                                               : 0u);
         const uint32_t s_buf = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
         uint32_t rr[32];

@@ -45,7 +45,7 @@ __global__ void attn_simt_kernel(AttnArgs a) {
     const SeqKeys sk = resolve_seq(p, a.use_prefix, a.seq_ids, a.prefix_len, a.prefix_valid, a.span_begin,
                                    a.span_end, b);
     if (!sk.ok && lane == 0) report_error(p.status, DEV_ERR_BAD_SEQ, b, a.seq_ids[b], 2);
-    const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
+    const MaskDesc m = mask_desc(a, b);
 
     float qv[kMaxPerLane], acc[kMaxPerLane];
     const uint16_t *qrow = a.q + (((int64_t)b * a.q_tokens + t) * a.q_heads + h) * D;
@@ -79,7 +79,7 @@ __global__ void attn_simt_kernel(AttnArgs a) {
             ks.q8 = vs.q8 = q8;
         } else {
             const int s = k - n_prefix;
-            vis = suffix_allowed(m, t, s, a.suffix_len);
+            vis = suffix_allowed(m, t, s, a.suffix_len, n_prefix);
             if (!vis) continue;
             ks.tile = p.suffix + suffix_tile_index(p, a.layer, sk.seq, 0, g) * p.suffix_tile_bytes;
             vs.tile = p.suffix + suffix_tile_index(p, a.layer, sk.seq, 1, g) * p.suffix_tile_bytes;

@@ -551,9 +551,9 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
     const bool row_ok = PACK ? (s_row < a.pack && pt->unit[s_row].rows_valid > 0) : r < pl.rows_valid;
     const int t = PACK ? (r - s_row * rpu) / a.group : (pl.qrow0 + r) / a.group;
     int s_tile = 0, first_tile = 0;  // unit of the current tile, and that unit's first CTA tile
-    const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
-    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
-    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
+    const MaskDesc m = mask_desc(a, pl.b);  // packed units never carry FLEX masks (the launcher checks)
+    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kFlexFlags));
+    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kFlexFlags));
     float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][H][128 rows]
     float *xl = xmax + 2 * H * kBM;               // [H][128 rows]
     const uint32_t xbar = bar(BAR_XCH + quarter);
@@ -591,7 +591,7 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
                              : (prefix_simple && key0 + 32 <= pl.sk.prefix_valid);
             vb = all_vis ? 0xffffffffu
                          : (row_ok ? vis_word(m, suffix, key0, t, pl.sk.prefix_valid, pl.sk.span_b, pl.sk.span_e,
-                                              a.suffix_len)
+                                              a.suffix_len, pl.sk.n_prefix)
                                    : 0u);
         }
         const uint32_t s_buf = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
@@ -1105,9 +1105,9 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
         const bool row_ok = r < pl.rows_valid;
         const int qr = pl.qrow0 + r;
         const int t = qr / a.group;
-        const MaskDesc m{a.mask_flags, a.chunk_tokens, a.chunk_stride, a.window_chunks, a.q_chunk0};
-        const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL));
-        const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM));
+        const MaskDesc m = mask_desc(a, pl.b);
+        const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kFlexFlags));
+        const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kFlexFlags));
         float m_used = -INFINITY, l = 0.0f;
         const float inv_scale_log2 = 1.0f / a.scale_log2;
         bool ok = true;
@@ -1129,7 +1129,7 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
             for (int w = 0; w < BN / 32; ++w)
                 vis_bits[w] = all_vis ? 0xffffffffu
                                       : (row_ok ? vis_word(m, suffix, key0 + 32 * w, t, pl.sk.prefix_valid, pl.sk.span_b,
-                                                           pl.sk.span_e, a.suffix_len)
+                                                           pl.sk.span_e, a.suffix_len, pl.sk.n_prefix)
                                                 : 0u);
             const uint32_t s_col = tmem + lane_base + C::S_COL + (uint32_t)(sb * BN);
             // common case: one pass, no new maximum (see softmax_tile_1pass)
@@ -1431,7 +1431,7 @@ int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
         // (and its set-up) per unit. Only when the units outnumber the SMs; no key splits.
         const int rpu = a.q_tokens * a.group;
         const int64_t n_units = (int64_t)a.n_batch * a.pool.kv_heads;
-        if (2 * rpu <= kBM && n_units > sm_count()) {
+        if (2 * rpu <= kBM && n_units > sm_count() && !(a.mask_flags & kFlexFlags)) {
             a.pack = std::min(kMaxPack, kBM / rpu);
             a.n_splits = 1;
             const int64_t ctas = (n_units + a.pack - 1) / a.pack;

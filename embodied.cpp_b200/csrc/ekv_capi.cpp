@@ -384,6 +384,13 @@ static int fill_attn_args(ekv_pool *p, const ekv_attn_params *prm, const void *q
         return EKV_ERR_INVALID_ARG;
     if ((prm->mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE)) && (!prm->span_begin || !prm->span_end))
         return EKV_ERR_INVALID_ARG;
+    if ((prm->mask_flags & (EKV_MASK_FLEX_SELF | EKV_MASK_FLEX_CROSS)) &&
+        (!prm->flex_meta || prm->flex_stride < 0 || (prm->n_batch > 1 && prm->flex_stride == 0) || prm->flex_q0 < 0 ||
+         prm->flex_k0 < 0 || prm->flex_window < 0))
+        return EKV_ERR_INVALID_ARG;
+    if (prm->mask_flags & ~(EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE |
+                            EKV_MASK_BLOCK_CAUSAL | EKV_MASK_FLEX_SELF | EKV_MASK_FLEX_CROSS))
+        return EKV_ERR_INVALID_ARG;
     a = ekv::AttnArgs{};
     a.pool = p->view;
     a.layer = prm->layer;
@@ -405,6 +412,11 @@ static int fill_attn_args(ekv_pool *p, const ekv_attn_params *prm, const void *q
     a.prefix_valid = prm->prefix_valid;
     a.span_begin = prm->span_begin;
     a.span_end = prm->span_end;
+    a.flex_meta = prm->flex_meta;
+    a.flex_stride = prm->flex_stride;
+    a.flex_q0 = prm->flex_q0;
+    a.flex_k0 = prm->flex_k0;
+    a.flex_window = prm->flex_window;
     a.q = (const uint16_t *)q;
     a.out = out;
     a.n_splits = 1;

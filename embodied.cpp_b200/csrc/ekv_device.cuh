@@ -9,6 +9,7 @@
 #include <cstdint>
 
 #include "../../include/ekv.h"
+#include "ekv_internal.h"
 #include "ekv_layout.cuh"
 
 namespace ekv {
@@ -34,13 +35,57 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float x) {
 //                     chunk qc = q_chunk0 + q / chunk_tokens, visible iff qc-window < kc <= qc
 //   SUFFIX_CAUSAL ... suffix key s visible iff s <= q          (models/smolvla.cpp:718-720)
 //   SUFFIX_PREFIX_LM  query 0 sees suffix key 0 only           (models/hy_vla.cpp:2355-2367)
+//   FLEX_SELF ....... flex_self_allowed over per-token metadata words (models/lingbot_va.cpp:9336-9344)
+//   FLEX_CROSS ...... flex_cross_allowed: query sequence valid and equal to the key's (:9346-9348)
 struct MaskDesc {
     int32_t flags, chunk_tokens, chunk_stride, window_chunks, q_chunk0;
+    const int32_t *flex;  // this batch element's metadata words (flex_meta + b * flex_stride), or null
+    int32_t flex_q0, flex_k0, flex_window;
 };
+
+constexpr int32_t kFlexFlags = EKV_MASK_FLEX_SELF | EKV_MASK_FLEX_CROSS;
+
+// A pair of metadata words (EKV_FLEX_META) under the FLEX flags of `flags`.
+__host__ __device__ __forceinline__ bool flex_allowed(int32_t flags, uint32_t qm, uint32_t km, int32_t window) {
+    const uint32_t qs = qm >> 24, ks = km >> 24;
+    if (qs == 0u || qs != ks) return false;  // padding query, or another sequence
+    if (flags & EKV_MASK_FLEX_SELF) {
+        const int32_t qf = (int32_t)(qm & 0x7FFFFFu), kf = (int32_t)(km & 0x7FFFFFu);
+        const bool qc = (qm >> 23) & 1u, kc = (km >> 23) & 1u;
+        const bool clean2clean = qc && kc && kf <= qf;
+        const bool noise2clean = !qc && kc && kf < qf;
+        const bool noise2noise = !qc && !kc && kf == qf;
+        const int32_t df = qf > kf ? qf - kf : kf - qf;
+        if (!((clean2clean || noise2clean || noise2noise) && df <= window)) return false;
+    }
+    return true;
+}
+
+// The mask description of batch element b of a call.
+__device__ __forceinline__ MaskDesc mask_desc(const AttnArgs &a, int b) {
+    MaskDesc m;
+    m.flags = a.mask_flags;
+    m.chunk_tokens = a.chunk_tokens;
+    m.chunk_stride = a.chunk_stride;
+    m.window_chunks = a.window_chunks;
+    m.q_chunk0 = a.q_chunk0;
+    m.flex = (a.mask_flags & kFlexFlags) ? a.flex_meta + (int64_t)b * a.flex_stride : nullptr;
+    m.flex_q0 = a.flex_q0;
+    m.flex_k0 = a.flex_k0;
+    m.flex_window = a.flex_window;
+    return m;
+}
+
+__device__ __forceinline__ bool flex_key_allowed(const MaskDesc &m, int q, int key_index) {
+    if (!(m.flags & kFlexFlags)) return true;
+    return flex_allowed(m.flags, (uint32_t)__ldg(m.flex + m.flex_q0 + q), (uint32_t)__ldg(m.flex + m.flex_k0 + key_index),
+                        m.flex_window);
+}
 
 __device__ __forceinline__ bool prefix_allowed(const MaskDesc &m, int q, int k, int prefix_valid,
                                                int span_b, int span_e) {
     if (k >= prefix_valid) return false;
+    if (!flex_key_allowed(m, q, k)) return false;
     const bool in_span = k >= span_b && k < span_e;
     if ((m.flags & EKV_MASK_SPAN_ONLY) && !in_span) return false;
     if ((m.flags & EKV_MASK_SPAN_EXCLUDE) && in_span) return false;
@@ -53,8 +98,9 @@ __device__ __forceinline__ bool prefix_allowed(const MaskDesc &m, int q, int k, 
     return true;
 }
 
-__device__ __forceinline__ bool suffix_allowed(const MaskDesc &m, int q, int s, int suffix_len) {
+__device__ __forceinline__ bool suffix_allowed(const MaskDesc &m, int q, int s, int suffix_len, int n_prefix) {
     if (s >= suffix_len) return false;
+    if (!flex_key_allowed(m, q, n_prefix + s)) return false;
     if ((m.flags & EKV_MASK_SUFFIX_CAUSAL) && s > q) return false;
     if ((m.flags & EKV_MASK_SUFFIX_PREFIX_LM) && q == 0 && s != 0) return false;
     return true;

@@ -37,6 +37,9 @@ struct AttnArgs {
     int32_t mask_flags, chunk_tokens, chunk_stride, window_chunks, q_chunk0;
     int32_t suffix_len, out_dtype, use_prefix;
     const int32_t *seq_ids, *prefix_len, *prefix_valid, *span_begin, *span_end;
+    // FLEX_SELF / FLEX_CROSS metadata (see ekv_attn_params)
+    const int32_t *flex_meta;
+    int32_t flex_stride, flex_q0, flex_k0, flex_window;
     const uint16_t *q;
     void *out;
     // key splitting (tensor-core kernel only)

@@ -28,6 +28,16 @@ MASK_SUFFIX_PREFIX_LM = 1 << 1
 MASK_SPAN_ONLY = 1 << 2
 MASK_SPAN_EXCLUDE = 1 << 3
 MASK_BLOCK_CAUSAL = 1 << 4
+MASK_FLEX_SELF = 1 << 5
+MASK_FLEX_CROSS = 1 << 6
+
+
+def flex_meta_word(seq: int, frame: int, clean: bool) -> int:
+    """EKV_FLEX_META: the metadata word of a token for the FLEX masks (negative seq = padding)."""
+    if seq < 0:
+        return 0
+    w = ((seq + 1) << 24) | ((1 if clean else 0) << 23) | (frame & 0x7FFFFF)
+    return w - (1 << 32) if w >= (1 << 31) else w
 ALGO_TC, ALGO_SIMT, ALGO_TC_PAIR, ALGO_TC_CTA, ALGO_TC_PAIR64 = 0, 1, 2, 3, 4
 
 # Device-side error codes written into the pool status word by kernels.
@@ -56,7 +66,9 @@ class AttnParams(C.Structure):
                 ("window_chunks", C.c_int32), ("q_chunk0", C.c_int32), ("suffix_len", C.c_int32),
                 ("out_dtype", C.c_int32), ("use_prefix", C.c_int32), ("reserved", C.c_int32),
                 ("seq_ids", C.c_void_p), ("prefix_len", C.c_void_p), ("prefix_valid", C.c_void_p),
-                ("span_begin", C.c_void_p), ("span_end", C.c_void_p)]
+                ("span_begin", C.c_void_p), ("span_end", C.c_void_p), ("flex_meta", C.c_void_p),
+                ("flex_stride", C.c_int32), ("flex_q0", C.c_int32), ("flex_k0", C.c_int32),
+                ("flex_window", C.c_int32)]
 
 
 class Tensor(C.Structure):
@@ -231,15 +243,18 @@ class Pool:
     def attention_params(self, *, layer, seq_ids, q_tokens, q_heads, scale, mask_flags=0,
                          chunk_tokens=0, chunk_stride=0, window_chunks=0, q_chunk0=0,
                          suffix_len=0, out_dtype=DTYPE_BF16, use_prefix=True, prefix_len=None,
-                         prefix_valid=None, span_begin=None, span_end=None) -> AttnParams:
+                         prefix_valid=None, span_begin=None, span_end=None, flex_meta=None, flex_stride=0,
+                         flex_q0=0, flex_k0=0, flex_window=0) -> AttnParams:
         p = AttnParams(layer, seq_ids.numel(), q_tokens, q_heads, scale, mask_flags, chunk_tokens,
                        chunk_stride, window_chunks, q_chunk0, suffix_len, out_dtype,
                        1 if use_prefix else 0, 0, seq_ids.data_ptr(),
                        None if prefix_len is None else prefix_len.data_ptr(),
                        None if prefix_valid is None else prefix_valid.data_ptr(),
                        None if span_begin is None else span_begin.data_ptr(),
-                       None if span_end is None else span_end.data_ptr())
-        p._keep = (seq_ids, prefix_len, prefix_valid, span_begin, span_end)
+                       None if span_end is None else span_end.data_ptr(),
+                       None if flex_meta is None else flex_meta.data_ptr(), flex_stride, flex_q0, flex_k0,
+                       flex_window)
+        p._keep = (seq_ids, prefix_len, prefix_valid, span_begin, span_end, flex_meta)
         return p
 
     def workspace_size(self, params: AttnParams) -> int:

@@ -149,6 +149,23 @@ int ekv_gather_suffix(ekv_pool *pool, int32_t layer, int32_t seq_id, int32_t n_r
 #define EKV_MASK_SPAN_ONLY (1 << 2)        /* GR00T image mask, groot_n1.cpp:717            */
 #define EKV_MASK_SPAN_EXCLUDE (1 << 3)     /* GR00T text mask, groot_n1.cpp:716             */
 #define EKV_MASK_BLOCK_CAUSAL (1 << 4)     /* chunked prefix, causal across chunks + window */
+/* LingBot-VA flex masks over per-token metadata (models/lingbot_va.cpp:9283-9348): every key k of
+ * the call (prefix keys, then suffix keys) has the metadata word flex_meta[b * flex_stride +
+ * flex_k0 + k], query token t the word flex_meta[b * flex_stride + flex_q0 + t], each word packed
+ * by EKV_FLEX_META. FLEX_SELF: flex_self_allowed -- same sequence, and clean query to clean key of
+ * an earlier or the same frame, noisy query to clean key of an earlier frame, or noisy query to
+ * noisy key of the same frame, with |query frame - key frame| <= flex_window. FLEX_CROSS:
+ * flex_cross_allowed -- the query's sequence is valid and equals the key's (text keys carry only
+ * their sequence id). Both combine (AND) with the other flags. */
+#define EKV_MASK_FLEX_SELF (1 << 5)
+#define EKV_MASK_FLEX_CROSS (1 << 6)
+/* Metadata word of a token: sequence id seq (0..254; a negative seq marks padding, which sees and
+ * is seen by nothing), frame id frame (0 .. 2^23 - 1), clean = 1 for the clean copy of a token
+ * (noise id 1 in the reference), 0 for its noisy copy. */
+#define EKV_FLEX_META(seq, frame, clean)                                                              \
+    ((int32_t)((seq) < 0 ? 0u                                                                     \
+                         : ((((uint32_t)(seq) + 1u) << 24) | ((uint32_t)((clean) ? 1 : 0) << 23) |     \
+                            ((uint32_t)(frame) & 0x7FFFFFu))))
 
 typedef struct ekv_attn_params {
     int32_t layer;
@@ -171,6 +188,13 @@ typedef struct ekv_attn_params {
     const int32_t *prefix_valid; /* keys >= prefix_valid are padding; default: prefix_len   */
     const int32_t *span_begin;   /* span for SPAN_ONLY / SPAN_EXCLUDE; default: empty       */
     const int32_t *span_end;
+    /* FLEX_SELF / FLEX_CROSS: device int32 metadata words (EKV_FLEX_META), flex_stride words per
+     * batch element; query token t reads word flex_q0 + t, key k word flex_k0 + k            */
+    const int32_t *flex_meta;
+    int32_t flex_stride;
+    int32_t flex_q0;
+    int32_t flex_k0;
+    int32_t flex_window;         /* FLEX_SELF: the largest visible |query frame - key frame|  */
 } ekv_attn_params;
 
 /* Bytes of workspace that lets ekv_attention split long key ranges across CTAs; 0 means the

@@ -125,8 +125,48 @@ void ekvo_dequantize_q8_0(const uint8_t *blocks, int64_t n, float *out) {
  * Masks
  * ------------------------------------------------------------------------------------------ */
 
+/* LingBot-VA flex masks over per-token metadata (models/lingbot_va.cpp:9273-9348): the packed
+ * words decoded back to the reference's seq_ids (-1 = padding), frame_ids and noise_ids. */
+static void flex_decode(int32_t w, int64_t *seq, int64_t *frame, int64_t *noise) {
+    const uint32_t u = (uint32_t)w;
+    *seq = (int64_t)(u >> 24) - 1;
+    *noise = (int64_t)((u >> 23) & 1u);
+    *frame = (int64_t)(u & 0x7FFFFFu);
+}
+
+/* flex_self_allowed, models/lingbot_va.cpp:9336-9344 */
+static int flex_self_allowed(int32_t qw, int32_t kw, int64_t window_size) {
+    int64_t qs, qf, qn, ks, kf, kn;
+    flex_decode(qw, &qs, &qf, &qn);
+    flex_decode(kw, &ks, &kf, &kn);
+    if (qs < 0 || qs != ks) return 0;
+    const int clean2clean = qn == 1 && kn == 1 && kf <= qf;
+    const int noise2clean = qn == 0 && kn == 1 && kf < qf;
+    const int noise2noise = qn == 0 && kn == 0 && kf == qf;
+    const int64_t df = qf > kf ? qf - kf : kf - qf;
+    return (clean2clean || noise2clean || noise2noise) && df <= window_size;
+}
+
+/* flex_cross_allowed, models/lingbot_va.cpp:9346-9348 (the key word carries its text_seq_id) */
+static int flex_cross_allowed(int32_t qw, int32_t kw) {
+    int64_t qs, qf, qn, ks, kf, kn;
+    flex_decode(qw, &qs, &qf, &qn);
+    flex_decode(kw, &ks, &kf, &kn);
+    return qs >= 0 && qs == ks;
+}
+
+static int flex_ok(const ekvo_mask *m, const ekvo_seq *s, int32_t q, int32_t k) {
+    if (!(m->flags & (EKVO_MASK_FLEX_SELF | EKVO_MASK_FLEX_CROSS))) return 1;
+    if (!s->flex_meta) return 0;
+    const int32_t qw = s->flex_meta[m->flex_q0 + q], kw = s->flex_meta[m->flex_k0 + k];
+    if ((m->flags & EKVO_MASK_FLEX_SELF) && !flex_self_allowed(qw, kw, m->flex_window)) return 0;
+    if ((m->flags & EKVO_MASK_FLEX_CROSS) && !flex_cross_allowed(qw, kw)) return 0;
+    return 1;
+}
+
 int ekvo_allowed(const ekvo_mask *m, const ekvo_seq *s, int32_t q, int32_t k) {
     if (k < 0) return 0;
+    if (k < s->n_prefix + s->n_suffix && !flex_ok(m, s, q, k)) return 0;
     if (k < s->n_prefix) {
         /* padding: models/smolvla.cpp:707-716 sets -inf on keys with prefix_valid == 0 */
         if (k >= s->prefix_valid) return 0;
@@ -209,6 +249,62 @@ static void attn_row_f32(const ekvo_attn_args *a, int32_t b, int32_t t, float *w
     }
 }
 
+/* One query row (b, t, h) into o[D], as attn_row_f32 computes it. */
+static void attn_one_row_f32(const ekvo_attn_args *a, int32_t b, int32_t t, int32_t h, float *w, float *o) {
+    const int32_t D = a->D, Hq = a->Hq, Hkv = a->Hkv, L = a->Lk_max;
+    const int32_t g = h / (Hq / Hkv);
+    const ekvo_seq *s = &a->seqs[b];
+    const int32_t nk = s->n_prefix + s->n_suffix;
+    const float *qr = a->q + (((int64_t)b * a->Tq + t) * Hq + h) * D;
+    float mx = -INFINITY;
+    for (int32_t k = 0; k < nk && k < L; ++k) {
+        w[k] = -INFINITY;
+        if (!ekvo_allowed(&a->mask, s, t, k)) continue;
+        const float *kr = a->k + (((int64_t)b * L + k) * Hkv + g) * D;
+        float dot = 0.0f;
+        for (int32_t d = 0; d < D; ++d) dot += kr[d] * qr[d];
+        float x = dot * a->scale;
+        if (a->dense_mask) x += a->dense_mask[((int64_t)b * a->Tq + t) * L + k];
+        w[k] = x;
+        if (x > mx) mx = x;
+    }
+    for (int32_t d = 0; d < D; ++d) o[d] = 0.0f;
+    if (mx == -INFINITY) return;
+    double sum = 0.0;
+    for (int32_t k = 0; k < nk && k < L; ++k) {
+        const float e = (w[k] == -INFINITY) ? 0.0f : expf(w[k] - mx);
+        w[k] = e;
+        sum += (double)e;
+    }
+    const float inv = (float)(1.0 / sum);
+    for (int32_t k = 0; k < nk && k < L; ++k) {
+        if (w[k] == 0.0f) continue;
+        const float p = w[k] * inv;
+        const float *vr = a->v + (((int64_t)b * L + k) * Hkv + g) * D;
+        for (int32_t d = 0; d < D; ++d) o[d] += p * vr[d];
+    }
+}
+
+typedef struct {
+    const ekvo_attn_args *a;
+    int32_t n_rows;
+    const int32_t *rows;
+    float *out;
+    atomic_int next;
+} rows_job;
+
+static void *rows_worker(void *arg) {
+    rows_job *j = (rows_job *)arg;
+    float *w = (float *)malloc(sizeof(float) * (size_t)(j->a->Lk_max > 0 ? j->a->Lk_max : 1));
+    for (;;) {
+        const int i = atomic_fetch_add(&j->next, 1);
+        if (i >= j->n_rows) break;
+        attn_one_row_f32(j->a, j->rows[3 * i], j->rows[3 * i + 1], j->rows[3 * i + 2], w, j->out + (int64_t)i * j->a->D);
+    }
+    free(w);
+    return NULL;
+}
+
 static void *attn_worker(void *arg) {
     attn_job *j = (attn_job *)arg;
     const ekvo_attn_args *a = j->a;
@@ -244,6 +340,29 @@ int ekvo_attention_f32(const ekvo_attn_args *a, int n_threads) {
     }
     pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)n_threads);
     for (int i = 0; i < n_threads; ++i) pthread_create(&th[i], NULL, attn_worker, &job);
+    for (int i = 0; i < n_threads; ++i) pthread_join(th[i], NULL);
+    free(th);
+    return 0;
+}
+
+int ekvo_attention_rows(const ekvo_attn_args *a, int32_t n_rows, const int32_t *rows, float *out, int n_threads) {
+    if (check_args(a) || n_rows < 0 || (n_rows && (!rows || !out))) return -1;
+    for (int32_t i = 0; i < n_rows; ++i)
+        if (rows[3 * i] < 0 || rows[3 * i] >= a->B || rows[3 * i + 1] < 0 || rows[3 * i + 1] >= a->Tq ||
+            rows[3 * i + 2] < 0 || rows[3 * i + 2] >= a->Hq)
+            return -1;
+    rows_job job;
+    job.a = a;
+    job.n_rows = n_rows;
+    job.rows = rows;
+    job.out = out;
+    atomic_init(&job.next, 0);
+    if (n_threads <= 1) {
+        rows_worker(&job);
+        return 0;
+    }
+    pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)n_threads);
+    for (int i = 0; i < n_threads; ++i) pthread_create(&th[i], NULL, rows_worker, &job);
     for (int i = 0; i < n_threads; ++i) pthread_join(th[i], NULL);
     free(th);
     return 0;

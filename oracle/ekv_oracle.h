@@ -51,7 +51,9 @@ enum {
     EKVO_MASK_SUFFIX_PREFIX_LM = 1 << 1, /* query token 0 sees only suffix key 0               */
     EKVO_MASK_SPAN_ONLY        = 1 << 2, /* prefix key visible iff inside [span_begin,span_end) */
     EKVO_MASK_SPAN_EXCLUDE     = 1 << 3, /* prefix key visible iff outside the span            */
-    EKVO_MASK_BLOCK_CAUSAL     = 1 << 4  /* chunked prefix: causal across chunks + window      */
+    EKVO_MASK_BLOCK_CAUSAL     = 1 << 4, /* chunked prefix: causal across chunks + window      */
+    EKVO_MASK_FLEX_SELF        = 1 << 5, /* LingBot flex_self_allowed over token metadata      */
+    EKVO_MASK_FLEX_CROSS       = 1 << 6  /* LingBot flex_cross_allowed (text keys)             */
 };
 
 typedef struct ekvo_seq {
@@ -60,6 +62,9 @@ typedef struct ekvo_seq {
     int32_t span_begin;   /* special span inside the prefix (GR00T image tokens)            */
     int32_t span_end;
     int32_t n_suffix;     /* keys after the prefix (this step's appended suffix)            */
+    /* FLEX masks: metadata words of this sequence, packed as EKV_FLEX_META of include/ekv.h:
+     * bits 31-24 sequence id + 1 (0 = padding), bit 23 noise id (1 = clean), bits 22-0 frame id */
+    const int32_t *flex_meta;
 } ekvo_seq;
 
 typedef struct ekvo_mask {
@@ -68,6 +73,9 @@ typedef struct ekvo_mask {
     int32_t chunk_stride;  /* BLOCK_CAUSAL: key-index stride of one chunk (>= chunk_tokens) */
     int32_t window_chunks; /* BLOCK_CAUSAL: chunks visible, the query's own one included    */
     int32_t q_chunk0;      /* BLOCK_CAUSAL: key-chunk index of query token 0's chunk         */
+    int32_t flex_q0;       /* FLEX: metadata index of query token 0                          */
+    int32_t flex_k0;       /* FLEX: metadata index of key 0 (prefix keys, then suffix keys)   */
+    int32_t flex_window;   /* FLEX_SELF: window_size, the largest visible frame distance       */
 } ekvo_mask;
 
 /* 1 if query token q (0-based within the call) may attend key k (prefix keys first). */
@@ -89,6 +97,10 @@ typedef struct ekvo_attn_args {
     ekvo_mask mask;
     float *out;
 } ekvo_attn_args;
+
+/* Rows (b, t, h) = rows[3 i .. 3 i + 2] only, into out[i][D]: the same arithmetic as
+ * ekvo_attention_f32 for a sample of a large call's query rows. */
+int ekvo_attention_rows(const ekvo_attn_args *a, int32_t n_rows, const int32_t *rows, float *out, int n_threads);
 
 /* float32 arithmetic with the softmax sum in double, as ggml's CPU soft_max does. */
 int ekvo_attention_f32(const ekvo_attn_args *a, int n_threads);

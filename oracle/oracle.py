@@ -21,16 +21,20 @@ MASK_SUFFIX_PREFIX_LM = 1 << 1
 MASK_SPAN_ONLY = 1 << 2
 MASK_SPAN_EXCLUDE = 1 << 3
 MASK_BLOCK_CAUSAL = 1 << 4
+MASK_FLEX_SELF = 1 << 5
+MASK_FLEX_CROSS = 1 << 6
 
 
 class Seq(C.Structure):
     _fields_ = [("n_prefix", C.c_int32), ("prefix_valid", C.c_int32),
-                ("span_begin", C.c_int32), ("span_end", C.c_int32), ("n_suffix", C.c_int32)]
+                ("span_begin", C.c_int32), ("span_end", C.c_int32), ("n_suffix", C.c_int32),
+                ("flex_meta", C.c_void_p)]
 
 
 class Mask(C.Structure):
     _fields_ = [("flags", C.c_int32), ("chunk_tokens", C.c_int32), ("chunk_stride", C.c_int32),
-                ("window_chunks", C.c_int32), ("q_chunk0", C.c_int32)]
+                ("window_chunks", C.c_int32), ("q_chunk0", C.c_int32), ("flex_q0", C.c_int32),
+                ("flex_k0", C.c_int32), ("flex_window", C.c_int32)]
 
 
 class AttnArgs(C.Structure):
@@ -76,6 +80,7 @@ def lib():
         L.ekvo_bf16_to_f32_n.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
         L.ekvo_quantize_q8_0.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
         L.ekvo_dequantize_q8_0.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
+        L.ekvo_attention_rows.argtypes = [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int]
         L.ekvo_allowed.restype = C.c_int
         L.ekvo_allowed.argtypes = [C.POINTER(Mask), C.POINTER(Seq), C.c_int32, C.c_int32]
         L.ekvo_attention_f32.restype = C.c_int
@@ -134,12 +139,23 @@ def dequantize_q8_0(blocks: np.ndarray) -> np.ndarray:
 
 # ---- masks and attention --------------------------------------------------------------------
 
-def make_mask(flags=0, chunk_tokens=0, chunk_stride=0, window_chunks=0, q_chunk0=0) -> Mask:
-    return Mask(flags, chunk_tokens, chunk_stride, window_chunks, q_chunk0)
+def make_mask(flags=0, chunk_tokens=0, chunk_stride=0, window_chunks=0, q_chunk0=0, flex_q0=0, flex_k0=0,
+              flex_window=0) -> Mask:
+    return Mask(flags, chunk_tokens, chunk_stride, window_chunks, q_chunk0, flex_q0, flex_k0, flex_window)
 
 
-def make_seqs(n_prefix, prefix_valid=None, span=None, n_suffix=0):
-    """n_prefix etc. are per-request sequences (or scalars broadcast over B)."""
+def flex_meta_word(seq: int, frame: int, noise: int) -> int:
+    """Pack a token's (seq_id, frame_id, noise_id) of the reference's LingBotFlexMaskMeta
+    (models/lingbot_va.cpp:9273-9280; seq -1 = padding, noise 1 = clean) as an int32 metadata word."""
+    if seq < 0:
+        return 0
+    w = ((seq + 1) << 24) | ((noise & 1) << 23) | (frame & 0x7FFFFF)
+    return w - (1 << 32) if w >= (1 << 31) else w
+
+
+def make_seqs(n_prefix, prefix_valid=None, span=None, n_suffix=0, flex_meta=None):
+    """n_prefix etc. are per-request sequences (or scalars broadcast over B); flex_meta is a list of
+    per-request int32 metadata arrays (kept alive by the returned array)."""
     n_prefix = np.atleast_1d(np.asarray(n_prefix, dtype=np.int32))
     B = n_prefix.size
     pv = n_prefix if prefix_valid is None else np.broadcast_to(np.asarray(prefix_valid, np.int32), (B,))
@@ -151,8 +167,15 @@ def make_seqs(n_prefix, prefix_valid=None, span=None, n_suffix=0):
         se = np.broadcast_to(np.asarray(span[1], np.int32), (B,))
     ns = np.broadcast_to(np.asarray(n_suffix, np.int32), (B,))
     arr = (Seq * B)()
+    keep = []
     for i in range(B):
-        arr[i] = Seq(int(n_prefix[i]), int(pv[i]), int(sb[i]), int(se[i]), int(ns[i]))
+        fm = None
+        if flex_meta is not None:
+            m = np.ascontiguousarray(flex_meta[i], np.int32)
+            keep.append(m)
+            fm = m.ctypes.data
+        arr[i] = Seq(int(n_prefix[i]), int(pv[i]), int(sb[i]), int(se[i]), int(ns[i]), fm)
+    arr._keep = keep
     return arr
 
 
@@ -184,6 +207,23 @@ def attention(q, k, v, seqs, mask: Mask, scale: float, dense_mask=None, precisio
         assert rc == 0
         return out64
     rc = lib().ekvo_attention_f32(C.byref(args), n_threads or os.cpu_count() or 1)
+    assert rc == 0
+    return out
+
+
+def attention_rows(q, k, v, seqs, mask: Mask, scale: float, rows, n_threads=0):
+    """The f32 oracle for a sample of query rows: rows is an int array [n][3] of (b, t, h); returns
+    [n][D]. q [B,Tq,Hq,D], k/v [B,Lk,Hkv,D] f32 (prefix keys then suffix keys)."""
+    q = np.ascontiguousarray(q, np.float32)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    rows = np.ascontiguousarray(rows, np.int32)
+    B, Tq, Hq, D = q.shape
+    Lk, Hkv = k.shape[1], k.shape[2]
+    out = np.zeros((rows.shape[0], D), np.float32)
+    args = AttnArgs(B, Tq, Hq, Hkv, D, Lk, scale, _ptr(q).value, _ptr(k).value, _ptr(v).value, None,
+                    C.addressof(seqs), mask, _ptr(out).value)
+    rc = lib().ekvo_attention_rows(C.byref(args), rows.shape[0], _ptr(rows), _ptr(out), n_threads or os.cpu_count() or 1)
     assert rc == 0
     return out
 

@@ -12,6 +12,9 @@ Sources of truth, none of them this repository's own code:
   * Dense mask matrices built by the loops of the reference mask builders
     (models/smolvla.cpp:705-725, models/hy_vla.cpp:2355-2367, models/groot_n1.cpp:708-718)
     restated over numpy arrays, for small shapes.
+  * LingBot-VA flex masks: the token metadata of build_flex_mask_meta and the dense masks of
+    flex_self_allowed / flex_cross_allowed (models/lingbot_va.cpp:9283-9348) restated over Python
+    lists for three small layouts.
 
 Usage:  python tests/golden/make_golden.py      (writes *.npz next to this file)
 """
@@ -156,12 +159,74 @@ def mask_builders():
     return out
 
 
+def lingbot_flex():
+    """LingBot-VA flex masks over the token metadata of build_flex_mask_meta
+    (models/lingbot_va.cpp:9283-9334), restated over Python lists: latent tokens (one per
+    (frame / pt, h / ph, w / pw) patch, frame id (f * pt) / chunk_size * 2) then action tokens
+    (frame id f / chunk_size * 2 + 1), each group first with noise id 0 and then repeated with noise id
+    1, then `padded_length` padding tokens (ids -1); text_seq_ids: `text_seq` ids per batch element.
+    Dense masks from flex_self_allowed (:9336-9344) and flex_cross_allowed (:9346-9348), for three
+    small layouts (one is the runtime layout of build_runtime_flex_meta, :9435-9440, with a
+    2-patch latent and a 2-frame action, chunk 1, window 4)."""
+    def meta(latent, action, padded_length, chunk_size, window_size, pt, ph, pw, text_seq):
+        lb, _, lf, lh, lw = latent
+        _, _, af, ah, aw = action
+        lat_seq, lat_frame, act_seq, act_frame = [], [], [], []
+        for b in range(lb):
+            for f in range(lf // pt):
+                for h in range(lh // ph):
+                    for w in range(lw // pw):
+                        lat_seq.append(b)
+                        lat_frame.append((f * pt) // chunk_size * 2)
+            for f in range(af):
+                for h in range(ah):
+                    for w in range(aw):
+                        act_seq.append(b)
+                        act_frame.append(f // chunk_size * 2 + 1)
+        seq = lat_seq + lat_seq + act_seq + act_seq + [-1] * padded_length
+        frame = lat_frame + lat_frame + act_frame + act_frame + [-1] * padded_length
+        noise = [0] * len(lat_seq) + [1] * len(lat_seq) + [0] * len(act_seq) + [1] * len(act_seq) + [-1] * padded_length
+        text = [b for b in range(lb) for _ in range(text_seq)]
+        n = len(seq)
+        self_m = np.zeros((n, n), bool)
+        for q in range(n):
+            for k in range(n):
+                if seq[q] < 0 or seq[q] != seq[k]:
+                    continue
+                qf, kf, qn, kn = frame[q], frame[k], noise[q], noise[k]
+                c2c = qn == 1 and kn == 1 and kf <= qf
+                n2c = qn == 0 and kn == 1 and kf < qf
+                n2n = qn == 0 and kn == 0 and kf == qf
+                self_m[q, k] = (c2c or n2c or n2n) and abs(qf - kf) <= window_size
+        cross_m = np.zeros((n, len(text)), bool)
+        for q in range(n):
+            for k in range(len(text)):
+                cross_m[q, k] = seq[q] >= 0 and seq[q] == text[k]
+        return (np.array(seq, np.int64), np.array(frame, np.int64), np.array(noise, np.int64),
+                np.array(text, np.int64), self_m, cross_m)
+
+    layouts = {
+        # (latent b, c, f, h, w), (action b, c, f, h, w), padded, chunk, window, pt, ph, pw, text
+        "runtime": ((1, 4, 2, 4, 4), (1, 7, 2, 2, 1), 3, 1, 4, 1, 2, 2, 6),
+        "chunks": ((1, 4, 8, 2, 2), (1, 7, 8, 1, 1), 5, 2, 2, 1, 1, 1, 4),
+        "batch2": ((2, 4, 4, 2, 2), (2, 7, 4, 1, 1), 2, 1, 1, 1, 2, 1, 3),
+    }
+    out = {}
+    for name, args in layouts.items():
+        seq, frame, noise, text, self_m, cross_m = meta(*args)
+        out[f"{name}_seq"], out[f"{name}_frame"], out[f"{name}_noise"], out[f"{name}_text"] = seq, frame, noise, text
+        out[f"{name}_self"], out[f"{name}_cross"] = self_m, cross_m
+        out[f"{name}_window"] = np.array(args[4], np.int64)
+    return out
+
+
 def main():
     np.savez_compressed(os.path.join(HERE, "q8_0_gguf.npz"), **q8_0_vectors())
     np.savez_compressed(os.path.join(HERE, "bf16_gguf.npz"), **bf16_vectors())
     np.savez_compressed(os.path.join(HERE, "f16_numpy.npz"), **f16_vectors())
     np.savez_compressed(os.path.join(HERE, "lingbot_smoke.npz"), **lingbot_smoke())
     np.savez_compressed(os.path.join(HERE, "mask_builders.npz"), **mask_builders())
+    np.savez_compressed(os.path.join(HERE, "lingbot_flex.npz"), **lingbot_flex())
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

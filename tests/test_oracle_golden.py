@@ -129,3 +129,34 @@ def test_ggml_q8_0_path_within_tolerance_of_exact_dequant():
     ggml = oracle.attention_ggml_q8_0(q, k, v, Lp, 1 / 16.0)
     d = np.abs(exact - ggml).max()
     assert d < 1e-2, d
+
+
+def _flex_words(g, layout):
+    seq, frame, noise = g[f"{layout}_seq"], g[f"{layout}_frame"], g[f"{layout}_noise"]
+    return [oracle.flex_meta_word(int(s), int(f), int(z)) if s >= 0 else 0 for s, f, z in zip(seq, frame, noise)]
+
+
+@pytest.mark.parametrize("layout", ["runtime", "chunks", "batch2"])
+def test_mask_lingbot_flex(layout):
+    """FLEX_SELF / FLEX_CROSS over packed metadata words against the dense masks of the reference's
+    flex_self_allowed / flex_cross_allowed over build_flex_mask_meta (models/lingbot_va.cpp:9283-9348)."""
+    g = load("lingbot_flex.npz")
+    words = _flex_words(g, layout)
+    n = len(words)
+    seq = oracle.make_seqs([n], n_suffix=0, flex_meta=[np.array(words, np.int32)])
+    m = oracle.make_mask(oracle.MASK_FLEX_SELF, flex_window=int(g[f"{layout}_window"]))
+    np.testing.assert_array_equal(oracle.allowed_matrix(m, seq[0], n, n), g[f"{layout}_self"])
+    # the keys split into a cached prefix and a suffix see the same metadata by key index
+    seq2 = oracle.make_seqs([n - 5], n_suffix=5, flex_meta=[np.array(words, np.int32)])
+    np.testing.assert_array_equal(oracle.allowed_matrix(m, seq2[0], n, n), g[f"{layout}_self"])
+    # cross: metadata = the query tokens' words, then the text keys' (sequence id only)
+    text = [oracle.flex_meta_word(int(t), 0, 0) for t in g[f"{layout}_text"]]
+    seqc = oracle.make_seqs([len(text)], n_suffix=0, flex_meta=[np.array(words + text, np.int32)])
+    mc = oracle.make_mask(oracle.MASK_FLEX_CROSS, flex_k0=n)
+    np.testing.assert_array_equal(oracle.allowed_matrix(mc, seqc[0], n, len(text)), g[f"{layout}_cross"])
+
+
+def test_flex_meta_word_packing_matches_library_binding():
+    import ekv
+    for seq, frame, clean in [(-1, 5, 1), (0, 0, 0), (0, 7, 1), (3, 123456, 0), (254, (1 << 23) - 1, 1)]:
+        assert ekv.flex_meta_word(seq, frame, clean) == oracle.flex_meta_word(seq, frame, clean)
