@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -25,6 +26,13 @@ bool valid_seq(const ekv_pool *p, int32_t id) {
 
 int32_t blocks_for(const ekv_pool *p, int32_t n_tokens) {
     return (n_tokens + p->cfg.block_tokens - 1) / p->cfg.block_tokens;
+}
+
+// The predicted range within the sequence's length (empty ranges normalised to [0, 0)).
+void clamp_pred(ekv_pool::Seq &q) {
+    q.pred_hi = std::min(q.pred_hi, q.n_tokens);
+    q.pred_lo = std::min(q.pred_lo, q.pred_hi);
+    if (q.pred_hi <= q.pred_lo) q.pred_lo = q.pred_hi = 0;
 }
 
 void mark_dirty(ekv_pool *p, int32_t id) {
@@ -238,6 +246,7 @@ int ekv_seq_create(ekv_pool *p, int32_t *seq_id) {
     q.live = true;
     q.n_tokens = 0;
     q.blocks.clear();
+    q.pred_lo = q.pred_hi = 0;
     mark_dirty(p, id);
     *seq_id = id;
     return EKV_OK;
@@ -249,6 +258,7 @@ int ekv_seq_free(ekv_pool *p, int32_t id) {
     for (int32_t b : q.blocks) p->free_blocks.insert(b);
     q.blocks.clear();
     q.n_tokens = 0;
+    q.pred_lo = q.pred_hi = 0;
     q.live = false;
     p->free_seq_ids.insert(id);
     mark_dirty(p, id);
@@ -273,6 +283,7 @@ int ekv_seq_resize(ekv_pool *p, int32_t id, int32_t n_tokens) {
         q.blocks.resize((size_t)need);
     }
     q.n_tokens = n_tokens;
+    clamp_pred(q);
     mark_dirty(p, id);
     return EKV_OK;
 }
@@ -295,6 +306,7 @@ int ekv_seq_set_blocks(ekv_pool *p, int32_t id, const int32_t *blocks, int32_t n
     q.blocks.assign(blocks, blocks + n_blocks);
     for (int32_t b : q.blocks) p->free_blocks.erase(b);
     q.n_tokens = n_tokens;
+    q.pred_lo = q.pred_hi = 0;
     mark_dirty(p, id);
     return EKV_OK;
 }
@@ -305,8 +317,61 @@ int ekv_seq_evict_front(ekv_pool *p, int32_t id, int32_t n_blocks) {
     if (n_blocks < 0 || n_blocks > (int32_t)q.blocks.size()) return EKV_ERR_RANGE;
     for (int32_t i = 0; i < n_blocks; ++i) p->free_blocks.insert(q.blocks[(size_t)i]);
     q.blocks.erase(q.blocks.begin(), q.blocks.begin() + n_blocks);
-    q.n_tokens = std::max(0, q.n_tokens - n_blocks * p->cfg.block_tokens);
+    const int32_t shift = n_blocks * p->cfg.block_tokens;
+    q.n_tokens = std::max(0, q.n_tokens - shift);
+    q.pred_lo = std::max(0, q.pred_lo - shift);
+    q.pred_hi = std::max(0, q.pred_hi - shift);
+    clamp_pred(q);
     mark_dirty(p, id);
+    return EKV_OK;
+}
+
+int ekv_seq_append_tokens(ekv_pool *p, int32_t id, int32_t n_tokens, int32_t pred) {
+    if (!valid_seq(p, id)) return EKV_ERR_NO_SEQ;
+    if (n_tokens < 0) return EKV_ERR_INVALID_ARG;
+    ekv_pool::Seq &q = p->seqs[(size_t)id];
+    const int32_t old = q.n_tokens;
+    const bool has_pred = q.pred_hi > q.pred_lo;
+    if (pred && has_pred && q.pred_hi != old) return EKV_ERR_UNSUPPORTED;  // a second predicted range
+    if ((int64_t)old + n_tokens > INT32_MAX) return EKV_ERR_RANGE;
+    if (const int rc = ekv_seq_resize(p, id, old + n_tokens)) return rc;
+    if (pred && n_tokens > 0) {
+        if (!has_pred) q.pred_lo = old;
+        q.pred_hi = old + n_tokens;
+    }
+    return EKV_OK;
+}
+
+int ekv_seq_clear_pred(ekv_pool *p, int32_t id) {
+    if (!valid_seq(p, id)) return EKV_ERR_NO_SEQ;
+    ekv_pool::Seq &q = p->seqs[(size_t)id];
+    if (q.pred_hi <= q.pred_lo) return EKV_OK;
+    const int32_t bt = p->cfg.block_tokens, lo = q.pred_lo, hi = q.pred_hi;
+    if (hi == q.n_tokens) {
+        q.pred_lo = q.pred_hi = 0;
+        return ekv_seq_resize(p, id, lo);  // truncation cannot fail
+    }
+    if (lo % bt || hi % bt) return EKV_ERR_UNSUPPORTED;
+    for (int32_t i = lo / bt; i < hi / bt; ++i) p->free_blocks.insert(q.blocks[(size_t)i]);
+    q.blocks.erase(q.blocks.begin() + lo / bt, q.blocks.begin() + hi / bt);
+    q.n_tokens -= hi - lo;
+    q.pred_lo = q.pred_hi = 0;
+    mark_dirty(p, id);
+    return EKV_OK;
+}
+
+int ekv_seq_restore(ekv_pool *p, int32_t id, int32_t n_tokens) {
+    if (!valid_seq(p, id)) return EKV_ERR_NO_SEQ;
+    ekv_pool::Seq &q = p->seqs[(size_t)id];
+    if (n_tokens < 0 || n_tokens > q.n_tokens) return EKV_ERR_RANGE;
+    return ekv_seq_resize(p, id, q.n_tokens - n_tokens);
+}
+
+int ekv_seq_get_pred(const ekv_pool *p, int32_t id, int32_t *lo, int32_t *hi) {
+    if (!valid_seq(p, id)) return EKV_ERR_NO_SEQ;
+    const ekv_pool::Seq &q = p->seqs[(size_t)id];
+    if (lo) *lo = q.pred_lo;
+    if (hi) *hi = q.pred_hi;
     return EKV_OK;
 }
 

@@ -20,6 +20,7 @@ struct ekv_pool {
         bool live = false;
         int32_t n_tokens = 0;
         std::vector<int32_t> blocks;
+        int32_t pred_lo = 0, pred_hi = 0;  // predicted tokens [pred_lo, pred_hi), empty when equal
     };
     std::vector<Seq> seqs;
     std::set<int32_t> free_seq_ids;

@@ -80,6 +80,7 @@ class Tensor(C.Structure):
 EXPORTED = [
     "ekv_pool_create", "ekv_pool_destroy", "ekv_pool_get_info", "ekv_pool_status", "ekv_pool_sync",
     "ekv_seq_create", "ekv_seq_free", "ekv_seq_resize", "ekv_seq_set_blocks", "ekv_seq_evict_front",
+    "ekv_seq_append_tokens", "ekv_seq_clear_pred", "ekv_seq_restore", "ekv_seq_get_pred",
     "ekv_seq_get", "ekv_append", "ekv_append_suffix", "ekv_gather", "ekv_gather_suffix",
     "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
     "ekv_strerror", "ekv_attention_noalloc", "ekv_flash_attn_ext",
@@ -105,6 +106,10 @@ def _load():
         "ekv_seq_resize": ([vp, i32, i32], C.c_int),
         "ekv_seq_set_blocks": ([vp, i32, pi32, i32, i32], C.c_int),
         "ekv_seq_evict_front": ([vp, i32, i32], C.c_int),
+        "ekv_seq_append_tokens": ([vp, i32, i32, i32], C.c_int),
+        "ekv_seq_clear_pred": ([vp, i32], C.c_int),
+        "ekv_seq_restore": ([vp, i32, i32], C.c_int),
+        "ekv_seq_get_pred": ([vp, i32, pi32, pi32], C.c_int),
         "ekv_seq_get": ([vp, i32, pi32, pi32, pi32, i32], C.c_int),
         "ekv_append": ([vp, i32, i32, vp, vp, vp, vp, i32, vp, vp, vp], C.c_int),
         "ekv_append_suffix": ([vp, i32, i32, vp, i32, vp, vp, vp], C.c_int),
@@ -213,6 +218,20 @@ class Pool:
 
     def seq_evict_front(self, seq, n_blocks):
         check(lib.ekv_seq_evict_front(self.h, seq, n_blocks), "ekv_seq_evict_front")
+
+    def seq_append_tokens(self, seq, n_tokens, pred=False):
+        check(lib.ekv_seq_append_tokens(self.h, seq, n_tokens, 1 if pred else 0), "ekv_seq_append_tokens")
+
+    def seq_clear_pred(self, seq):
+        check(lib.ekv_seq_clear_pred(self.h, seq), "ekv_seq_clear_pred")
+
+    def seq_restore(self, seq, n_tokens):
+        check(lib.ekv_seq_restore(self.h, seq, n_tokens), "ekv_seq_restore")
+
+    def seq_get_pred(self, seq):
+        lo, hi = C.c_int32(), C.c_int32()
+        check(lib.ekv_seq_get_pred(self.h, seq, C.byref(lo), C.byref(hi)), "ekv_seq_get_pred")
+        return lo.value, hi.value
 
     def seq_get(self, seq) -> SeqView:
         nt, nb = C.c_int32(), C.c_int32()

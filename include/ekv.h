@@ -108,6 +108,24 @@ int ekv_seq_set_blocks(ekv_pool *pool, int32_t seq_id, const int32_t *blocks, in
  * the role of LingBotKVCache::allocate_slots_into's oldest-id eviction,
  * models/lingbot_va.cpp:8806-8825). Later tokens move down by n_blocks*block_tokens. */
 int ekv_seq_evict_front(ekv_pool *pool, int32_t seq_id, int32_t n_blocks);
+/* ---- predicted tokens (LingBot-VA's rollout appends predicted K/V, attends, then rolls them back
+ * before the clean K/V of the same chunk are appended: LingBotKVCache::update_with_workspace's
+ * is_pred, restore and clear_pred, models/lingbot_va.cpp:8853-8886, 8946-8966). A sequence holds at
+ * most one range of predicted tokens. ---- */
+/* Grow the sequence by n_tokens at its tail (blocks as ekv_seq_resize allocates them); pred != 0 marks
+ * them predicted. A predicted append extends the predicted range only when that range ends at the
+ * tail (EKV_ERR_UNSUPPORTED otherwise); a clean append after predicted tokens leaves them inside. */
+int ekv_seq_append_tokens(ekv_pool *pool, int32_t seq_id, int32_t n_tokens, int32_t pred);
+/* Drop the predicted tokens (clear_pred). A predicted range at the tail is truncated (its blocks freed
+ * as they empty), so the next append writes the clean tokens in place; a range inside the sequence
+ * must start and end on block boundaries (its blocks leave the table and later tokens move down;
+ * EKV_ERR_UNSUPPORTED otherwise). */
+int ekv_seq_clear_pred(ekv_pool *pool, int32_t seq_id);
+/* Roll back the last n_tokens appended (restore of the last update's slots): truncation. */
+int ekv_seq_restore(ekv_pool *pool, int32_t seq_id, int32_t n_tokens);
+/* The predicted range [*lo, *hi) in token positions (*lo == *hi == 0 when there is none). */
+int ekv_seq_get_pred(const ekv_pool *pool, int32_t seq_id, int32_t *lo, int32_t *hi);
+
 /* Host view of a sequence: length, block count, and up to `cap` block ids. */
 int ekv_seq_get(const ekv_pool *pool, int32_t seq_id, int32_t *n_tokens, int32_t *n_blocks,
                 int32_t *blocks, int32_t cap);

@@ -8,7 +8,12 @@ Restates, at block granularity, the slot policy of LingBotKVCache
     each sequence's block table is ordered oldest-first, so oldest-chunk eviction drops blocks
     from the front of the table;
   * a request that cannot be satisfied changes nothing and reports failure (:8791-8792,
-    :8827-8828).
+    :8827-8828);
+  * predicted tokens (is_pred, :8853-8886) are rolled back by clear_pred (:8954-8966) and the last
+    update by restore (:8946-8952). The slot store frees those slots and its next update takes the
+    lowest free slots again, so the clean tokens land where the predicted ones were; the paged pool
+    keeps one predicted range per sequence and truncates it (or, inside the sequence, drops its
+    whole blocks), which gives the same key order.
 Sequence slots follow the same lowest-free-first rule. Lengths are in tokens.
 """
 from __future__ import annotations
@@ -31,7 +36,7 @@ class PoolModel:
             return None
         s = min(self.free_seqs)
         self.free_seqs.remove(s)
-        self.seqs[s] = {"n": 0, "blocks": []}
+        self.seqs[s] = {"n": 0, "blocks": [], "pred": (0, 0)}
         return s
 
     def seq_free(self, s):
@@ -61,7 +66,58 @@ class PoolModel:
             self.free.update(q["blocks"][need:])
             del q["blocks"][need:]
         q["n"] = n_tokens
+        self._clamp(q)
         return "ok"
+
+    @staticmethod
+    def _clamp(q):
+        lo, hi = q["pred"]
+        hi = min(hi, q["n"])
+        lo = min(lo, hi)
+        q["pred"] = (lo, hi) if hi > lo else (0, 0)
+
+    def seq_append_tokens(self, s, n, pred):
+        if s not in self.seqs:
+            return "no_seq"
+        if n < 0:
+            return "invalid"
+        q = self.seqs[s]
+        old = q["n"]
+        lo, hi = q["pred"]
+        if pred and hi > lo and hi != old:
+            return "unsupported"
+        r = self.seq_resize(s, old + n)
+        if r != "ok":
+            return r
+        if pred and n > 0:
+            q["pred"] = (old if hi <= lo else lo, old + n)
+        return "ok"
+
+    def seq_clear_pred(self, s):
+        if s not in self.seqs:
+            return "no_seq"
+        q = self.seqs[s]
+        lo, hi = q["pred"]
+        if hi <= lo:
+            return "ok"
+        if hi == q["n"]:
+            q["pred"] = (0, 0)
+            return self.seq_resize(s, lo)
+        if lo % self.bt or hi % self.bt:
+            return "unsupported"
+        self.free.update(q["blocks"][lo // self.bt:hi // self.bt])
+        del q["blocks"][lo // self.bt:hi // self.bt]
+        q["n"] -= hi - lo
+        q["pred"] = (0, 0)
+        return "ok"
+
+    def seq_restore(self, s, n):
+        if s not in self.seqs:
+            return "no_seq"
+        q = self.seqs[s]
+        if n < 0 or n > q["n"]:
+            return "range"
+        return self.seq_resize(s, q["n"] - n)
 
     def seq_evict_front(self, s, n):
         if s not in self.seqs:
@@ -72,6 +128,9 @@ class PoolModel:
         self.free.update(q["blocks"][:n])
         del q["blocks"][:n]
         q["n"] = max(0, q["n"] - n * self.bt)
+        lo, hi = q["pred"]
+        q["pred"] = (max(0, lo - n * self.bt), max(0, hi - n * self.bt))
+        self._clamp(q)
         return "ok"
 
     def seq_set_blocks(self, s, blocks, n_tokens):
@@ -89,4 +148,5 @@ class PoolModel:
         q["blocks"] = list(blocks)
         self.free.difference_update(blocks)
         q["n"] = n_tokens
+        q["pred"] = (0, 0)
         return "ok"

@@ -53,9 +53,11 @@ def test_host_pool_allocation_matches_model():
     pool = host_pool()
     model = PoolModel(40, 16, 6, 12)
     code = {"ok": ekv.OK, "no_seq": ekv.ERR_NO_SEQ, "range": ekv.ERR_RANGE,
-            "exhausted": ekv.ERR_POOL_EXHAUSTED, "invalid": ekv.ERR_INVALID_ARG}
-    for step in range(3000):
-        op = rng.choice(["create", "free", "resize", "resize", "evict", "set"])
+            "exhausted": ekv.ERR_POOL_EXHAUSTED, "invalid": ekv.ERR_INVALID_ARG,
+            "unsupported": ekv.ERR_UNSUPPORTED}
+    for step in range(4000):
+        op = rng.choice(["create", "free", "resize", "resize", "evict", "set", "append", "append", "clear_pred",
+                         "restore"])
         live = sorted(model.seqs)
         if op == "create":
             want = model.seq_create()
@@ -89,9 +91,28 @@ def test_host_pool_allocation_matches_model():
             arr = (C.c_int32 * max(1, len(blocks)))(*blocks)
             rc = ekv.lib.ekv_seq_set_blocks(pool.h, s, arr, len(blocks), n)
             assert rc == code[want], (step, op, want, rc)
+        elif op == "append" and live:
+            s = rng.choice(live)
+            n = rng.choice([rng.randint(0, 40), 16 * rng.randint(0, 3)])
+            pred = rng.random() < 0.5
+            want = model.seq_append_tokens(s, n, pred)
+            rc = ekv.lib.ekv_seq_append_tokens(pool.h, s, n, 1 if pred else 0)
+            assert rc == code[want], (step, op, want, rc)
+        elif op == "clear_pred" and live:
+            s = rng.choice(live)
+            want = model.seq_clear_pred(s)
+            rc = ekv.lib.ekv_seq_clear_pred(pool.h, s)
+            assert rc == code[want], (step, op, want, rc)
+        elif op == "restore" and live:
+            s = rng.choice(live)
+            n = rng.randint(0, 40)
+            want = model.seq_restore(s, n)
+            rc = ekv.lib.ekv_seq_restore(pool.h, s, n)
+            assert rc == code[want], (step, op, want, rc)
         for s, q in model.seqs.items():
             v = pool.seq_get(s)
             assert v.n_tokens == q["n"] and v.blocks == q["blocks"], (step, s)
+            assert pool.seq_get_pred(s) == q["pred"], (step, s)
         assert pool.info().free_blocks == len(model.free)
     pool.close()
 
@@ -136,3 +157,34 @@ def test_append_suffix_attention_validates_before_enqueueing():
     assert f(pool.h, C.byref(prm), buf, buf, buf, buf, None, 0, None) == ekv.ERR_INVALID_ARG
     prm.layer, prm.q_heads = 0, 0
     assert f(pool.h, C.byref(prm), buf, buf, buf, buf, None, 0, None) == ekv.ERR_INVALID_ARG
+
+
+def test_predicted_tokens_roll_back():
+    """LingBotKVCache's predict -> clear_pred -> clean append (models/lingbot_va.cpp:8853-8886,
+    8954-8966): the clean tokens take the predicted ones' positions and blocks."""
+    pool = host_pool()
+    s = pool.seq_create()
+    pool.seq_append_tokens(s, 40)
+    pool.seq_append_tokens(s, 30, pred=True)
+    assert pool.seq_get_pred(s) == (40, 70)
+    blocks = pool.seq_get(s).blocks
+    pool.seq_clear_pred(s)
+    assert pool.seq_get(s).n_tokens == 40 and pool.seq_get_pred(s) == (0, 0)
+    pool.seq_append_tokens(s, 30)
+    assert pool.seq_get(s).blocks == blocks  # same blocks, same positions
+    # a predicted range inside the sequence leaves as whole blocks; unaligned ones are refused
+    pool.seq_resize(s, 48)
+    pool.seq_append_tokens(s, 32, pred=True)
+    pool.seq_append_tokens(s, 5)
+    before = pool.seq_get(s).blocks
+    pool.seq_clear_pred(s)
+    v = pool.seq_get(s)
+    assert v.n_tokens == 53 and v.blocks == before[:3] + before[5:]
+    pool.seq_append_tokens(s, 3, pred=True)
+    pool.seq_append_tokens(s, 2)
+    with pytest.raises(ekv.EkvError) as e:
+        pool.seq_clear_pred(s)
+    assert e.value.code == ekv.ERR_UNSUPPORTED
+    pool.seq_restore(s, 5)  # the rollback of the last two updates takes the predicted tokens too
+    assert pool.seq_get(s).n_tokens == 53 and pool.seq_get_pred(s) == (0, 0)
+    pool.close()
