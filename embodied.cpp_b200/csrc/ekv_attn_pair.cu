@@ -90,7 +90,8 @@ struct PairCfg {
 enum {
     PB_K_FULL = 0,       // [6] bf16: this CTA's K half landed (forwarded by its relay warp)
     PB_KINIT = 6,        // [2] rank 0: both CTAs' K halves of tiles 0 and 1
-                         // 8-11 unused
+    PB_STALL = 8,        // rank 0: never arrived on (ekv_debug_expire_wait)
+                         // 9-11 unused
     PB_K_EMPTY = 12,     // [6] S(j) done (committed to both CTAs): K stage free, S(j) readable
     PB_V_FULL = 18,      // [6] bf16: this CTA's V half landed (forwarded by its relay warp)
                          // 24-29 unused
@@ -469,10 +470,10 @@ __device__ __forceinline__ void pair_fail(const AttnArgs &a, volatile int *abort
     report_error(a.pool.status, DEV_ERR_TIMEOUT, where, blockIdx.x, blockIdx.z);
 }
 
-__device__ __forceinline__ bool pair_xsync(uint32_t xbar, int use, volatile int *abort) {
+__device__ __forceinline__ bool pair_xsync(uint32_t xbar, int use, volatile int *abort, long long budget) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(xbar);
-    return mbar_wait(xbar, (uint32_t)use & 1u, abort, kWaitBudget);
+    return mbar_wait(xbar, (uint32_t)use & 1u, abort, budget);
 }
 
 // ---- softmax / epilogue of one CTA (warps 0-7): warp w owns query row (w & 3) * 32 + lane and
@@ -505,7 +506,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
     for (int jj = 0; jj < n; ++jj) {
         const int sb = jj & 1;
         const int j = pl.j0 + jj;
-        if (!(ok = mbar_wait(bar(PB_K_EMPTY + jj % NS), stage_parity(jj, NS), abort, kWaitBudget))) break;
+        if (!(ok = mbar_wait(bar(PB_K_EMPTY + jj % NS), stage_parity(jj, NS), abort, a.wait_budget))) break;
         tc_fence_after();
         if (r == 0 && h == 0 && jj < 50) TRACE(300 + jj);
         const bool suffix = j >= pl.np_tiles;
@@ -529,7 +530,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
         }
         const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
         xmax[((jj & 1) * 2 + h) * kBM + r] = cm;
-        if (!(ok = pair_xsync(xbar, uses++, abort))) break;
+        if (!(ok = pair_xsync(xbar, uses++, abort, a.wait_budget))) break;
         const float rmax = fmaxf(cm, xmax[((jj & 1) * 2 + (h ^ 1)) * kBM + r]);
         if (__any_sync(0xffffffffu, rmax > (m_used + 8.0f) * inv_scale_log2)) {
             const float m_tile = rmax * a.scale_log2;
@@ -547,7 +548,7 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
             }
             if (__any_sync(0xffffffffu, rescale)) {
                 if (!(ok = mbar_wait(bar(PB_V_EMPTY + (jj - 1) % NS), stage_parity(jj - 1, NS), abort,
-                                             kWaitBudget)))
+                                             a.wait_budget)))
                     break;
                 tc_fence_after();
 #pragma unroll 1
@@ -594,14 +595,14 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
     }
     if (!ok) pair_fail(a, abort, 3);
     if (ok && n > 0) {
-        ok = mbar_wait(bar(PB_V_EMPTY + (n - 1) % NS), stage_parity(n - 1, NS), abort, kWaitBudget);
+        ok = mbar_wait(bar(PB_V_EMPTY + (n - 1) % NS), stage_parity(n - 1, NS), abort, a.wait_budget);
         if (!ok) pair_fail(a, abort, 4);
         tc_fence_after();
     }
     // ---- epilogue: row sum over both halves, then this warp's D/2 columns of O ----
     if (r == 0 && h == 0) TRACE(10);
     xl[h * kBM + r] = l;
-    if (ok && !pair_xsync(xbar, uses++, abort)) {
+    if (ok && !pair_xsync(xbar, uses++, abort, a.wait_budget)) {
         ok = false;
         pair_fail(a, abort, 7);
     }
@@ -726,6 +727,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             mbar_init(bar(PB_RAW_EMPTY + s), kDq / 32);
         }
         mbar_init(bar(PB_DONE), 1);
+        mbar_init(bar(PB_STALL), 1);
         for (int q = 0; q < 4; ++q) mbar_init(bar(PB_XCH + q), 2);
         *abort = 0;
         mbar_init_fence();
@@ -822,7 +824,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 };
                 auto issue_pv = [&](int jj) {
                     const int st = jj % NS, sb = jj & 1;
-                    if (!mbar_wait(bar(PB_PVK + st), stage_parity(jj, NS), abort, kWaitBudget)) return false;
+                    if (!mbar_wait(bar(PB_PVK + st), stage_parity(jj, NS), abort, a.wait_budget)) return false;
                     tc_fence_after();
                     if (jj < 50) TRACE(900 + jj);
                     const uint64_t bd0 = sdesc(v_addr + st * C::VH_BYTES, C::V_LBO, C::V_SBO, C::LAYOUT);
@@ -842,8 +844,10 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 };
                 // S(0), S(1), then P.V(j) and S(j + 2) for each j: one wait per tile
                 bool ok = true;
+                // test hook (ekv_debug_expire_wait): a wait on a barrier nothing arrives on
+                if (a.debug_stall) ok = mbar_wait(bar(PB_STALL), 0, abort, a.wait_budget);
                 for (int jj = 0; ok && jj < 2 && jj < n; ++jj) {
-                    ok = mbar_wait(bar(PB_KINIT + jj), 0, abort, kWaitBudget);
+                    ok = mbar_wait(bar(PB_KINIT + jj), 0, abort, a.wait_budget);
                     tc_fence_after();
                     if (ok) issue_s(jj);
                 }
@@ -853,7 +857,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 }
                 if (!ok) pair_fail(a, abort, 1);
                 mma_commit_pair(bar(PB_DONE));
-                mbar_wait(bar(PB_DONE), 0, abort, kWaitBudget);
+                mbar_wait_drain(bar(PB_DONE), 0, a.wait_budget);
             }
         }
         __syncwarp();
@@ -867,7 +871,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             int issued = 0;
             for (int it = 0; it < np; ++it) {
                 const int r = it % NR;
-                if (it >= NR && !mbar_wait(bar(PB_RAW_EMPTY + r), stage_parity(it - NR, NR), abort, kWaitBudget)) {
+                if (it >= NR && !mbar_wait(bar(PB_RAW_EMPTY + r), stage_parity(it - NR, NR), abort, a.wait_budget)) {
                     pair_fail(a, abort, 2);
                     break;
                 }
@@ -878,7 +882,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             }
             if (lane == 0 && *abort)
                 for (int jj = max(0, issued - NR); jj < issued; ++jj)
-                    mbar_wait(bar(PB_RAW_FULL + jj % NR), stage_parity(jj, NR), abort, kWaitBudget / 4);
+                    mbar_wait_drain(bar(PB_RAW_FULL + jj % NR), stage_parity(jj, NR), a.wait_budget);
         } else {
             uint8_t *stages = kv ? sV : sK;
             const int sbytes = kv ? C::VH_BYTES : C::KH_BYTES;
@@ -886,7 +890,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             int issued = 0;
             for (int it = 0; it < n; ++it) {
                 const int st = it % NS;
-                if (it >= NS && !mbar_wait(bar(b_empty + st), stage_parity(it - NS, NS), abort, kWaitBudget)) {
+                if (it >= NS && !mbar_wait(bar(b_empty + st), stage_parity(it - NS, NS), abort, a.wait_budget)) {
                     pair_fail(a, abort, 2);
                     break;
                 }
@@ -897,14 +901,14 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             }
             if (lane == 0 && *abort)
                 for (int jj = max(0, issued - NS); jj < issued; ++jj)
-                    mbar_wait(bar(b_full + jj % NS), stage_parity(jj, NS), abort, kWaitBudget / 4);
+                    mbar_wait_drain(bar(b_full + jj % NS), stage_parity(jj, NS), a.wait_budget);
         }
     } else if (!Q8 && warp == C::RELAY_WARP) {
         // ---- bf16: forward "this CTA's K/V half landed" to rank 0, in the order its MMAs use
         // them: K(0), K(1), then V(j) and K(j + 2) per tile ----
         if (n > 0 && lane == 0) {
             auto relay = [&](uint32_t local, uint32_t parity, int remote) {
-                if (!mbar_wait(local, parity, abort, kWaitBudget)) return false;
+                if (!mbar_wait(local, parity, abort, a.wait_budget)) return false;
                 mbar_arrive_remote(bar0_rank0 + 8u * (uint32_t)remote);
                 return true;
             };
@@ -931,9 +935,9 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                 const uint8_t *raw = sRaw + rs * C::RAW_BYTES;
                 uint8_t *kdst = sK + st * C::KH_BYTES, *vdst = sV + st * C::VH_BYTES;
                 // both operand stages free (S(j - NS) and P.V(j - NS) done), raw landed
-                bool ok = jj < NS || (mbar_wait(bar(PB_K_EMPTY + st), stage_parity(jj - NS, NS), abort, kWaitBudget) &&
-                                      mbar_wait(bar(PB_V_EMPTY + st), stage_parity(jj - NS, NS), abort, kWaitBudget));
-                if (ok && prefix) ok = mbar_wait(bar(PB_RAW_FULL + rs), stage_parity(jj, C::NRAW), abort, kWaitBudget);
+                bool ok = jj < NS || (mbar_wait(bar(PB_K_EMPTY + st), stage_parity(jj - NS, NS), abort, a.wait_budget) &&
+                                      mbar_wait(bar(PB_V_EMPTY + st), stage_parity(jj - NS, NS), abort, a.wait_budget));
+                if (ok && prefix) ok = mbar_wait(bar(PB_RAW_FULL + rs), stage_parity(jj, C::NRAW), abort, a.wait_budget);
                 if (!ok) {
                     pair_fail(a, abort, 6);
                     break;
@@ -1005,6 +1009,10 @@ int pair_choose_splits(int64_t pair_units, int max_tiles, int sms) {
 // One launch of the pair kernel (plus the merge when keys are split), head_dim 256.
 int launch_attention_pair(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms) {
     const bool q8 = a.pool.dtype == EKV_DTYPE_Q8_0;
+    if (take_debug_stall()) {
+        a.debug_stall = 1;
+        a.wait_budget = kDebugWaitBudget;
+    }
     const int smem_bytes = q8 ? PairCfg<true>::SMEM : PairCfg<false>::SMEM;
     const int threads = q8 ? PairCfg<true>::THREADS : PairCfg<false>::THREADS;
     static int attr_done[64][2] = {};

@@ -1506,23 +1506,23 @@ extern "C" int ekv_debug_set_trace(unsigned long long *buf) {
 namespace ekv {
 #endif
 
-size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix) {
+size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix, int sms) {
     if (prm.q_heads <= 0 || p.kv_heads <= 0 || prm.q_heads % p.kv_heads) return 0;
     const int group = prm.q_heads / p.kv_heads;
     const int bn = p.head_dim > 128 ? 64 : 128;
     const int n_qtiles = (prm.q_tokens * group + kBM - 1) / kBM;
     const int64_t units = (int64_t)prm.n_batch * p.kv_heads * n_qtiles;
     const int max_tiles = (max_prefix + bn - 1) / bn + (prm.suffix_len + bn - 1) / bn;
-    const int sp = choose_splits(units, max_tiles);
+    const int sp = choose_split_count(units, max_tiles, sms);
     size_t need = sp <= 1 ? 0 : (size_t)units * sp * kBM * (p.head_dim + 2) * sizeof(float);
     if (p.head_dim == 256) {  // the CTA-pair kernel's choice (pairs of 128-row tiles)
         const int n_pairs = (prm.q_tokens * group + 2 * kBM - 1) / (2 * kBM);
         const int64_t pair_units = (int64_t)prm.n_batch * p.kv_heads * n_pairs;
-        const int psp = pair_choose_splits(pair_units, max_tiles, sm_count());
+        const int psp = pair_choose_splits(pair_units, max_tiles, sms);
         if (psp > 1) need = std::max(need, (size_t)pair_units * 2 * psp * kBM * (p.head_dim + 2) * sizeof(float));
         // the 128-key pair kernel's choice
         const int max_tiles128 = (max_prefix + 127) / 128 + (prm.suffix_len + 127) / 128;
-        const int psp128 = pair128_choose_splits(pair_units, max_tiles128, sm_count());
+        const int psp128 = pair128_choose_splits(pair_units, max_tiles128, sms);
         if (psp128 > 1)
             need = std::max(need, (size_t)pair_units * 2 * psp128 * kBM * (p.head_dim + 2) * sizeof(float));
     }

@@ -40,16 +40,46 @@ void mark_dirty(ekv_pool *p, int32_t id) {
     p->any_dirty = true;
 }
 
-int set_device(const ekv_pool *p) {
-    if (p->cfg.device < 0) return EKV_ERR_UNSUPPORTED;  // host-only pool
-    return cudaSetDevice(p->cfg.device) == cudaSuccess ? EKV_OK : EKV_ERR_CUDA;
-}
+// Makes the pool's device current for one entry point and restores the caller's current device when
+// the entry point returns (a library inside a host such as a ggml backend must not move its device).
+class DeviceScope {
+  public:
+    explicit DeviceScope(const ekv_pool *p) {
+        if (p->cfg.device < 0) {
+            rc_ = EKV_ERR_UNSUPPORTED;  // host-only pool
+            return;
+        }
+        if (cudaGetDevice(&prev_) != cudaSuccess) {
+            cudaGetLastError();
+            rc_ = EKV_ERR_CUDA;
+            return;
+        }
+        if (prev_ != p->cfg.device && cudaSetDevice(p->cfg.device) != cudaSuccess) {
+            rc_ = EKV_ERR_CUDA;
+            return;
+        }
+        switched_ = prev_ != p->cfg.device;
+    }
+    ~DeviceScope() {
+        if (switched_) cudaSetDevice(prev_);
+    }
+    DeviceScope(const DeviceScope &) = delete;
+    DeviceScope &operator=(const DeviceScope &) = delete;
+    int rc() const { return rc_; }
+
+  private:
+    int prev_ = 0;
+    int rc_ = EKV_OK;
+    bool switched_ = false;
+};
 
 }  // namespace
 
 namespace ekv {
 static std::atomic<unsigned long long> g_launches{0};
 void note_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+static std::atomic<int> g_debug_stall{0};
+bool take_debug_stall() { return g_debug_stall.exchange(0, std::memory_order_relaxed) != 0; }
 }  // namespace ekv
 
 extern "C" {
@@ -57,6 +87,11 @@ extern "C" {
 const char *ekv_version(void) { return "ekv 0.1 (sm_100a)"; }
 
 uint64_t ekv_launch_count(void) { return ekv::g_launches.load(std::memory_order_relaxed); }
+
+int ekv_debug_expire_wait(int32_t enable) {
+    ekv::g_debug_stall.store(enable ? 1 : 0, std::memory_order_relaxed);
+    return EKV_OK;
+}
 
 const char *ekv_strerror(int code) {
     switch (code) {
@@ -89,7 +124,13 @@ int ekv_pool_create(const ekv_pool_config *cfg, ekv_pool **out) {
     ekv_pool *p = new (std::nothrow) ekv_pool();
     if (!p) return EKV_ERR_ALLOC;
     p->cfg = c;
-    if (c.device >= 0 && cudaSetDevice(c.device) != cudaSuccess) {
+    const DeviceScope dev_scope(p);
+    if (c.device >= 0 && dev_scope.rc()) {
+        delete p;
+        return dev_scope.rc();
+    }
+    p->sms = 148;
+    if (c.device >= 0 && cudaDeviceGetAttribute(&p->sms, cudaDevAttrMultiProcessorCount, c.device) != cudaSuccess) {
         delete p;
         return EKV_ERR_CUDA;
     }
@@ -173,7 +214,7 @@ int ekv_pool_destroy(ekv_pool *p) {
         delete p;
         return EKV_OK;
     }
-    cudaSetDevice(p->cfg.device);
+    const DeviceScope dev_scope(p);
     cudaDeviceSynchronize();
     if (p->h_status) cudaFreeHost(p->h_status);
     if (p->dev_base) cudaFree(p->dev_base);
@@ -202,7 +243,8 @@ int ekv_pool_status(ekv_pool *p, int32_t *code, ekv_stream_t stream) {
         *code = EKV_OK;
         return EKV_OK;
     }
-    if (const int e = set_device(p)) return e;
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
     cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemcpyAsync(p->h_status, p->view.status, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaMemsetAsync(p->view.status, 0, 4 * sizeof(int32_t), s) != cudaSuccess ||
@@ -215,7 +257,8 @@ int ekv_pool_status(ekv_pool *p, int32_t *code, ekv_stream_t stream) {
 int ekv_pool_sync(ekv_pool *p, ekv_stream_t stream) {
     if (!p) return EKV_ERR_INVALID_ARG;
     if (!p->any_dirty || p->cfg.device < 0) return EKV_OK;
-    if (const int e = set_device(p)) return e;
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
     cudaStream_t s = (cudaStream_t)stream;
     const int32_t W = p->cfg.max_blocks_per_seq;
     // Pageable sources: cudaMemcpyAsync stages them before returning, so the host vectors may
@@ -394,7 +437,8 @@ int ekv_append(ekv_pool *p, int32_t layer, int32_t n_batch, const int32_t *seq_i
     if (!p || !seq_ids || !dst_pos || !n_rows || !src_row || !k || !v) return EKV_ERR_INVALID_ARG;
     if (layer < 0 || layer >= p->cfg.n_layers || n_batch < 0 || max_rows < 0) return EKV_ERR_INVALID_ARG;
     if (n_batch == 0 || max_rows == 0) return EKV_OK;
-    if (const int e = set_device(p)) return e;
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
     return ekv::launch_append(p->view, layer, n_batch, seq_ids, dst_pos, n_rows, src_row, max_rows,
                               k, v, (cudaStream_t)stream);
 }
@@ -405,7 +449,8 @@ int ekv_append_suffix(ekv_pool *p, int32_t layer, int32_t n_batch, const int32_t
     if (layer < 0 || layer >= p->cfg.n_layers || n_batch < 0 || n_rows < 0) return EKV_ERR_INVALID_ARG;
     if (n_rows > p->cfg.suffix_tokens) return EKV_ERR_RANGE;
     if (n_batch == 0 || n_rows == 0) return EKV_OK;
-    if (const int e = set_device(p)) return e;
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
     return ekv::launch_append_suffix(p->view, layer, n_batch, seq_ids, n_rows, k, v, (cudaStream_t)stream);
 }
 
@@ -417,7 +462,8 @@ int ekv_gather(ekv_pool *p, int32_t layer, int32_t id, int32_t pos0, int32_t n_r
     if (!valid_seq(p, id)) return EKV_ERR_NO_SEQ;
     if (pos0 < 0 || n_rows < 0 || pos0 + n_rows > p->seqs[(size_t)id].n_tokens) return EKV_ERR_RANGE;
     if (n_rows == 0) return EKV_OK;
-    if (const int e = set_device(p)) return e;
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
     return ekv::launch_gather(p->view, layer, id, pos0, n_rows, format, k_out, v_out, (cudaStream_t)stream);
 }
 
@@ -429,7 +475,8 @@ int ekv_gather_suffix(ekv_pool *p, int32_t layer, int32_t id, int32_t n_rows, in
     if (!valid_seq(p, id)) return EKV_ERR_NO_SEQ;
     if (n_rows < 0 || n_rows > p->cfg.suffix_tokens) return EKV_ERR_RANGE;
     if (n_rows == 0) return EKV_OK;
-    if (const int e = set_device(p)) return e;
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
     return ekv::launch_gather_suffix(p->view, layer, id, n_rows, format, k_out, v_out, (cudaStream_t)stream);
 }
 
@@ -485,12 +532,14 @@ static int fill_attn_args(ekv_pool *p, const ekv_attn_params *prm, const void *q
     a.q = (const uint16_t *)q;
     a.out = out;
     a.n_splits = 1;
+    a.wait_budget = ekv::kDefaultWaitBudget;
+    a.debug_stall = 0;
     return EKV_OK;
 }
 
 size_t ekv_attention_workspace_size(const ekv_pool *p, const ekv_attn_params *prm) {
     if (!p || !prm) return 0;
-    return ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens);
+    return ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens, p->sms);
 }
 
 int ekv_attention_algo(ekv_pool *p, const ekv_attn_params *prm, const void *q, void *out,
@@ -498,11 +547,12 @@ int ekv_attention_algo(ekv_pool *p, const ekv_attn_params *prm, const void *q, v
     ekv::AttnArgs a;
     const int rc = fill_attn_args(p, prm, q, out, a);
     if (rc) return rc;
-    if (const int e = set_device(p)) return e;
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
     if (algo == EKV_ALGO_SIMT) return ekv::launch_attention_simt(a, (cudaStream_t)stream);
     if (algo != EKV_ALGO_TC && algo != EKV_ALGO_TC_PAIR && algo != EKV_ALGO_TC_CTA && algo != EKV_ALGO_TC_PAIR64)
         return EKV_ERR_INVALID_ARG;
-    const size_t need = ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens);
+    const size_t need = ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens, p->sms);
     if (workspace && ((uintptr_t)workspace & 15)) return EKV_ERR_INVALID_ARG;
     if (workspace && need && workspace_bytes >= need) {
         // The split count and the workspace carve-up are recomputed by the launcher.
@@ -533,7 +583,8 @@ int ekv_append_suffix_attention(ekv_pool *p, const ekv_attn_params *prm, const v
     ekv::AttnArgs a;
     if (const int rc = fill_attn_args(p, prm, q, out, a)) return rc;
     if (workspace && ((uintptr_t)workspace & 15)) return EKV_ERR_INVALID_ARG;
-    if (const int e = set_device(p)) return e;
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
     const cudaStream_t s = (cudaStream_t)stream;
     if (p->cfg.head_dim == 256) {
         // the CTA-pair kernel reads the suffix from the caller's buffers; the slot is not written
@@ -544,7 +595,7 @@ int ekv_append_suffix_attention(ekv_pool *p, const ekv_attn_params *prm, const v
                                                  k_suffix, v_suffix, s);
         if (rc) return rc;
     }
-    const size_t need = ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens);
+    const size_t need = ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens, p->sms);
     if (workspace && need && workspace_bytes >= need) {
         a.ws_o = (float *)workspace;
         a.n_splits = 0;

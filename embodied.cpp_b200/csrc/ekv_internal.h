@@ -27,6 +27,7 @@ struct ekv_pool {
     std::vector<uint8_t> dirty;    // per sequence: table/length changed since the last sync
     bool any_dirty = false;
     int32_t *h_status = nullptr;   // pinned, 4 ints
+    int sms = 148;                 // SM count of the pool's device (key-split sizing)
 };
 
 namespace ekv {
@@ -54,7 +55,16 @@ struct AttnArgs {
     // most 64 query rows (the CTA's 128 rows hold several units, each seeing only its own keys);
     // 0 = one unit's 128-row tile per CTA
     int32_t pack;
+    // 64-key CTA-pair kernel: clock cycles a bounded wait gives up after, and the test hook of
+    // ekv_debug_expire_wait (1: the MMA-issuing thread waits on a barrier nothing arrives on)
+    long long wait_budget;
+    int32_t debug_stall;
 };
+
+constexpr long long kDefaultWaitBudget = 4000000000LL;  // clock cycles, about 2 s
+constexpr long long kDebugWaitBudget = 20000000LL;      // about 10 ms
+// Consumed by the next launch of the 64-key CTA-pair kernel (ekv_debug_expire_wait).
+bool take_debug_stall();
 
 // Kernels launched by this library in this process (ekv_launch_count); every launch site adds its
 // launches after cudaLaunch* returned.
@@ -77,7 +87,7 @@ int launch_attention_simt(const AttnArgs &a, cudaStream_t s);
 // query rows. Other head dims always run one CTA per 128 query rows.
 enum class TcKernel { Auto, Pair, OneCta, Pair64 };
 int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k);
-size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix);
+size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix, int sms);
 // CTA-pair kernel (head_dim 256); n_splits == 0 in `a` = choose from the workspace at a.ws_o
 int launch_attention_pair(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms);
 int pair_choose_splits(int64_t pair_units, int max_tiles, int sms);

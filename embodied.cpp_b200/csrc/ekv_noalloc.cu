@@ -35,6 +35,7 @@ extern "C" int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, c
     const int dev = pool->cfg.device;
     if (dev < 0) return EKV_ERR_UNSUPPORTED;  // host-only pool
     if (dev >= kMaxDevices) return EKV_ERR_UNSUPPORTED;
+    // sized for the pool's device (its SM count sets the key splits), whatever device is current
     const size_t need = ekv_attention_workspace_size(pool, p);
     if (need > (size_t)EKV_NOALLOC_SCRATCH_BYTES) return EKV_ERR_RANGE;
     void *ws = nullptr;
@@ -42,10 +43,17 @@ extern "C" int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, c
         std::lock_guard<std::mutex> lock(g_scratch_mu);
         if (!g_scratch_addr[dev]) {
             // Set-up, once per device, with that device current: the array's name is only a
-            // host-side stand-in, the kernels need its device address.
-            if (cudaSetDevice(dev) != cudaSuccess) return EKV_ERR_CUDA;
+            // host-side stand-in, the kernels need its device address. The caller's current device
+            // is put back afterwards.
+            int prev = 0;
+            if (cudaGetDevice(&prev) != cudaSuccess) {
+                cudaGetLastError();
+                return EKV_ERR_CUDA;
+            }
+            if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return EKV_ERR_CUDA;
             void *addr = nullptr;
             const cudaError_t e = cudaGetSymbolAddress(&addr, g_ekv_noalloc_scratch);
+            if (prev != dev) cudaSetDevice(prev);
             if (e != cudaSuccess || !addr) {
                 cudaGetLastError();
                 return EKV_ERR_CUDA;

@@ -68,6 +68,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Bounded wait that ignores the abort flag: for draining work already in flight (bulk copies, MMAs)
+// before a CTA that gave up releases its shared or tensor memory.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, long long budget) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (clock64() - t0 > budget) return false;
+    }
+}
+
 // ---- bulk async copy global -> shared (completion counted in bytes on an mbarrier) ----
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
     asm volatile(

@@ -84,7 +84,7 @@ EXPORTED = [
     "ekv_seq_get", "ekv_append", "ekv_append_suffix", "ekv_gather", "ekv_gather_suffix",
     "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
     "ekv_strerror", "ekv_attention_noalloc", "ekv_flash_attn_ext",
-    "ekv_mul_mat_soft_max_mul_mat", "ekv_append_suffix_attention", "ekv_launch_count",
+    "ekv_mul_mat_soft_max_mul_mat", "ekv_append_suffix_attention", "ekv_launch_count", "ekv_debug_expire_wait",
 ]
 NOALLOC_SCRATCH_BYTES = 16 << 20  # EKV_NOALLOC_SCRATCH_BYTES
 
@@ -108,6 +108,7 @@ def _load():
         "ekv_seq_evict_front": ([vp, i32, i32], C.c_int),
         "ekv_seq_append_tokens": ([vp, i32, i32, i32], C.c_int),
         "ekv_seq_clear_pred": ([vp, i32], C.c_int),
+        "ekv_debug_expire_wait": ([i32], C.c_int),
         "ekv_seq_restore": ([vp, i32, i32], C.c_int),
         "ekv_seq_get_pred": ([vp, i32, pi32, pi32], C.c_int),
         "ekv_seq_get": ([vp, i32, pi32, pi32, pi32, i32], C.c_int),

@@ -309,6 +309,14 @@ int ekv_mul_mat_soft_max_mul_mat(const ekv_tensor *k, const ekv_tensor *q, const
                                  const ekv_tensor *mask, float scale, float max_bias, const ekv_tensor *dst,
                                  ekv_stream_t stream);
 
+/* Test hook for the kernels' failure path: with enable != 0, the next launch of the 64-key CTA-pair
+ * kernel (head_dim 256 on Q8_0 pools, or EKV_ALGO_TC_PAIR64) has its MMA-issuing thread wait on a
+ * barrier that nothing arrives on, and every wait of that launch gives up after about 10 ms (instead
+ * of about 2 s). The launch records the kernel timeout in the pool's status word (ekv_pool_status),
+ * writes zeros, drains its copies and MMAs in flight and returns; the context stays usable. No
+ * counterpart in the reference. */
+int ekv_debug_expire_wait(int32_t enable);
+
 const char *ekv_version(void);
 /* Kernels this library has launched in this process, on every device (a diagnostic: the difference
  * across a region of calls is the launches they made). */

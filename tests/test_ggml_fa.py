@@ -322,3 +322,26 @@ def test_triple_pi05_layer(contig_v, masked):
     torch.cuda.synchronize()
     want = oracle.flash_attn_ext(_np(q), _np(k), _np(vf)[None, None], _np(mask), scale=1.0 / 16)
     assert np.abs(_np(dst) - want.transpose(0, 2, 1, 3)).max() < TOL
+
+
+@pytest.mark.gpu
+def test_triple_fully_masked_row_gives_zero():
+    """A query row whose every key is masked: ggml's soft_max_ext would give NaN there (max -inf,
+    exp(-inf - -inf)); the fused triple gives 0, as the fused flash_attn_ext op and
+    dense_masked_attention_ref (models/lingbot_va.cpp:9503-9506) do. The other rows are unchanged."""
+    import torch
+    torch.manual_seed(33)
+    Tq, Hq, D, Tk = 6, 2, 64, 40
+    k = (torch.randn(1, 1, Tk, D, device="cuda") * 0.5)
+    vf = (torch.randn(Tk, D, device="cuda") * 0.5)
+    q = (torch.randn(1, Hq, Tq, D, device="cuda") * 0.5)
+    mask = torch.zeros(1, 1, Tq, Tk, device="cuda")
+    mask[..., 2, :] = float("-inf")                            # row 2 sees no key
+    mask[..., 4, 10:] = float("-inf")
+    dst = torch.full((1, Hq, Tq, D), float("nan"), device="cuda")
+    ekv.mul_mat_soft_max_mul_mat(k, q, vf.t()[None, None], mask, dst, scale=0.125)
+    torch.cuda.synchronize()
+    got = _np(dst)
+    assert np.all(got[:, :, 2] == 0.0)
+    want = oracle.flash_attn_ext(_np(q), _np(k), _np(vf)[None, None], _np(mask), scale=0.125)
+    assert np.abs(got - want.transpose(0, 2, 1, 3)).max() < TOL
