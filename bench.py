@@ -363,6 +363,171 @@ class LingbotWorkload:
                 self.pool.attention(self.params[w][l], self.q[i, l], self.out[i, l], workspace=self.ws, stream=stream)
 
 
+class ServeWorkload:
+    """a stream of pi0.5-shaped Q8_0 requests (prefix U[600, 1000], 50 action
+    tokens, 10 denoise steps, 18 layers) served by the library's batching scheduler (ekv_sched_*)
+    over one pool sized to `pool_gb` GB. Requests arrive at 256 / 10 per tick (a tick = one denoise
+    step of every active request = 18 ekv_append_suffix_attention calls over the whole batch, plus
+    the prefix appends of the requests admitted in it), so that in steady state 256 requests are
+    active, about 26 complete per tick and the ones admitted next take the blocks they gave back
+    (lowest free first). One bench step = 10 ticks (the work of one batch-256 predict)."""
+
+    NSET = 36  # distinct per-call input sets (two ticks' worth, > L2), cycled
+
+    def __init__(self, cfg, seed, device, pool_gb):
+        import torch
+        import ekv
+        self.torch, self.ekv = torch, ekv
+        self.B, self.plo, self.phi = cfg["batch"], cfg["plo"], cfg["phi"]
+        self.rng = np.random.default_rng(seed)
+        row_q8 = HKV * D // 32 * 34
+        self.block_bytes_all_layers = N_LAYERS * 2 * BT * row_q8
+        self.n_blocks = int(pool_gb * 1e9 // self.block_bytes_all_layers)
+        self.pool_gb = pool_gb
+        self.pool = ekv.Pool(device=device, dtype=ekv.DTYPE_Q8_0, block_tokens=BT, n_blocks=self.n_blocks,
+                             kv_heads=HKV, head_dim=D, n_layers=N_LAYERS, max_seqs=self.B,
+                             max_blocks_per_seq=(self.phi + BT - 1) // BT, suffix_tokens=TQ)
+        self.sched = ekv.Scheduler(self.pool, self.B, N_STEPS)
+        dev = f"cuda:{device}"
+        g = torch.Generator(device=dev).manual_seed(seed)
+        rn = lambda *shape: (torch.randn(shape, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        self.src_rows = 64 * self.phi  # admissions of one tick, packed
+        self.pk = rn(N_LAYERS, self.src_rows, HKV, D)
+        self.pv = rn(N_LAYERS, self.src_rows, HKV, D)
+        self.sk = rn(self.NSET, self.B, TQ, HKV, D)
+        self.sv = rn(self.NSET, self.B, TQ, HKV, D)
+        self.q = rn(self.NSET, self.B, TQ, HQ, D)
+        self.out = torch.empty((self.NSET, self.B, TQ, HQ, D), dtype=torch.bfloat16, device=dev)
+        self.ws = None
+        self.next_id, self.tick_no, self.call_no = 0, 0, 0
+        self.pvalid = {}
+
+    def arrivals(self):
+        k = self.tick_no
+        n = (self.B * (k + 1)) // N_STEPS - (self.B * k) // N_STEPS
+        for _ in range(n):
+            plen = int(self.rng.integers(self.plo, self.phi + 1))
+            self.sched.submit(self.next_id, plen, plen)
+            self.pvalid[self.next_id] = plen
+            self.next_id += 1
+
+    def tick(self, stream, ev=None):
+        """Enqueue one tick; returns its counts. `ev` (start, end) brackets the 18 attention calls."""
+        ekv = self.ekv
+        self.arrivals()
+        t = self.sched.begin_tick(stream)
+        if t.admitted_index:
+            if t.admitted_rows > self.src_rows:
+                raise RuntimeError("admissions of one tick exceed the packed source rows")
+            for l in range(N_LAYERS):
+                self.pool.append(l, t.admitted_seq_ids, t.admitted_zeros, t.admitted_prefix_len, t.admitted_src_row,
+                                 t.max_admitted_prefix, self.pk[l], self.pv[l], stream=stream)
+        n = t.n_batch
+        prms = [self.pool.attention_params(layer=l, seq_ids=t.seq_ids, q_tokens=TQ, q_heads=HQ, scale=SCALE,
+                                           suffix_len=TQ, out_dtype=ekv.DTYPE_BF16, prefix_valid=t.prefix_valid)
+                for l in range(N_LAYERS)]
+        need = max(self.pool.workspace_size(p) for p in prms) if n else 0
+        if need and (self.ws is None or self.ws.numel() < need):
+            self.ws = self.torch.empty(need, dtype=self.torch.uint8, device=self.q.device)
+        if ev is not None:
+            ev[0].record(stream)
+        for l in range(N_LAYERS):
+            c = self.call_no % self.NSET
+            self.call_no += 1
+            if n:
+                self.pool.append_suffix_attention(prms[l], self.sk[c, :n], self.sv[c, :n], self.q[c, :n],
+                                                  self.out[c, :n], workspace=self.ws, stream=stream)
+        if ev is not None:
+            ev[1].record(stream)
+        lk = np.array([self.pvalid[r] for r in t.request_ids], np.float64) + TQ
+        flop = float((4.0 * TQ * HQ * lk * D).sum()) * N_LAYERS
+        b_kv = 34.0 / 32.0
+        byts = float((TQ * HQ * D * 2 * 2 + 2 * HKV * (lk - TQ) * D * b_kv + 2 * HKV * TQ * D * 2).sum()) * N_LAYERS
+        done = self.sched.end_tick()
+        for r in done:
+            del self.pvalid[r]
+        self.tick_no += 1
+        return dict(qtok=n * TQ * N_LAYERS, flop=flop, bytes=byts, reused=t.blocks_reused,
+                    admitted=len(t.admitted_index), active=n, completed=len(done))
+
+
+def run_serve(args, cfg):
+    """BASELINE config 5 through the batching scheduler: the same JSON contract, weak scaling (each
+    rank serves its own request stream with 256 active), no data-path collective."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
+    free, _ = torch.cuda.mem_get_info(local)
+    pool_gb = min(args.pool_gb, free / 1e9 - 12.0)  # room for the inputs and the context
+    wl = ServeWorkload(cfg, 1234 + rank, local, pool_gb)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup * N_STEPS):
+        wl.tick(stream)
+    torch.cuda.synchronize()
+    if wl.pool.status() != 0:
+        raise RuntimeError("device status word set during warm-up")
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    clocks = Clocks(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n_ticks = args.steps * N_STEPS
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ticks)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = wl.ekv.lib.ekv_launch_count()
+    tot = dict(qtok=0, flop=0.0, bytes=0.0, reused=0, admitted=0, completed=0, active=0)
+    t_start.record(stream)
+    for k in range(n_ticks):
+        r = wl.tick(stream, evs[k])
+        for key in tot:
+            tot[key] += r[key]
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    launches = wl.ekv.lib.ekv_launch_count() - n0
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = dispatch.max_over_ranks(t_start.elapsed_time(t_end), device=f"cuda:{local}")
+    attn_s = sum(a.elapsed_time(b) for a, b in evs) / 1e3
+    n_calls = n_ticks * N_LAYERS
+    call_s = attn_s / n_calls
+    peaks = load_peaks()
+    ach = tot["flop"] / attn_s / 1e12
+    roof = {"bound": "tensor", "achieved": ach, "peak": peaks["tc"], "unit": "TFLOP/s", "frac": ach / peaks["tc"],
+            "traffic": None, "peak_source": peaks["source"] + " (burst bf16 figure)", "avg_launch_us": call_s * 1e6,
+            "kernel": "attn_pair_kernel<Q8>",
+            "algorithmic_per_launch": {"flop": tot["flop"] / n_calls, "bytes": tot["bytes"] / n_calls},
+            "timed": "CUDA events around each tick's 18 ekv_append_suffix_attention calls, divided by the calls"}
+    status = wl.pool.status()
+    line = {"metric": METRIC, "value": world * tot["qtok"] / (ms / 1e3), "unit": "query-tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 MMA, f32 accumulate (Q8_0 cache)",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "description": cfg["desc"], "max_active_per_gpu": wl.B,
+                       "pool_gb": round(wl.pool_gb, 1), "pool_blocks": wl.n_blocks,
+                       "step": "10 scheduler ticks (one denoise step of every active request each)",
+                       "parallelism": f"request-sharded x{world}", "l2": "inputs > L2 (36 distinct call sets)"},
+            "serving": {"avg_active": tot["active"] / n_ticks, "admitted_per_step": tot["admitted"] / args.steps,
+                        "completed_per_step": tot["completed"] / args.steps,
+                        "blocks_reused_per_step": tot["reused"] / args.steps,
+                        "timing": "CUDA events from the first to the last tick, host scheduling and prefix "
+                                  "appends inside"},
+            "roofline": roof, "clocks": clk, "gpu_launches": int(launches), "device_status": status}
+    wl.sched.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_other(args, cfg):
     """Configs 3 and 4 on one GPU: the same JSON contract as the default config, without the
     end-to-end and CPU legs (the headline metric is config 2's)."""
@@ -559,6 +724,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the requests per GPU (profiling cases)")
+    ap.add_argument("--pool-gb", type=float, default=150.0, help="serve_q8_b256: pool size per GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config in OTHER_CONFIGS:
@@ -574,6 +740,9 @@ def main():
         args.workload = f"{args.config}@batch{args.batch}"  # a profiling case, not the headline config
     if args.impl == "reference":
         run_reference(args, cfg)
+        return
+    if args.config == "serve_q8_b256":
+        run_serve(args, cfg)
         return
 
     import torch

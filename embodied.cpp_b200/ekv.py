@@ -71,6 +71,16 @@ class AttnParams(C.Structure):
                 ("flex_window", C.c_int32)]
 
 
+class SchedBatch(C.Structure):
+    _fields_ = [("n_batch", C.c_int32), ("request_ids", C.POINTER(C.c_uint64)),
+                ("seq_ids_host", C.POINTER(C.c_int32)), ("steps", C.POINTER(C.c_int32)),
+                ("seq_ids", C.c_void_p), ("prefix_valid", C.c_void_p), ("n_admitted", C.c_int32),
+                ("max_admitted_prefix", C.c_int32), ("admitted_index", C.POINTER(C.c_int32)),
+                ("admitted_seq_ids", C.c_void_p), ("admitted_zeros", C.c_void_p),
+                ("admitted_prefix_len", C.c_void_p), ("admitted_src_row", C.c_void_p), ("admitted_rows", C.c_int32),
+                ("blocks_reused", C.c_int64), ("queued", C.c_int32)]
+
+
 class Tensor(C.Structure):
     """ekv_tensor: a ggml-ordered strided device tensor (ne[0] fastest, nb in bytes)."""
     _fields_ = [("data", C.c_void_p), ("type", C.c_int32), ("ne", C.c_int64 * 4), ("nb", C.c_int64 * 4)]
@@ -85,6 +95,8 @@ EXPORTED = [
     "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
     "ekv_strerror", "ekv_attention_noalloc", "ekv_flash_attn_ext",
     "ekv_mul_mat_soft_max_mul_mat", "ekv_append_suffix_attention", "ekv_launch_count", "ekv_debug_expire_wait",
+    "ekv_flow_step_f32", "ekv_guidance_f32", "ekv_sched_create", "ekv_sched_destroy", "ekv_sched_submit",
+    "ekv_sched_begin_tick", "ekv_sched_end_tick", "ekv_sched_stats",
 ]
 NOALLOC_SCRATCH_BYTES = 16 << 20  # EKV_NOALLOC_SCRATCH_BYTES
 
@@ -109,7 +121,15 @@ def _load():
         "ekv_seq_append_tokens": ([vp, i32, i32, i32], C.c_int),
         "ekv_seq_clear_pred": ([vp, i32], C.c_int),
         "ekv_debug_expire_wait": ([i32], C.c_int),
+        "ekv_flow_step_f32": ([vp, vp, C.c_int64, C.c_float, i32, vp], C.c_int),
+        "ekv_guidance_f32": ([vp, vp, C.c_int64, C.c_float, i32, i32, vp], C.c_int),
         "ekv_seq_restore": ([vp, i32, i32], C.c_int),
+        "ekv_sched_create": ([vp, i32, i32, C.POINTER(vp)], C.c_int),
+        "ekv_sched_destroy": ([vp], C.c_int),
+        "ekv_sched_submit": ([vp, C.c_uint64, i32, i32], C.c_int),
+        "ekv_sched_begin_tick": ([vp, C.POINTER(SchedBatch), vp], C.c_int),
+        "ekv_sched_end_tick": ([vp, C.POINTER(C.c_uint64), i32, pi32], C.c_int),
+        "ekv_sched_stats": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64), pi32, pi32], C.c_int),
         "ekv_seq_get_pred": ([vp, i32, pi32, pi32], C.c_int),
         "ekv_seq_get": ([vp, i32, pi32, pi32, pi32, i32], C.c_int),
         "ekv_append": ([vp, i32, i32, vp, vp, vp, vp, i32, vp, vp, vp], C.c_int),
@@ -292,6 +312,100 @@ class Pool:
         check(lib.ekv_append_suffix_attention(self.h, C.byref(params), _ptr(k_suffix), _ptr(v_suffix), _ptr(q),
                                               _ptr(out), _ptr(workspace), ws_bytes, _stream(stream)),
               "ekv_append_suffix_attention")
+
+
+class DevArray:
+    """A device (or, for a host-only pool, host) int32 array owned by the library: what
+    Pool.attention_params and Pool.append read from a tensor (numel, data_ptr)."""
+
+    def __init__(self, ptr, n):
+        self.ptr, self.n = ptr or 0, n
+
+    def numel(self):
+        return self.n
+
+    def data_ptr(self):
+        return self.ptr
+
+
+@dataclass
+class Tick:
+    """One tick of the scheduler (ekv_sched_batch): every active request runs its next denoise step."""
+    n_batch: int
+    request_ids: list
+    seq_ids_host: list
+    steps: list
+    seq_ids: DevArray
+    prefix_valid: DevArray
+    admitted_index: list
+    admitted_seq_ids: DevArray
+    admitted_zeros: DevArray
+    admitted_prefix_len: DevArray
+    admitted_src_row: DevArray
+    admitted_rows: int
+    max_admitted_prefix: int
+    blocks_reused: int
+    queued: int
+
+
+class Scheduler:
+    """Batching scheduler over a pool (ekv_sched_*): first come first served admission, one denoise
+    step of every active request per tick, blocks freed (and reused) on completion."""
+
+    def __init__(self, pool: Pool, max_batch: int, n_steps: int):
+        self.pool = pool
+        self.h = C.c_void_p()
+        check(lib.ekv_sched_create(pool.h, max_batch, n_steps, C.byref(self.h)), "ekv_sched_create")
+
+    def close(self):
+        if self.h:
+            lib.ekv_sched_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def submit(self, request_id, prefix_len, prefix_valid=None):
+        pv = prefix_len if prefix_valid is None else prefix_valid
+        check(lib.ekv_sched_submit(self.h, request_id, prefix_len, pv), "ekv_sched_submit")
+
+    def begin_tick(self, stream=None) -> Tick:
+        b = SchedBatch()
+        s = None if self.pool.cfg.device < 0 else _stream(stream)
+        check(lib.ekv_sched_begin_tick(self.h, C.byref(b), s), "ekv_sched_begin_tick")
+        n, na = b.n_batch, b.n_admitted
+        return Tick(n, list(b.request_ids[:n]) if n else [], list(b.seq_ids_host[:n]) if n else [],
+                    list(b.steps[:n]) if n else [], DevArray(b.seq_ids, n), DevArray(b.prefix_valid, n),
+                    list(b.admitted_index[:na]) if na else [], DevArray(b.admitted_seq_ids, na),
+                    DevArray(b.admitted_zeros, na), DevArray(b.admitted_prefix_len, na),
+                    DevArray(b.admitted_src_row, na), b.admitted_rows, b.max_admitted_prefix,
+                    b.blocks_reused, b.queued)
+
+    def end_tick(self, cap=4096) -> list:
+        arr = (C.c_uint64 * cap)()
+        nf = C.c_int32()
+        check(lib.ekv_sched_end_tick(self.h, arr, cap, C.byref(nf)), "ekv_sched_end_tick")
+        return list(arr[: min(nf.value, cap)])
+
+    def stats(self) -> dict:
+        c, r, a, q = C.c_int64(), C.c_int64(), C.c_int32(), C.c_int32()
+        check(lib.ekv_sched_stats(self.h, C.byref(c), C.byref(r), C.byref(a), C.byref(q)), "ekv_sched_stats")
+        return dict(completed=c.value, blocks_reused=r.value, active=a.value, queued=q.value)
+
+
+def flow_step(sample, velocity, delta, bf16_round=False, stream=None):
+    """ekv_flow_step_f32 on contiguous f32 torch tensors of equal size (sample updated in place)."""
+    check(lib.ekv_flow_step_f32(_ptr(sample), _ptr(velocity), sample.numel(), float(delta), 1 if bf16_round else 0,
+                                _stream(stream)), "ekv_flow_step_f32")
+
+
+def guidance(cond, uncond, scale, use_guidance=True, bf16_round=False, stream=None):
+    """ekv_guidance_f32 on contiguous f32 torch tensors (cond updated in place)."""
+    check(lib.ekv_guidance_f32(_ptr(cond), _ptr(uncond), cond.numel(), float(scale), 1 if use_guidance else 0,
+                               1 if bf16_round else 0, _stream(stream)), "ekv_guidance_f32")
 
 
 _TORCH_DTYPES = {"torch.float32": DTYPE_F32, "torch.float16": DTYPE_F16, "torch.bfloat16": DTYPE_BF16}

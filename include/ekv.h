@@ -309,6 +309,62 @@ int ekv_mul_mat_soft_max_mul_mat(const ekv_tensor *k, const ekv_tensor *q, const
                                  const ekv_tensor *mask, float scale, float max_bias, const ekv_tensor *dst,
                                  ekv_stream_t stream);
 
+/* ---- batching scheduler over the pool ----
+ * The reference serves one vla.PredictRequest at a time (serving/vla-server.cpp:240-523). The scheduler
+ * queues requests (request_id of serving/vla.proto:33-71 and the prefix they produce), admits them
+ * first come first served while sequence slots and blocks allow, runs every active request's next
+ * denoise step in the same layer-step calls (a tick), and frees a request's blocks when its last step
+ * is done, so later admissions reuse them. Per tick the caller: ekv_sched_begin_tick, appends the
+ * prefix K/V of the admitted requests (ekv_append with the batch's admitted_* arrays, all layers), runs the
+ * layer-steps (ekv_attn_params.seq_ids / prefix_valid = the batch's arrays, n_batch = n_batch), then
+ * ekv_sched_end_tick. Host pointers in the batch stay valid until the next begin_tick; device arrays
+ * are rewritten (stream-ordered) by it. One scheduler per pool; calls are not re-entrant. */
+typedef struct ekv_sched ekv_sched;
+typedef struct ekv_sched_batch {
+    int32_t n_batch;                /* active requests this tick                                   */
+    const uint64_t *request_ids;    /* host [n_batch]                                              */
+    const int32_t *seq_ids_host;    /* host [n_batch]                                              */
+    const int32_t *steps;           /* host [n_batch]: the denoise step each request runs this tick */
+    const int32_t *seq_ids;         /* device [n_batch]: ekv_attn_params.seq_ids                    */
+    const int32_t *prefix_valid;    /* device [n_batch]: ekv_attn_params.prefix_valid               */
+    int32_t n_admitted;             /* requests admitted this tick (their prefix K/V are due)       */
+    int32_t max_admitted_prefix;    /* the longest of their prefixes (ekv_append's max_rows)        */
+    const int32_t *admitted_index;  /* host [n_admitted]: their positions in the batch              */
+    const int32_t *admitted_seq_ids;    /* device [n_admitted]: ekv_append's seq_ids              */
+    const int32_t *admitted_zeros;      /* device [n_admitted]: zeros (ekv_append's dst_pos)        */
+    const int32_t *admitted_prefix_len; /* device [n_admitted]: ekv_append's n_rows               */
+    const int32_t *admitted_src_row;    /* device [n_admitted]: ekv_append's src_row when the admitted
+                                           requests' prefix rows are packed back to back in order */
+    int32_t admitted_rows;              /* the packed rows in all                                  */
+    int64_t blocks_reused;          /* blocks handed to this tick's admissions that a request held before */
+    int32_t queued;                 /* requests still waiting                                       */
+} ekv_sched_batch;
+int ekv_sched_create(ekv_pool *pool, int32_t max_batch, int32_t n_steps, ekv_sched **out);
+int ekv_sched_destroy(ekv_sched *sched);
+/* Queue a request whose prefix has prefix_len tokens (keys >= prefix_valid are padding). */
+int ekv_sched_submit(ekv_sched *sched, uint64_t request_id, int32_t prefix_len, int32_t prefix_valid);
+int ekv_sched_begin_tick(ekv_sched *sched, ekv_sched_batch *batch, ekv_stream_t stream);
+/* Every active request has run one more step; finished ones (up to cap ids into `finished`) free their
+ * sequences. */
+int ekv_sched_end_tick(ekv_sched *sched, uint64_t *finished, int32_t cap, int32_t *n_finished);
+int ekv_sched_stats(const ekv_sched *sched, int64_t *completed, int64_t *blocks_reused, int32_t *active,
+                    int32_t *queued);
+
+/* ---- the sampler's per-step elementwise work (a denoise loop with no host round trip) ---- */
+/* sample[i] += delta * velocity[i] over n f32 values: the product and the sum each rounded (no fused
+ * multiply-add), then rounded to bf16 (nearest even) when bf16_round != 0. Replaces the Euler step of
+ * pi0.5 (x_t + dt * velocity, models/pi05.cpp:856), GR00T's host-side action update (actions += dt *
+ * velocity after a device-to-host copy every step, models/groot_n1.cpp:756-766) and
+ * lingbot_scheduler_step_f32 (kernels/lingbot/lingbot_flex_attn_cuda.cu:40-52, 305-319). */
+int ekv_flow_step_f32(float *sample, const float *velocity, int64_t n, float delta, int32_t bf16_round,
+                      ekv_stream_t stream);
+/* Classifier-free guidance in place over n f32 values: c = cond_in_out[i] (bf16-rounded when
+ * bf16_round != 0); with use_guidance, u = uncond[i] (likewise rounded) and c = u + scale * (c - u)
+ * (rounded again). Replaces lingbot_model_output_guidance_f32
+ * (kernels/lingbot/lingbot_flex_attn_cuda.cu:54-73, 321-337). */
+int ekv_guidance_f32(float *cond_in_out, const float *uncond, int64_t n, float scale, int32_t use_guidance,
+                     int32_t bf16_round, ekv_stream_t stream);
+
 /* Test hook for the kernels' failure path: with enable != 0, the next launch of the 64-key CTA-pair
  * kernel (head_dim 256 on Q8_0 pools, or EKV_ALGO_TC_PAIR64) has its MMA-issuing thread wait on a
  * barrier that nothing arrives on, and every wait of that launch gives up after about 10 ms (instead

@@ -150,3 +150,59 @@ class PoolModel:
         q["n"] = n_tokens
         q["pred"] = (0, 0)
         return "ok"
+
+
+class SchedModel:
+    """Reference model of the batching scheduler over PoolModel: requests queue first come first
+    served; a tick admits from the head of the queue while a sequence slot and the request's prefix
+    blocks are free (the head that does not fit waits, and so does everything behind it), then every
+    active request runs one step; a request that has run n_steps frees its sequence. The reference
+    serves one request per predict (serving/vla-server.cpp:240-523); this is the batched version."""
+
+    def __init__(self, pool: PoolModel, max_batch: int, n_steps: int):
+        self.pool, self.max_batch, self.n_steps = pool, max_batch, n_steps
+        self.queue, self.active = [], []
+        self.used = set()
+        self.completed = self.reused = 0
+
+    def submit(self, rid, prefix_len, prefix_valid):
+        if self.pool._need(prefix_len) > min(self.pool.max_bps, self.pool.n_blocks):
+            return "range"
+        self.queue.append((rid, prefix_len, prefix_valid))
+        return "ok"
+
+    def begin_tick(self):
+        for a in self.active:
+            a["adm"] = False
+        reused = 0
+        while self.queue and len(self.active) < self.max_batch:
+            rid, plen, pvalid = self.queue[0]
+            s = self.pool.seq_create()
+            if s is None:
+                break
+            if self.pool.seq_resize(s, plen) != "ok":
+                self.pool.seq_free(s)
+                break
+            for b in self.pool.seqs[s]["blocks"]:
+                reused += b in self.used
+                self.used.add(b)
+            self.queue.pop(0)
+            self.active.append(dict(rid=rid, seq=s, step=0, plen=plen, pvalid=pvalid, adm=True))
+        self.reused += reused
+        return dict(request_ids=[a["rid"] for a in self.active], seq_ids=[a["seq"] for a in self.active],
+                    steps=[a["step"] for a in self.active], prefix_valid=[a["pvalid"] for a in self.active],
+                    admitted_index=[i for i, a in enumerate(self.active) if a["adm"]],
+                    blocks_reused=reused, queued=len(self.queue))
+
+    def end_tick(self):
+        done, keep = [], []
+        for a in self.active:
+            a["step"] += 1
+            if a["step"] < self.n_steps:
+                keep.append(a)
+            else:
+                self.pool.seq_free(a["seq"])
+                done.append(a["rid"])
+                self.completed += 1
+        self.active = keep
+        return done

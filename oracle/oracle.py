@@ -312,3 +312,27 @@ def attention_ggml_q8_0(q, k, v, n_prefix, scale):
             out[b, :, h] = (p / p.sum(axis=1, keepdims=True)) @ vh[b, :, h // g]
     del n_prefix
     return out
+
+
+def flow_step(sample, velocity, delta, bf16_round=False):
+    """The sampler's Euler step as the reference computes it in f32: sample + (velocity * delta),
+    the product and the sum each rounded to f32 (lingbot_scheduler_step_f32's __fmul_rn / __fadd_rn,
+    kernels/lingbot/lingbot_flex_attn_cuda.cu:40-52; x_t + scale(velocity, dt), models/pi05.cpp:856),
+    then bf16 round-to-nearest-even when bf16_round (lingbot_bf16_round_device, :36-38)."""
+    s = np.asarray(sample, np.float32)
+    r = (s + (np.asarray(velocity, np.float32) * np.float32(delta)).astype(np.float32)).astype(np.float32)
+    return bf16_to_f32(f32_to_bf16(r)) if bf16_round else r
+
+
+def guidance(cond, uncond, scale, use_guidance=True, bf16_round=False):
+    """Classifier-free guidance of lingbot_model_output_guidance_f32 (kernels/lingbot/
+    lingbot_flex_attn_cuda.cu:54-73): c (bf16-rounded when asked), then u + scale * (c - u) with each
+    operation rounded to f32 and the result bf16-rounded when asked."""
+    rnd = (lambda x: bf16_to_f32(f32_to_bf16(np.asarray(x, np.float32)))) if bf16_round else (lambda x: x)
+    c = rnd(np.asarray(cond, np.float32))
+    if not use_guidance:
+        return c
+    u = rnd(np.asarray(uncond, np.float32))
+    d = (c - u).astype(np.float32)
+    v = (u + (np.float32(scale) * d).astype(np.float32)).astype(np.float32)
+    return rnd(v)
