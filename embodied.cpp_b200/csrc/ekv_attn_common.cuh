@@ -36,11 +36,28 @@ __device__ __forceinline__ void trace_clock(int slot) {
     if (trace_cta()) s_trace[slot] = (unsigned int)clock64();
 }
 #define TRACE_CLK(slot) trace_clock(slot)
+// every CTA: [start, end, SM id] at 2 * kTraceSlots + 4 * (linear block id)
+__device__ __forceinline__ unsigned long long trace_span_slot() {
+    return 2ull * kTraceSlots + 4ull * (blockIdx.x + gridDim.x * (blockIdx.y + (unsigned long long)gridDim.y * blockIdx.z));
+}
 __device__ __forceinline__ void trace_init() {
+    if (c_trace) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        c_trace[trace_span_slot()] = t;
+    }
     if (trace_cta())
         for (int i = 0; i < kTraceSlots; ++i) s_trace[i] = 0u;
 }
 __device__ __forceinline__ void trace_flush() {
+    if (c_trace && threadIdx.x == 0) {
+        unsigned long long t;
+        unsigned int smid;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        c_trace[trace_span_slot() + 1] = t;
+        c_trace[trace_span_slot() + 2] = smid;
+    }
     if (trace_cta())
         for (int i = threadIdx.x; i < kTraceSlots; i += blockDim.x) c_trace[blockIdx.x * kTraceSlots + i] = s_trace[i];
 }

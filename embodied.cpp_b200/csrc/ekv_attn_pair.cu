@@ -705,9 +705,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
     }
     const PairPlan pl = make_pair_plan(a);
     if (threadIdx.x == 0) TRACE(1);
-    const uint32_t peer = (uint32_t)(pl.rank ^ 1);
     const uint32_t bar0_rank0 = mapa_shared(bar0, 0);  // rank 0's barrier block (cluster window)
-    const uint32_t bar0_peer = mapa_shared(bar0, peer);
     if (threadIdx.x == 0 && !pl.sk.ok) report_error(a.pool.status, DEV_ERR_BAD_SEQ, pl.b, a.seq_ids[pl.b], 3);
 
     if (threadIdx.x == 0) {
@@ -818,8 +816,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                     for (int g = 0; g < D / 64; ++g)
                         mma_ts_x4<true>(d_tmem, *reinterpret_cast<const uint32_t(*)[4]>(av + 4 * g),
                                         *reinterpret_cast<const uint64_t(*)[4]>(bv + 4 * g), idS, g > 0 ? 1u : 0u);
-                    mma_commit_pair(bar(PB_K_EMPTY + st));
-                    mma_commit_pair(bar0_peer + 8u * (uint32_t)(PB_K_EMPTY + st));
+                    mma_commit_both(bar(PB_K_EMPTY + st));
                     if (jj < 50) TRACE(200 + jj);
                 };
                 auto issue_pv = [&](int jj) {
@@ -837,8 +834,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
                         bv[kk] = bd0 + ((uint32_t)kk * 2u * C::V_SBO >> 4);
                     }
                     mma_ts_x4<true>(tmem + C::O_COL, av, bv, idO, jj > 0 ? 1u : 0u);
-                    mma_commit_pair(bar(PB_V_EMPTY + st));
-                    mma_commit_pair(bar0_peer + 8u * (uint32_t)(PB_V_EMPTY + st));
+                    mma_commit_both(bar(PB_V_EMPTY + st));
                     if (jj < 50) TRACE(250 + jj);
                     return true;
                 };

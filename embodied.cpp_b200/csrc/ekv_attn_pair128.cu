@@ -767,9 +767,7 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
         TRACE(0);
     }
     const P2Plan pl = make_p2_plan(a);
-    const uint32_t peer = (uint32_t)(pl.rank ^ 1);
     const uint32_t bar0_r0 = mapa_shared(bar0, 0);  // rank 0's barrier block (cluster window)
-    const uint32_t bar0_peer = mapa_shared(bar0, peer);
     if (threadIdx.x == 0 && !pl.sk.ok) report_error(a.pool.status, DEV_ERR_BAD_SEQ, pl.b, a.seq_ids[pl.b], 3);
 
     if (threadIdx.x == 0) {
@@ -843,8 +841,7 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
                     }
                     mma_ss_x4<true>(d_tmem, av, bv, idS, g > 0 ? 1u : 0u);
                 }
-                mma_commit_pair(bar(P2_SFULL + st));
-                mma_commit_pair(bar0_peer + 8u * (uint32_t)(P2_SFULL + st));
+                mma_commit_both(bar(P2_SFULL + st));
                 if (jj < 64) TRACE(300 + jj);
             };
             auto issue_pv = [&](int jj) {
@@ -868,8 +865,7 @@ __global__ void __launch_bounds__(P2Cfg<Q8>::THREADS, 1)
                     }
                     mma_ts_x4<true>(tmem + C::O_COL, av, bv, idO, (jj > 0 || g > 0) ? 1u : 0u);
                 }
-                mma_commit_pair(bar(P2_PVDONE + st));
-                mma_commit_pair(bar0_peer + 8u * (uint32_t)(P2_PVDONE + st));
+                mma_commit_both(bar(P2_PVDONE + st));
                 return true;
             };
             bool ok = true;

@@ -458,6 +458,16 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
                  : "memory");
 }
 
+// One commit that arrives on the mbarrier at the same shared-memory offset in both CTAs of the pair
+// (`bar` is this CTA's address of it). A commit costs the tensor pipe about as much as a short MMA,
+// so the pair signals both CTAs with one instead of two.
+__device__ __forceinline__ void mma_commit_both(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
