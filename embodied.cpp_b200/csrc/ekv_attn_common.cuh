@@ -137,6 +137,7 @@ __device__ __forceinline__ uint32_t vis_word(const MaskDesc &m, bool suffix, int
         return (m.flags & kFlexFlags) ? flex_word(m, t, n_prefix + w0, sbits) : sbits;
     }
     uint32_t bits = range_bits(0, prefix_valid, w0);
+    if (m.flags & kMaskBits) bits &= w0 >= 0 ? mask_bits_word(m, t, w0) : 0u;
     if (m.flags & EKV_MASK_SPAN_ONLY) bits &= range_bits(span_b, span_e, w0);
     if (m.flags & EKV_MASK_SPAN_EXCLUDE) bits &= ~range_bits(span_b, span_e, w0);
     if (m.flags & EKV_MASK_BLOCK_CAUSAL) {

@@ -494,8 +494,8 @@ __device__ __forceinline__ void pair_softmax(const AttnArgs &a, const PairPlan &
     const bool row_ok = r < pl.rows_valid;
     const int t = (pl.qrow0 + r) / a.group;
     const MaskDesc m = mask_desc(a, pl.b);
-    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kFlexFlags));
-    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kFlexFlags));
+    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kVisWordFlags));
+    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kVisWordFlags));
     float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][2 half][128 rows]
     float *xl = xmax + 4 * kBM;                   // [2 half][128 rows]
     const uint32_t xbar = bar(PB_XCH + quarter);

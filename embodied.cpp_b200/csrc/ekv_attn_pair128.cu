@@ -545,8 +545,8 @@ __device__ __forceinline__ void p2_softmax(const AttnArgs &a, const P2Plan &pl, 
     const bool row_ok = r < pl.rows_valid;
     const int t = (pl.qrow0 + r) / a.group;
     const MaskDesc m = mask_desc(a, pl.b);
-    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kFlexFlags));
-    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kFlexFlags));
+    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kVisWordFlags));
+    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kVisWordFlags));
     float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][SMH][128 rows]
     float *xl = xmax + 2 * SMH * kBM;             // [SMH][128 rows]
     const uint32_t xbar = bar(P2_XCH + quarter);

@@ -552,8 +552,8 @@ __device__ __forceinline__ void softmax_split_role(const AttnArgs &a, const Plan
     const int t = PACK ? (r - s_row * rpu) / a.group : (pl.qrow0 + r) / a.group;
     int s_tile = 0, first_tile = 0;  // unit of the current tile, and that unit's first CTA tile
     const MaskDesc m = mask_desc(a, pl.b);  // packed units never carry FLEX masks (the launcher checks)
-    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kFlexFlags));
-    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kFlexFlags));
+    const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kVisWordFlags));
+    const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kVisWordFlags));
     float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][H][128 rows]
     float *xl = xmax + 2 * H * kBM;               // [H][128 rows]
     const uint32_t xbar = bar(BAR_XCH + quarter);
@@ -1106,8 +1106,8 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
         const int qr = pl.qrow0 + r;
         const int t = qr / a.group;
         const MaskDesc m = mask_desc(a, pl.b);
-        const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kFlexFlags));
-        const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kFlexFlags));
+        const bool prefix_simple = !(a.mask_flags & (EKV_MASK_SPAN_ONLY | EKV_MASK_SPAN_EXCLUDE | EKV_MASK_BLOCK_CAUSAL | kVisWordFlags));
+        const bool suffix_simple = !(a.mask_flags & (EKV_MASK_SUFFIX_CAUSAL | EKV_MASK_SUFFIX_PREFIX_LM | kVisWordFlags));
         float m_used = -INFINITY, l = 0.0f;
         const float inv_scale_log2 = 1.0f / a.scale_log2;
         bool ok = true;
@@ -1431,7 +1431,7 @@ int launch_impl(AttnArgs a, cudaStream_t s, size_t ws_bytes) {
         // (and its set-up) per unit. Only when the units outnumber the SMs; no key splits.
         const int rpu = a.q_tokens * a.group;
         const int64_t n_units = (int64_t)a.n_batch * a.pool.kv_heads;
-        if (2 * rpu <= kBM && n_units > sm_count() && !(a.mask_flags & kFlexFlags)) {
+        if (2 * rpu <= kBM && n_units > sm_count() && !(a.mask_flags & kVisWordFlags)) {
             a.pack = std::min(kMaxPack, kBM / rpu);
             a.n_splits = 1;
             const int64_t ctas = (n_units + a.pack - 1) / a.pack;

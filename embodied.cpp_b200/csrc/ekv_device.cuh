@@ -41,9 +41,17 @@ struct MaskDesc {
     int32_t flags, chunk_tokens, chunk_stride, window_chunks, q_chunk0;
     const int32_t *flex;  // this batch element's metadata words (flex_meta + b * flex_stride), or null
     int32_t flex_q0, flex_k0, flex_window;
+    const uint32_t *bits;  // kMaskBits: this batch element's visibility rows, or null
+    int32_t bits_words;    // 32-bit words per query row
 };
 
 constexpr int32_t kFlexFlags = EKV_MASK_FLEX_SELF | EKV_MASK_FLEX_CROSS;
+// Internal (not settable through ekv_attn_params): prefix-key visibility from an explicit bitmask,
+// bit k % 32 of word [t][k / 32] of the batch element's rows -- a ggml 0 / -inf mask tensor
+// converted by the ggml op surface.
+constexpr int32_t kMaskBits = 1 << 30;
+// Flags under which a tile's visibility is taken per row from vis_word.
+constexpr int32_t kVisWordFlags = kFlexFlags | kMaskBits;
 
 // A pair of metadata words (EKV_FLEX_META) under the FLEX flags of `flags`.
 __host__ __device__ __forceinline__ bool flex_allowed(int32_t flags, uint32_t qm, uint32_t km, int32_t window) {
@@ -73,7 +81,21 @@ __device__ __forceinline__ MaskDesc mask_desc(const AttnArgs &a, int b) {
     m.flex_q0 = a.flex_q0;
     m.flex_k0 = a.flex_k0;
     m.flex_window = a.flex_window;
+    m.bits = (a.mask_flags & kMaskBits)
+                 ? a.mask_bits + (int64_t)(b % a.mask_bits_nb) * a.q_tokens * a.mask_bits_words
+                 : nullptr;
+    m.bits_words = a.mask_bits_words;
     return m;
+}
+
+// Visibility bits of keys [w0, w0 + 32) for query token t under kMaskBits (w0 >= 0).
+__device__ __forceinline__ uint32_t mask_bits_word(const MaskDesc &m, int t, int w0) {
+    const uint32_t *row = m.bits + (int64_t)t * m.bits_words;
+    const int wi = w0 >> 5, sh = w0 & 31;
+    const uint32_t lo = wi < m.bits_words ? __ldg(row + wi) : 0u;
+    if (sh == 0) return lo;
+    const uint32_t hi = wi + 1 < m.bits_words ? __ldg(row + wi + 1) : 0u;
+    return (lo >> sh) | (hi << (32 - sh));
 }
 
 __device__ __forceinline__ bool flex_key_allowed(const MaskDesc &m, int q, int key_index) {

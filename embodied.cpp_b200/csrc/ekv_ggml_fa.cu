@@ -13,18 +13,21 @@
 // mul_mat, soft_max_ext, mul_mat over permuted copies); ekv_mul_mat_soft_max_mul_mat takes that triple's
 // operands and result in their own layouts.
 //
-// One warp per query row: the row's q is staged in shared memory as f32, each lane scores one
-// key of a 32-key chunk (reading its K row), the chunk's running max / sum update is a warp
-// reduction, and each lane accumulates Dv/32 output columns over the chunk's V rows. This is the
-// compatibility shim for arbitrary strided tensors; the paged pool and ekv_attention are the
-// tensor-core path.
+// Calls whose shape the tcgen05 kernels take (head_dim 64 / 128 / 256, no softcap, no ALiBi, a mask
+// shared by the heads) are staged and run there (ekv_ggml_tc.cu). The rest run here, one warp per
+// query row: the row's q is staged in shared memory as f32, each lane scores one key of a 32-key
+// chunk (reading its K row), the chunk's running max / sum update is a warp reduction, and each lane
+// accumulates Dv/32 output columns over the chunk's V rows. The same kernel, gated by a device flag,
+// redoes a tensor-core call whose mask turned out to carry additive values.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 
 #include "../../include/ekv.h"
 #include "ekv_device.cuh"
+#include "ekv_ggml.h"
 #include "ekv_internal.h"
 
 namespace ekv {
@@ -66,12 +69,17 @@ __device__ __forceinline__ float warp_sum(float x) {
     return x;
 }
 
-__global__ void __launch_bounds__(kFaWarps * 32) flash_attn_ext_kernel(const FaArgs a) {
+// Grid-stride over (8-query group, head, batch) tiles; with `only_if`, nothing is done unless *only_if.
+__global__ void __launch_bounds__(kFaWarps * 32) flash_attn_ext_kernel(const FaArgs a, const int32_t *only_if) {
     __shared__ float sq[kFaWarps][kFaMaxD];
+    if (only_if && *(volatile const int32_t *)only_if == 0) return;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int64_t iq1 = (int64_t)blockIdx.x * kFaWarps + warp;  // query
-    const int iq2 = blockIdx.y, iq3 = blockIdx.z;                // head, batch
-    if (iq1 >= a.q.ne[1]) return;
+    const int64_t nx = (a.q.ne[1] + kFaWarps - 1) / kFaWarps, n_tiles = nx * a.q.ne[2] * a.q.ne[3];
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const int64_t iq1 = (tile % nx) * kFaWarps + warp;  // query
+    const int iq2 = (int)((tile / nx) % a.q.ne[2]), iq3 = (int)(tile / (nx * a.q.ne[2]));  // head, batch
+    __syncwarp();
+    if (iq1 >= a.q.ne[1]) continue;
     const int D = (int)a.q.ne[0], Dv = (int)a.v.ne[0];
     const int64_t Tk = a.k.ne[1];
     const int64_t ik2 = iq2 / (a.q.ne[2] / a.k.ne[2]), ik3 = iq3 / (a.q.ne[3] / a.k.ne[3]);
@@ -134,6 +142,7 @@ __global__ void __launch_bounds__(kFaWarps * 32) flash_attn_ext_kernel(const FaA
         const int d = lane + 32 * i;
         if (d < Dv) *(float *)(orow + d * a.dnb[0]) = acc[i] * inv;
     }
+    }
 }
 
 int elem_size(int32_t type) {
@@ -170,8 +179,9 @@ namespace ekv {
 namespace {
 
 // The op on validated-type tensors in flash_attn_ext order: v {Dv, Tk, Hkv, Bk}, dst {Dv, Hq, Tq, B}.
-int run_flash_attn(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask, float scale,
-                   float max_bias, float logit_softcap, const ekv_tensor *dst, cudaStream_t stream) {
+// Validation shared by the op's entry points (ggml's shape rules); EKV_OK for a valid call.
+int check_flash_attn(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask, float scale,
+                     float max_bias, float logit_softcap, const ekv_tensor *dst) {
     if (!tensor_ok(q, false) || !tensor_ok(k, false) || !tensor_ok(v, false) || !tensor_ok(dst, true))
         return EKV_ERR_INVALID_ARG;
     if (mask && (!tensor_ok(mask, false) || mask->type == EKV_DTYPE_BF16)) return EKV_ERR_INVALID_ARG;
@@ -189,6 +199,31 @@ int run_flash_attn(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v
     if (q->ne[0] > kFaMaxD || v->ne[0] > kFaMaxDv) return EKV_ERR_UNSUPPORTED;
     if ((q->ne[1] + kFaWarps - 1) / kFaWarps > 0x7fffffff || q->ne[2] > 65535 || q->ne[3] > 65535)
         return EKV_ERR_UNSUPPORTED;
+    return EKV_OK;
+}
+
+// The op on validated tensors in flash_attn_ext order: v {Dv, Tk, Hkv, Bk}, dst {Dv, Hq, Tq, B}.
+// `ws` / `ws_bytes`: the caller's workspace for the tensor-core route, or (ws == null, use_cache)
+// the library's per-device one; without either the call runs on the CUDA cores.
+int run_flash_attn(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask, float scale,
+                   float max_bias, float logit_softcap, const ekv_tensor *dst, void *ws, size_t ws_bytes,
+                   bool use_cache, cudaStream_t stream) {
+    if (const int rc = check_flash_attn(q, k, v, mask, scale, max_bias, logit_softcap, dst)) return rc;
+    const int32_t *redo = nullptr;
+    const size_t need = ggml_tc_workspace(q, k, v, mask, max_bias, logit_softcap, dst);
+    if (need) {
+        if (!ws && use_cache) {
+            ws = ggml_tc_cached_workspace(need);
+            ws_bytes = ws ? need : 0;
+        }
+        if (ws) {
+            const int rc = ggml_tc_run(q, k, v, mask, scale, max_bias, logit_softcap, dst, ws, ws_bytes, stream, &redo);
+            if (rc) return rc;
+            if (!redo) return EKV_OK;
+        } else if (!use_cache) {
+            return EKV_ERR_RANGE;  // the tensor-core route needs the workspace the caller was told
+        }
+    }
 
     FaArgs a;
     a.q = fa_view(q);
@@ -207,8 +242,14 @@ int run_flash_attn(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v
     a.m1 = std::pow(2.0f, -(max_bias / 2.0f) / (float)a.n_head_log2);
     a.dst = (uint8_t *)dst->data;
     for (int i = 0; i < 4; ++i) a.dnb[i] = dst->nb[i];
-    const dim3 grid((unsigned)((q->ne[1] + kFaWarps - 1) / kFaWarps), (unsigned)q->ne[2], (unsigned)q->ne[3]);
-    flash_attn_ext_kernel<<<grid, kFaWarps * 32, 0, stream>>>(a);
+    // grid-stride: the full grid, or one wave where the launch only redoes a call whose mask held
+    // additive values (and exits at once when it did not)
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t n_tiles = ((q->ne[1] + kFaWarps - 1) / kFaWarps) * q->ne[2] * q->ne[3];
+    const int64_t cap = redo ? (int64_t)sms * 8 : (int64_t)1 << 30;
+    flash_attn_ext_kernel<<<(unsigned)std::min(n_tiles, cap), kFaWarps * 32, 0, stream>>>(a, redo);
     if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
     note_launches(1);
     return EKV_OK;
@@ -230,22 +271,68 @@ ekv_tensor swap_dims(const ekv_tensor &t, int i, int j) {
 extern "C" int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask,
                                   float scale, float max_bias, float logit_softcap, const ekv_tensor *dst,
                                   ekv_stream_t stream) {
-    return ekv::run_flash_attn(q, k, v, mask, scale, max_bias, logit_softcap, dst, (cudaStream_t)stream);
+    return ekv::run_flash_attn(q, k, v, mask, scale, max_bias, logit_softcap, dst, nullptr, 0, true,
+                               (cudaStream_t)stream);
+}
+
+extern "C" size_t ekv_flash_attn_ext_workspace_size(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v,
+                                                    const ekv_tensor *mask, float max_bias, float logit_softcap,
+                                                    const ekv_tensor *dst) {
+    if (ekv::check_flash_attn(q, k, v, mask, 1.0f, max_bias, logit_softcap, dst)) return 0;
+    return ekv::ggml_tc_workspace(q, k, v, mask, max_bias, logit_softcap, dst);
+}
+
+extern "C" int ekv_flash_attn_ext_ws(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v,
+                                     const ekv_tensor *mask, float scale, float max_bias, float logit_softcap,
+                                     const ekv_tensor *dst, void *workspace, size_t workspace_bytes,
+                                     ekv_stream_t stream) {
+    return ekv::run_flash_attn(q, k, v, mask, scale, max_bias, logit_softcap, dst, workspace, workspace_bytes, false,
+                               (cudaStream_t)stream);
 }
 
 // mul_mat(K, Q) -> soft_max_ext(kq, mask, scale, max_bias) -> mul_mat(V, attn) of models/pi05.cpp:414-418:
 // the same computation as the fused op with V given keys-fastest ({Tk, Dv, ...}, the permute(1, 2, 0, 3)
 // of :412) and the result in mul_mat order {Dv, Tq, Hq, B} (before the permute of :419-420). Both are
 // views of the caller's bytes with two dimensions exchanged.
+namespace ekv {
+namespace {
+// The triple's V and result as flash_attn_ext-ordered views, or false for mismatched shapes.
+bool triple_views(const ekv_tensor *k, const ekv_tensor *q, const ekv_tensor *v, const ekv_tensor *dst, ekv_tensor &vt,
+                  ekv_tensor &dt) {
+    if (!k || !q || !v || !dst) return false;
+    // mul_mat(V, attn) contracts V's ne[0] with attn's ne[0] = keys; V's heads and batch are K's
+    if (v->ne[0] != k->ne[1] || v->ne[2] != k->ne[2] || v->ne[3] != k->ne[3]) return false;
+    if (dst->ne[0] != v->ne[1] || dst->ne[1] != q->ne[1] || dst->ne[2] != q->ne[2] || dst->ne[3] != q->ne[3])
+        return false;
+    vt = swap_dims(*v, 0, 1);
+    dt = swap_dims(*dst, 1, 2);
+    return true;
+}
+}  // namespace
+}  // namespace ekv
+
 extern "C" int ekv_mul_mat_soft_max_mul_mat(const ekv_tensor *k, const ekv_tensor *q, const ekv_tensor *v,
                                             const ekv_tensor *mask, float scale, float max_bias, const ekv_tensor *dst,
                                             ekv_stream_t stream) {
-    using namespace ekv;
-    if (!k || !q || !v || !dst) return EKV_ERR_INVALID_ARG;
-    // mul_mat(V, attn) contracts V's ne[0] with attn's ne[0] = keys; V's heads and batch are K's
-    if (v->ne[0] != k->ne[1] || v->ne[2] != k->ne[2] || v->ne[3] != k->ne[3]) return EKV_ERR_INVALID_ARG;
-    if (dst->ne[0] != v->ne[1] || dst->ne[1] != q->ne[1] || dst->ne[2] != q->ne[2] || dst->ne[3] != q->ne[3])
-        return EKV_ERR_INVALID_ARG;
-    const ekv_tensor vt = swap_dims(*v, 0, 1), dt = swap_dims(*dst, 1, 2);
-    return run_flash_attn(q, k, &vt, mask, scale, max_bias, 0.0f, &dt, (cudaStream_t)stream);
+    ekv_tensor vt, dt;
+    if (!ekv::triple_views(k, q, v, dst, vt, dt)) return EKV_ERR_INVALID_ARG;
+    return ekv::run_flash_attn(q, k, &vt, mask, scale, max_bias, 0.0f, &dt, nullptr, 0, true, (cudaStream_t)stream);
+}
+
+extern "C" size_t ekv_mul_mat_soft_max_mul_mat_workspace_size(const ekv_tensor *k, const ekv_tensor *q,
+                                                              const ekv_tensor *v, const ekv_tensor *mask,
+                                                              float max_bias, const ekv_tensor *dst) {
+    ekv_tensor vt, dt;
+    if (!ekv::triple_views(k, q, v, dst, vt, dt)) return 0;
+    return ekv_flash_attn_ext_workspace_size(q, k, &vt, mask, max_bias, 0.0f, &dt);
+}
+
+extern "C" int ekv_mul_mat_soft_max_mul_mat_ws(const ekv_tensor *k, const ekv_tensor *q, const ekv_tensor *v,
+                                               const ekv_tensor *mask, float scale, float max_bias,
+                                               const ekv_tensor *dst, void *workspace, size_t workspace_bytes,
+                                               ekv_stream_t stream) {
+    ekv_tensor vt, dt;
+    if (!ekv::triple_views(k, q, v, dst, vt, dt)) return EKV_ERR_INVALID_ARG;
+    return ekv::run_flash_attn(q, k, &vt, mask, scale, max_bias, 0.0f, &dt, workspace, workspace_bytes, false,
+                               (cudaStream_t)stream);
 }

@@ -59,6 +59,10 @@ struct AttnArgs {
     // ekv_debug_expire_wait (1: the MMA-issuing thread waits on a barrier nothing arrives on)
     long long wait_budget;
     int32_t debug_stall;
+    // kMaskBits (the ggml op surface): visibility rows [mask_bits_nb][q_tokens][mask_bits_words],
+    // batch element b reading rows b % mask_bits_nb
+    const uint32_t *mask_bits;
+    int32_t mask_bits_words, mask_bits_nb;
 };
 
 constexpr long long kDefaultWaitBudget = 4000000000LL;  // clock cycles, about 2 s

@@ -94,7 +94,8 @@ EXPORTED = [
     "ekv_seq_get", "ekv_append", "ekv_append_suffix", "ekv_gather", "ekv_gather_suffix",
     "ekv_attention_workspace_size", "ekv_attention", "ekv_attention_algo", "ekv_version",
     "ekv_strerror", "ekv_attention_noalloc", "ekv_flash_attn_ext",
-    "ekv_mul_mat_soft_max_mul_mat", "ekv_append_suffix_attention", "ekv_launch_count", "ekv_debug_expire_wait",
+    "ekv_mul_mat_soft_max_mul_mat", "ekv_flash_attn_ext_workspace_size", "ekv_flash_attn_ext_ws",
+    "ekv_mul_mat_soft_max_mul_mat_workspace_size", "ekv_mul_mat_soft_max_mul_mat_ws", "ekv_append_suffix_attention", "ekv_launch_count", "ekv_debug_expire_wait",
     "ekv_flow_step_f32", "ekv_guidance_f32", "ekv_sched_create", "ekv_sched_destroy", "ekv_sched_submit",
     "ekv_sched_begin_tick", "ekv_sched_end_tick", "ekv_sched_stats",
 ]
@@ -144,6 +145,14 @@ def _load():
         "ekv_flash_attn_ext": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 3 + [C.POINTER(Tensor), vp], C.c_int),
         "ekv_mul_mat_soft_max_mul_mat": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 2 + [C.POINTER(Tensor), vp],
                                          C.c_int),
+        "ekv_flash_attn_ext_workspace_size": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 2 + [C.POINTER(Tensor)],
+                                              C.c_size_t),
+        "ekv_flash_attn_ext_ws": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 3 + [C.POINTER(Tensor), vp, C.c_size_t, vp],
+                                  C.c_int),
+        "ekv_mul_mat_soft_max_mul_mat_workspace_size": ([C.POINTER(Tensor)] * 4 + [C.c_float, C.POINTER(Tensor)],
+                                                        C.c_size_t),
+        "ekv_mul_mat_soft_max_mul_mat_ws": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 2 + [C.POINTER(Tensor), vp,
+                                                                                         C.c_size_t, vp], C.c_int),
         "ekv_version": ([], C.c_char_p),
         "ekv_launch_count": ([], C.c_uint64),
         "ekv_strerror": ([C.c_int], C.c_char_p),
@@ -431,24 +440,48 @@ def ggml_view(t) -> Tensor:
     return g
 
 
-def flash_attn_ext(q, k, v, mask, dst, *, scale, max_bias=0.0, logit_softcap=0.0, stream=None):
+def flash_attn_ext(q, k, v, mask, dst, *, scale, max_bias=0.0, logit_softcap=0.0, workspace=None, stream=None):
     """ggml_flash_attn_ext on torch tensors given in reversed ggml order: q [B, Hq, Tq, D],
     k [Bk, Hkv, Tk, D], v [Bk, Hkv, Tk, Dv], mask [Mb, Mh, >=Tq, >=Tk] (or None) and the f32
-    result dst [B, Tq, Hq, Dv]; any of them may be a permuted or sliced view."""
+    result dst [B, Tq, Hq, Dv]; any of them may be a permuted or sliced view. With `workspace` (a
+    uint8 device tensor of flash_attn_ext_workspace_size bytes) the call stages into it
+    (ekv_flash_attn_ext_ws), else into the library's per-device workspace."""
     gm = None if mask is None else C.byref(ggml_view(mask))
-    check(lib.ekv_flash_attn_ext(C.byref(ggml_view(q)), C.byref(ggml_view(k)), C.byref(ggml_view(v)), gm,
-                                 scale, max_bias, logit_softcap, C.byref(ggml_view(dst)), _stream(stream)),
-          "ekv_flash_attn_ext")
+    args = (C.byref(ggml_view(q)), C.byref(ggml_view(k)), C.byref(ggml_view(v)), gm, scale, max_bias, logit_softcap,
+            C.byref(ggml_view(dst)))
+    if workspace is None:
+        check(lib.ekv_flash_attn_ext(*args, _stream(stream)), "ekv_flash_attn_ext")
+    else:
+        check(lib.ekv_flash_attn_ext_ws(*args, _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                        _stream(stream)), "ekv_flash_attn_ext_ws")
 
 
-def mul_mat_soft_max_mul_mat(k, q, v, mask, dst, *, scale, max_bias=0.0, stream=None):
+def flash_attn_ext_workspace_size(q, k, v, mask, dst, *, max_bias=0.0, logit_softcap=0.0) -> int:
+    """Bytes of the tensor-core staging of this flash_attn_ext call (0: it runs on the CUDA cores)."""
+    gm = None if mask is None else C.byref(ggml_view(mask))
+    return lib.ekv_flash_attn_ext_workspace_size(C.byref(ggml_view(q)), C.byref(ggml_view(k)), C.byref(ggml_view(v)),
+                                                 gm, max_bias, logit_softcap, C.byref(ggml_view(dst)))
+
+
+def mul_mat_soft_max_mul_mat(k, q, v, mask, dst, *, scale, max_bias=0.0, workspace=None, stream=None):
     """The ggml triple mul_mat(K, Q) -> soft_max_ext -> mul_mat(V, .) on torch tensors in reversed ggml
     order: k [Bk, Hkv, Tk, D], q [B, Hq, Tq, D], v [Bk, Hkv, Dv, Tk] (keys fastest), mask
-    [Mb, Mh, >=Tq, >=Tk] or None, f32 dst [B, Hq, Tq, Dv]."""
+    [Mb, Mh, >=Tq, >=Tk] or None, f32 dst [B, Hq, Tq, Dv]. `workspace` as for flash_attn_ext."""
     gm = None if mask is None else C.byref(ggml_view(mask))
-    check(lib.ekv_mul_mat_soft_max_mul_mat(C.byref(ggml_view(k)), C.byref(ggml_view(q)), C.byref(ggml_view(v)), gm,
-                                           scale, max_bias, C.byref(ggml_view(dst)), _stream(stream)),
-          "ekv_mul_mat_soft_max_mul_mat")
+    args = (C.byref(ggml_view(k)), C.byref(ggml_view(q)), C.byref(ggml_view(v)), gm, scale, max_bias,
+            C.byref(ggml_view(dst)))
+    if workspace is None:
+        check(lib.ekv_mul_mat_soft_max_mul_mat(*args, _stream(stream)), "ekv_mul_mat_soft_max_mul_mat")
+    else:
+        check(lib.ekv_mul_mat_soft_max_mul_mat_ws(*args, _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                                  _stream(stream)), "ekv_mul_mat_soft_max_mul_mat_ws")
+
+
+def mul_mat_soft_max_mul_mat_workspace_size(k, q, v, mask, dst, *, max_bias=0.0) -> int:
+    gm = None if mask is None else C.byref(ggml_view(mask))
+    return lib.ekv_mul_mat_soft_max_mul_mat_workspace_size(C.byref(ggml_view(k)), C.byref(ggml_view(q)),
+                                                           C.byref(ggml_view(v)), gm, max_bias,
+                                                           C.byref(ggml_view(dst)))
 
 
 def version() -> str:

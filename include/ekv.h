@@ -285,7 +285,15 @@ int ekv_append_suffix_attention(ekv_pool *pool, const ekv_attn_params *p, const 
  * score = scale * q.k, or logit_softcap * tanh(scale * q.k / logit_softcap) when logit_softcap != 0;
  * then + slope(h) * mask (slope = 1 when max_bias == 0, else the ALiBi slope of head h; needs a
  * mask); softmax over keys in f32; rows whose every score is -inf give 0. D <= 512, Dv <= 256.
- * This is the op-surface shim: the paged pool and ekv_attention are the tensor-core hot path. */
+ * Tensor cores: calls with D == Dv in {64, 128, 256}, logit_softcap == 0, max_bias == 0 and a mask
+ * shared by the heads (Mh == 1) are staged into a workspace -- K/V as a one-layer bf16 pool in
+ * 64-token blocks, Q as bf16 rows, the mask as visibility bits -- and run by the kernels of
+ * ekv_attention (bf16 operands, f32 accumulation; tolerance as ekv_attention's bf16 path). A mask
+ * whose visible entries are not all 0 is detected on the device while it is converted, and the call
+ * is then redone exactly on the CUDA cores. Other calls run one warp per query row on the CUDA cores
+ * (f32). ekv_flash_attn_ext stages into a workspace the library holds per device (grown on demand,
+ * which waits for the device: make the first call of a shape outside graph capture; calls sharing it
+ * must be stream-ordered); ekv_flash_attn_ext_ws takes the caller's. */
 typedef struct ekv_tensor {
     void *data;     /* device pointer */
     int32_t type;   /* EKV_DTYPE_F32, EKV_DTYPE_F16 or EKV_DTYPE_BF16 */
@@ -295,6 +303,16 @@ typedef struct ekv_tensor {
 int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask,
                        float scale, float max_bias, float logit_softcap, const ekv_tensor *dst,
                        ekv_stream_t stream);
+/* Workspace bytes the tensor-core route of this call needs (16-byte aligned), or 0 where the call
+ * runs on the CUDA cores (or is invalid). */
+size_t ekv_flash_attn_ext_workspace_size(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v,
+                                         const ekv_tensor *mask, float max_bias, float logit_softcap,
+                                         const ekv_tensor *dst);
+/* ekv_flash_attn_ext with the caller's workspace (graph-capturable): EKV_ERR_RANGE when the size
+ * reported above is non-zero and workspace_bytes is below it. */
+int ekv_flash_attn_ext_ws(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, const ekv_tensor *mask,
+                          float scale, float max_bias, float logit_softcap, const ekv_tensor *dst, void *workspace,
+                          size_t workspace_bytes, ekv_stream_t stream);
 
 /* The ggml triple of models/pi05.cpp:414-418 (also models/smolvla.cpp and models/hy_vla.cpp expert
  * layers): kq = mul_mat(K, Q) at F32 precision, attn = soft_max_ext(kq, mask, scale, max_bias),
@@ -308,6 +326,12 @@ int ekv_flash_attn_ext(const ekv_tensor *q, const ekv_tensor *k, const ekv_tenso
 int ekv_mul_mat_soft_max_mul_mat(const ekv_tensor *k, const ekv_tensor *q, const ekv_tensor *v,
                                  const ekv_tensor *mask, float scale, float max_bias, const ekv_tensor *dst,
                                  ekv_stream_t stream);
+/* Workspace size and explicit-workspace form of the triple, as for ekv_flash_attn_ext. */
+size_t ekv_mul_mat_soft_max_mul_mat_workspace_size(const ekv_tensor *k, const ekv_tensor *q, const ekv_tensor *v,
+                                                   const ekv_tensor *mask, float max_bias, const ekv_tensor *dst);
+int ekv_mul_mat_soft_max_mul_mat_ws(const ekv_tensor *k, const ekv_tensor *q, const ekv_tensor *v,
+                                    const ekv_tensor *mask, float scale, float max_bias, const ekv_tensor *dst,
+                                    void *workspace, size_t workspace_bytes, ekv_stream_t stream);
 
 /* ---- batching scheduler over the pool ----
  * The reference serves one vla.PredictRequest at a time (serving/vla-server.cpp:240-523). The scheduler

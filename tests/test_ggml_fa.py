@@ -5,8 +5,10 @@ attention oracle; the C-ABI rejects malformed tensors before any CUDA call (no k
 GPU: parity with the oracle on the reference's call shapes (models/hy_vla.cpp:376-378 permuted
 self-attention, :439-441 time attention under hy_mem_causal_mask, :859 GQA with a mask;
 models/lingbot_va.cpp:1263-1266), plus softcap, ALiBi, f16/bf16 inputs, batch broadcast, the
-largest head dims, fully masked rows and strided outputs. Tolerance: max-abs 2e-4 (f32 arithmetic
-against float64; inputs are rounded to their storage type before the oracle sees them).
+largest head dims, fully masked rows and strided outputs. Calls the tcgen05 kernels take (head_dim
+64/128/256, no softcap or ALiBi, a head-shared mask) run there on bf16 operands: max-abs 2e-2, the
+bf16 tolerance of the attention path; the rest run on the CUDA cores in f32: max-abs 2e-4 against
+float64 (inputs are rounded to their storage type before the oracle sees them).
 """
 import ctypes as C
 import os
@@ -18,7 +20,8 @@ import ekv
 import oracle
 
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-TOL = 2e-4
+TOL = 2e-4     # CUDA-core route, f32
+TOL_TC = 2e-2  # tensor-core route, bf16 operands, f32 accumulation
 
 
 # ---------------------------------------------------------------- oracle pins (CPU)
@@ -125,17 +128,31 @@ def _np(t):
     return t.detach().float().cpu().numpy().astype(np.float64)
 
 
+TOL_OF = {}
+
+
 def run(q, k, v, mask, *, scale, max_bias=0.0, softcap=0.0, dst=None):
+    """One call; also records in TOL_OF[id(dst)] the tolerance of the route it took (the tensor-core
+    route launches the staging kernels and the attention, the CUDA-core route one kernel)."""
     import torch
     B, Hq, Tq, _ = q.shape
     Dv = v.shape[3]
     if dst is None:
         dst = torch.full((B, Tq, Hq, Dv), float("nan"), dtype=torch.float32, device="cuda")
+    tc = ekv.flash_attn_ext_workspace_size(q, k, v, mask, dst, max_bias=max_bias, logit_softcap=softcap) > 0
+    n0 = ekv.lib.ekv_launch_count()
     ekv.flash_attn_ext(q, k, v, mask, dst, scale=scale, max_bias=max_bias, logit_softcap=softcap)
     torch.cuda.synchronize()
+    launched = ekv.lib.ekv_launch_count() - n0
+    assert (launched >= 4) == tc, (launched, tc)
     want = oracle.flash_attn_ext(_np(q), _np(k), _np(v), None if mask is None else _np(mask),
                                  scale=scale, max_bias=max_bias, logit_softcap=softcap)
+    TOL_OF[id(dst)] = TOL_TC if tc else TOL
     return dst, want
+
+
+def tol(dst):
+    return TOL_OF[id(dst)]
 
 
 def causal_f16(n, device):
@@ -154,7 +171,7 @@ def test_hy_self_attention_permuted_views():
     qkv = torch.randn(seq, 3 * H * D, device="cuda")
     views = [qkv[:, i * H * D:(i + 1) * H * D].view(seq, H, D).permute(1, 0, 2)[None] for i in range(3)]
     dst, want = run(*views, None, scale=D ** -0.5)
-    assert np.abs(_np(dst) - want).max() < TOL
+    assert np.abs(_np(dst) - want).max() < tol(dst)
 
 
 @pytest.mark.gpu
@@ -169,7 +186,7 @@ def test_hy_time_attention_causal_mask(frames):
     Q, K, V = (t.permute(1, 2, 0, 3) for t in (q4, k4, v4))  # [P, H, T, D] views
     mask = causal_f16(frames, "cuda")[None, None]
     dst, want = run(Q, K, V, mask, scale=D ** -0.5)
-    assert np.abs(_np(dst) - want).max() < TOL
+    assert np.abs(_np(dst) - want).max() < tol(dst)
 
 
 @pytest.mark.gpu
@@ -188,7 +205,7 @@ def test_hy_expert_gqa_mask(hq, hkv):
     m[:, 0] = 0.0
     mask = m.to(torch.float16)[None, None]
     dst, want = run(q, k, v, mask, scale=D ** -0.5)
-    assert np.abs(_np(dst) - want).max() < TOL
+    assert np.abs(_np(dst) - want).max() < tol(dst)
 
 
 @pytest.mark.gpu
@@ -204,7 +221,7 @@ def test_half_inputs_and_f32_mask_per_head(dtype):
     mask = torch.randn(B, Hq, Tq, Tk, device="cuda")
     mask[..., 5:9] = float("-inf")
     dst, want = run(q, k, v, mask, scale=0.1)
-    assert np.abs(_np(dst) - want).max() < TOL
+    assert np.abs(_np(dst) - want).max() < tol(dst)
 
 
 @pytest.mark.gpu
@@ -217,9 +234,9 @@ def test_softcap_alibi_and_batch_broadcast():
     v = torch.randn(Bk, Hkv, Tk, D, device="cuda")
     mask = (-torch.arange(Tk, device="cuda").float().abs()).expand(1, 1, Tq, Tk).contiguous()
     dst, want = run(q, k, v, mask, scale=0.125, max_bias=8.0, softcap=20.0)
-    assert np.abs(_np(dst) - want).max() < TOL
+    assert np.abs(_np(dst) - want).max() < tol(dst)
     dst, want = run(q, k, v, None, scale=0.125, softcap=5.0)
-    assert np.abs(_np(dst) - want).max() < TOL
+    assert np.abs(_np(dst) - want).max() < tol(dst)
 
 
 @pytest.mark.gpu
@@ -231,7 +248,7 @@ def test_head_dims_and_key_counts(d, dv, tk):
     k = torch.randn(1, 2, tk, d, device="cuda") * 0.2
     v = torch.randn(1, 2, tk, dv, device="cuda")
     dst, want = run(q, k, v, None, scale=1.0)
-    assert np.abs(_np(dst) - want).max() < TOL
+    assert np.abs(_np(dst) - want).max() < tol(dst)
 
 
 @pytest.mark.gpu
@@ -250,7 +267,7 @@ def test_fully_masked_rows_and_strided_dst():
     dst, want = run(q, k, v, mask, scale=0.125, dst=dst)
     got = _np(dst)
     assert np.all(got[:, 3] == 0.0)
-    assert np.abs(got - want).max() < TOL
+    assert np.abs(got - want).max() < tol(dst)
     rest = big.clone()
     rest[:, :, 1:, 8:8 + D] = 7.0
     assert torch.all(rest == 7.0)
@@ -321,7 +338,7 @@ def test_triple_pi05_layer(contig_v, masked):
     ekv.mul_mat_soft_max_mul_mat(k, q, v, mask, dst, scale=1.0 / 16)
     torch.cuda.synchronize()
     want = oracle.flash_attn_ext(_np(q), _np(k), _np(vf)[None, None], _np(mask), scale=1.0 / 16)
-    assert np.abs(_np(dst) - want.transpose(0, 2, 1, 3)).max() < TOL
+    assert np.abs(_np(dst) - want.transpose(0, 2, 1, 3)).max() < TOL_TC
 
 
 @pytest.mark.gpu
@@ -344,4 +361,90 @@ def test_triple_fully_masked_row_gives_zero():
     got = _np(dst)
     assert np.all(got[:, :, 2] == 0.0)
     want = oracle.flash_attn_ext(_np(q), _np(k), _np(vf)[None, None], _np(mask), scale=0.125)
-    assert np.abs(got - want.transpose(0, 2, 1, 3)).max() < TOL
+    assert np.abs(got - want.transpose(0, 2, 1, 3)).max() < TOL_TC
+
+
+# ---------------------------------------------------------------- the tensor-core route
+
+def test_workspace_size_picks_the_route():
+    """Host logic only: which calls the tensor-core route takes, and that its workspace covers the
+    staged K/V (two bf16 copies in 64-token blocks), Q and the mask bits."""
+    def ws(q, k, v, m, dst, max_bias=0.0, softcap=0.0):
+        r = lambda t: None if t is None else C.byref(t)
+        return ekv.lib.ekv_flash_attn_ext_workspace_size(r(q), r(k), r(v), r(m), max_bias, softcap, r(dst))
+    q, k, v = fake([128, 50, 8, 4]), fake([128, 300, 2, 4]), fake([128, 300, 2, 4])
+    m, dst = fake([300, 50, 1, 1], ekv.DTYPE_F16), fake([128, 8, 50, 4])
+    n = ws(q, k, v, m, dst)
+    assert n >= 4 * 2 * 2 * 320 * 128 * 2 + 4 * 50 * 8 * 128 * 2
+    assert ws(q, k, v, None, dst) > 0
+    assert ws(q, k, v, m, dst, softcap=10.0) == 0                        # softcap: CUDA cores
+    assert ws(q, k, v, m, dst, max_bias=8.0) == 0                        # ALiBi: CUDA cores
+    assert ws(q, k, v, fake([300, 50, 8, 1], ekv.DTYPE_F16), dst) == 0   # per-head mask
+    assert ws(fake([96, 50, 8, 4]), fake([96, 300, 2, 4]), fake([96, 300, 2, 4]), m, fake([96, 8, 50, 4])) == 0
+    assert ws(q, k, fake([64, 300, 2, 4]), m, fake([64, 8, 50, 4])) == 0  # Dv != D
+    assert ws(q, fake([64, 300, 2, 4]), v, m, dst) == 0                  # invalid call
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("d", [64, 128, 256])
+def test_tensor_core_route_gqa_batch_broadcast_and_mask(d):
+    """GQA, K/V batch broadcast (B = 2 Bk), a binary F16 mask per batch element with padding and a
+    causal block, f16 K/V: the staged call on the tcgen05 kernels against the oracle."""
+    import torch
+    torch.manual_seed(d)
+    B, Bk, Hq, Hkv, Tq, Tk = 4, 2, 8, 2, 37, 203
+    q = torch.randn(B, Hq, Tq, d, device="cuda") * 0.5
+    k = (torch.randn(Bk, Hkv, Tk, d, device="cuda") * 0.5).to(torch.float16)
+    v = (torch.randn(Bk, Hkv, Tk, d, device="cuda") * 0.5).to(torch.float16)
+    m = torch.zeros(B, 1, Tq + 3, Tk + 13, device="cuda")
+    m[:, :, :, 150:180] = float("-inf")
+    m[1, :, :, :40] = float("-inf")
+    m[2, :, 5:9, 100:] = float("-inf")
+    dst, want = run(q, k, v, m.to(torch.float16), scale=d ** -0.5)
+    assert tol(dst) == TOL_TC
+    assert np.abs(_np(dst) - want).max() < TOL_TC
+
+
+@pytest.mark.gpu
+def test_additive_mask_is_redone_exactly():
+    """A head-shared mask with additive (finite, non-zero) entries on a tensor-core shape: the
+    conversion flags it and the CUDA-core kernel redoes the call, so the result is f32-exact."""
+    import torch
+    torch.manual_seed(77)
+    B, Hq, Hkv, Tq, Tk, D = 2, 4, 4, 21, 90, 64
+    q, k, v = (torch.randn(B, h, n, D, device="cuda") for h, n in ((Hq, Tq), (Hkv, Tk), (Hkv, Tk)))
+    mask = torch.randn(B, 1, Tq, Tk, device="cuda")
+    mask[..., 7:11] = float("-inf")
+    dst, want = run(q, k, v, mask, scale=0.125)
+    assert np.abs(_np(dst) - want).max() < TOL
+
+
+@pytest.mark.gpu
+def test_explicit_workspace_and_too_small():
+    import torch
+    torch.manual_seed(3)
+    B, H, Tq, Tk, D = 2, 8, 50, 866, 256
+    q = torch.randn(B, H, Tq, D, device="cuda") * 0.5
+    k = torch.randn(B, 1, Tk, D, device="cuda") * 0.5
+    v = torch.randn(B, 1, Tk, D, device="cuda") * 0.5
+    dst = torch.empty(B, Tq, H, D, device="cuda")
+    n = ekv.flash_attn_ext_workspace_size(q, k, v, None, dst)
+    assert n > 0
+    small = torch.empty(n - 256, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ekv.EkvError) as e:
+        ekv.flash_attn_ext(q, k, v, None, dst, scale=1 / 16, workspace=small)
+    assert e.value.code == ekv.ERR_RANGE
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    ekv.flash_attn_ext(q, k, v, None, dst, scale=1 / 16, workspace=ws)
+    torch.cuda.synchronize()
+    want = oracle.flash_attn_ext(_np(q), _np(k), _np(v), None, scale=1 / 16)
+    assert np.abs(_np(dst) - want).max() < TOL_TC
+    # the triple with its own workspace
+    vt = v.transpose(2, 3)
+    dt = torch.empty(B, H, Tq, D, device="cuda")
+    nt = ekv.mul_mat_soft_max_mul_mat_workspace_size(k, q, vt, None, dt)
+    assert nt > 0
+    ekv.mul_mat_soft_max_mul_mat(k, q, vt, None, dt, scale=1 / 16, workspace=torch.empty(nt, dtype=torch.uint8,
+                                                                                          device="cuda"))
+    torch.cuda.synchronize()
+    assert np.abs(_np(dt) - want.transpose(0, 2, 1, 3)).max() < TOL_TC
