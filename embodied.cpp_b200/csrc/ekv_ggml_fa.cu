@@ -248,7 +248,7 @@ int run_flash_attn(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t n_tiles = ((q->ne[1] + kFaWarps - 1) / kFaWarps) * q->ne[2] * q->ne[3];
-    const int64_t cap = redo ? (int64_t)sms * 8 : (int64_t)1 << 30;
+    const int64_t cap = redo ? (int64_t)sms : (int64_t)1 << 30;
     flash_attn_ext_kernel<<<(unsigned)std::min(n_tiles, cap), kFaWarps * 32, 0, stream>>>(a, redo);
     if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
     note_launches(1);

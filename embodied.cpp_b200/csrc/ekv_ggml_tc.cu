@@ -18,6 +18,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cmath>
 #include <cstdint>
 #include <mutex>
@@ -55,8 +56,30 @@ __device__ __forceinline__ float gg_load(int32_t type, const uint8_t *p) {
     return bf16_bits_to_f32(*(const uint16_t *)p);
 }
 
-// 8 consecutive elements (stride nb0) of a row -> 8 bf16 (round to nearest even)
+// 8 consecutive elements (stride nb0) of a row -> 8 bf16 (round to nearest even); one or two
+// 16-byte loads where the elements are adjacent and aligned
 __device__ __forceinline__ uint4 gg_load8_bf16(const GgTensor &t, const uint8_t *row) {
+    const bool packed = ((uintptr_t)row & 15) == 0 &&
+                        t.nb[0] == (t.type == EKV_DTYPE_F32 ? 4 : 2);
+    if (packed && t.type == EKV_DTYPE_BF16) return *(const uint4 *)row;
+    if (packed && t.type == EKV_DTYPE_F32) {
+        const float4 a = *(const float4 *)row, b = *(const float4 *)(row + 16);
+        const __nv_bfloat162 w0 = __floats2bfloat162_rn(a.x, a.y), w1 = __floats2bfloat162_rn(a.z, a.w);
+        const __nv_bfloat162 w2 = __floats2bfloat162_rn(b.x, b.y), w3 = __floats2bfloat162_rn(b.z, b.w);
+        return make_uint4(*(const uint32_t *)&w0, *(const uint32_t *)&w1, *(const uint32_t *)&w2, *(const uint32_t *)&w3);
+    }
+    if (packed) {  // f16
+        const uint4 h = *(const uint4 *)row;
+        const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*(const __half2 *)&hw[i]);
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(f.x, f.y);
+            w[i] = *(const uint32_t *)&b2;
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
     uint32_t w[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -69,43 +92,54 @@ __device__ __forceinline__ uint4 gg_load8_bf16(const GgTensor &t, const uint8_t 
 }
 
 // K and V ({D, Tk, Hkv, Bk}) -> bf16 pool tiles: row j of K batch element b is row j % 64 of block
-// b * nbk + j / 64. One thread per 8 consecutive d of one (b, h, j) row, K and V; rows j >= Tk of
-// the last block are zero (their keys are masked, and a zero V row keeps P.V finite).
-__global__ void gg_pack_kv_kernel(const GgTensor k, const GgTensor v, const PoolView p, int nbk) {
-    const int D = p.head_dim, W = p.swz_bytes;
-    const int64_t rows = (int64_t)nbk * kGgBT;
-    const int64_t units = k.ne[3] * k.ne[2] * rows * (D / 8);
-    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
-        const int d8 = (int)(u % (D / 8));
-        int64_t r = u / (D / 8);
-        const int64_t j = r % rows;
-        r /= rows;
-        const int h = (int)(r % k.ne[2]);
-        const int b = (int)(r / k.ne[2]);
-        uint4 kw = make_uint4(0, 0, 0, 0), vw = kw;
-        if (j < k.ne[1]) {
-            kw = gg_load8_bf16(k, k.p + d8 * 8 * k.nb[0] + j * k.nb[1] + h * k.nb[2] + b * k.nb[3]);
-            vw = gg_load8_bf16(v, v.p + d8 * 8 * v.nb[0] + j * v.nb[1] + h * v.nb[2] + b * v.nb[3]);
+// b * nbk + j / 64. One thread per 8 consecutive d of one (kv, b, h, j) row; consecutive threads take
+// consecutive d or, for a tensor whose keys are its contiguous dimension (the triple's V, {Tk, Dv}
+// permuted), consecutive keys, so that a warp's loads stay coalesced. Rows j >= Tk of the last block
+// are zero (their keys are masked, and a zero V row keeps P.V finite). Index arithmetic is 32-bit
+// (the planner bounds the unit count).
+__global__ void gg_pack_kv_kernel(const GgTensor k, const GgTensor v, const PoolView p, int nbk, bool k_keys_fastest,
+                                  bool v_keys_fastest) {
+    const int D = p.head_dim, W = p.swz_bytes, D8 = D / 8;
+    const int rows = nbk * kGgBT, H = (int)k.ne[2];
+    const int units = (int)k.ne[3] * H * rows * D8;
+    for (int u2 = blockIdx.x * blockDim.x + threadIdx.x; u2 < 2 * units; u2 += gridDim.x * blockDim.x) {
+        const int kv = u2 >= units;
+        const int u = u2 - kv * units;
+        const GgTensor &t = kv ? v : k;
+        int d8, j, r;
+        if (kv ? v_keys_fastest : k_keys_fastest) {
+            j = u % rows;
+            r = u / rows;
+            d8 = r % D8;
+            r /= D8;
+        } else {
+            d8 = u % D8;
+            r = u / D8;
+            j = r % rows;
+            r /= rows;
         }
-        const int block = b * nbk + (int)(j / kGgBT), row = (int)(j % kGgBT);
-        const uint32_t off = tile_elem_off(row, d8 * 8, D, W);
-        *(uint4 *)(p.prefix + prefix_tile_index(p, 0, block, 0, h) * p.tile_bytes + off) = kw;
-        *(uint4 *)(p.prefix + prefix_tile_index(p, 0, block, 1, h) * p.tile_bytes + off) = vw;
+        const int h = r % H, b = r / H;
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (j < t.ne[1])
+            w = gg_load8_bf16(t, t.p + (int64_t)d8 * 8 * t.nb[0] + (int64_t)j * t.nb[1] + (int64_t)h * t.nb[2] +
+                                     (int64_t)b * t.nb[3]);
+        const int block = b * nbk + (j >> 6), row = j & (kGgBT - 1);
+        *(uint4 *)(p.prefix + prefix_tile_index(p, 0, block, kv, h) * p.tile_bytes + tile_elem_off(row, d8 * 8, D, W)) = w;
     }
 }
 
 // Q ({D, Tq, Hq, Bq}) -> bf16 [Bq][Tq][Hq][D]
 __global__ void gg_pack_q_kernel(const GgTensor q, uint16_t *out) {
-    const int D = (int)q.ne[0];
-    const int64_t units = q.ne[3] * q.ne[1] * q.ne[2] * (D / 8);
-    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
-        const int d8 = (int)(u % (D / 8));
-        int64_t r = u / (D / 8);
-        const int h = (int)(r % q.ne[2]);
-        r /= q.ne[2];
-        const int t = (int)(r % q.ne[1]);
-        const int b = (int)(r / q.ne[1]);
-        *(uint4 *)(out + u * 8) = gg_load8_bf16(q, q.p + d8 * 8 * q.nb[0] + t * q.nb[1] + h * q.nb[2] + b * q.nb[3]);
+    const int D8 = (int)q.ne[0] / 8, H = (int)q.ne[2], T = (int)q.ne[1];
+    const int units = (int)q.ne[3] * T * H * D8;
+    for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
+        const int d8 = u % D8;
+        int r = u / D8;
+        const int h = r % H;
+        r /= H;
+        const int t = r % T, b = r / T;
+        *(uint4 *)(out + (int64_t)u * 8) = gg_load8_bf16(q, q.p + (int64_t)d8 * 8 * q.nb[0] + (int64_t)t * q.nb[1] +
+                                                                (int64_t)h * q.nb[2] + (int64_t)b * q.nb[3]);
     }
 }
 
@@ -148,18 +182,24 @@ __global__ void gg_mask_bits_kernel(const GgTensor m, uint32_t *bits, int Tq, in
     if (__any_sync(0xffffffffu, odd) && lane == 0) atomicOr(nonbinary, 1);
 }
 
-// [Bq][Tq][Hq][D] f32 -> dst ({D, Hq, Tq, Bq} order of flash_attn_ext, any byte strides)
-__global__ void gg_scatter_out_kernel(const float *o, uint8_t *dst, int64_t D, int64_t Hq, int64_t Tq, int64_t Bq,
-                                      int64_t nb0, int64_t nb1, int64_t nb2, int64_t nb3) {
-    const int64_t n = D * Hq * Tq * Bq;
-    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < n; u += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t d = u % D;
-        int64_t r = u / D;
-        const int64_t h = r % Hq;
+// [Bq][Tq][Hq][D] f32 -> dst ({D, Hq, Tq, Bq} order of flash_attn_ext, any byte strides): one thread
+// per 4 consecutive d (one 16-byte load), 32-bit index arithmetic.
+__global__ void gg_scatter_out_kernel(const float *o, uint8_t *dst, int D, int Hq, int Tq, int Bq, int64_t nb0,
+                                      int64_t nb1, int64_t nb2, int64_t nb3) {
+    const int D4 = D / 4;
+    const int n = Bq * Tq * Hq * D4;
+    for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < n; u += gridDim.x * blockDim.x) {
+        const int d4 = u % D4;
+        int r = u / D4;
+        const int h = r % Hq;
         r /= Hq;
-        const int64_t t = r % Tq;
-        const int64_t b = r / Tq;
-        *(float *)(dst + d * nb0 + h * nb1 + t * nb2 + b * nb3) = o[u];
+        const int t = r % Tq, b = r / Tq;
+        const float4 x = *(const float4 *)(o + (int64_t)u * 4);
+        uint8_t *row = dst + (int64_t)h * nb1 + (int64_t)t * nb2 + (int64_t)b * nb3 + (int64_t)d4 * 4 * nb0;
+        *(float *)(row) = x.x;
+        *(float *)(row + nb0) = x.y;
+        *(float *)(row + 2 * nb0) = x.z;
+        *(float *)(row + 3 * nb0) = x.w;
     }
 }
 
@@ -209,7 +249,10 @@ bool gg_plan(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, cons
     pl.nbk = (pl.Tk + kGgBT - 1) / kGgBT;
     pl.words = (pl.Tk + 31) / 32;
     pl.direct_out = contiguous_dst(dst);
-    if ((int64_t)pl.Bk * pl.nbk > (int64_t)1 << 30) return false;
+    // 32-bit index arithmetic in the staging kernels: twice the K/V rows, and the Q / output elements
+    if ((int64_t)2 * pl.Bk * pl.Hkv * pl.nbk * kGgBT * (pl.D / 8) > INT32_MAX ||
+        (int64_t)pl.Bq * pl.Tq * pl.Hq * pl.D > INT32_MAX)
+        return false;
 
     PoolView &p = pl.view;
     p = PoolView{};
@@ -318,8 +361,9 @@ int ggml_tc_run(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, c
     constexpr int T = 256;
     gg_meta_kernel<<<grid_for(std::max<int64_t>(p.n_blocks, pl.Bq), T), T, 0, s>>>(
         p.block_tables, p.seq_lens, seq_ids, p.status, flag, pl.Bk, pl.nbk, pl.Tk, pl.Bq);
-    const int64_t kv_units = (int64_t)pl.Bk * pl.Hkv * pl.nbk * kGgBT * (pl.D / 8);
-    gg_pack_kv_kernel<<<grid_for(kv_units, T), T, 0, s>>>(gg_view(k), gg_view(v), p, pl.nbk);
+    const int64_t kv_units = (int64_t)2 * pl.Bk * pl.Hkv * pl.nbk * kGgBT * (pl.D / 8);
+    gg_pack_kv_kernel<<<grid_for(kv_units, T), T, 0, s>>>(gg_view(k), gg_view(v), p, pl.nbk, k->nb[1] < k->nb[0],
+                                                          v->nb[1] < v->nb[0]);
     const int64_t q_units = (int64_t)pl.Bq * pl.Tq * pl.Hq * (pl.D / 8);
     gg_pack_q_kernel<<<grid_for(q_units, T), T, 0, s>>>(gg_view(q), qb);
     int launches = 3;
@@ -358,7 +402,7 @@ int ggml_tc_run(const ekv_tensor *q, const ekv_tensor *k, const ekv_tensor *v, c
     a.mask_bits_nb = pl.Bm;
     if (const int rc = launch_attention_tc(a, s, TcKernel::Auto)) return rc;
     if (!pl.direct_out) {
-        const int64_t n = (int64_t)pl.D * pl.Hq * pl.Tq * pl.Bq;
+        const int64_t n = (int64_t)pl.D / 4 * pl.Hq * pl.Tq * pl.Bq;
         gg_scatter_out_kernel<<<grid_for(n, T), T, 0, s>>>(ob, (uint8_t *)dst->data, pl.D, pl.Hq, pl.Tq, pl.Bq,
                                                            dst->nb[0], dst->nb[1], dst->nb[2], dst->nb[3]);
         if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
