@@ -529,12 +529,20 @@ def run_serve(args, cfg):
 
 
 def run_other(args, cfg):
-    """Configs 3 and 4 on one GPU: the same JSON contract as the default config, without the
-    end-to-end and CPU legs (the headline metric is config 2's)."""
+    """Configs 3 and 4: the same JSON contract as the default config, without the end-to-end and CPU
+    legs (the headline metric is config 2's). Under torchrun every rank runs its own copy of the
+    workload -- GR00T: its own 128 requests; LingBot: its own episode (one per GPU) -- with no
+    data-path collective; the time is the maximum over ranks."""
     import torch
-    torch.cuda.set_device(0)
+    import torch.distributed as dist
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
     cls = GrootWorkload if cfg["kind"] == "groot" else LingbotWorkload
-    wl = cls(cfg["batch"], 0)
+    wl = cls(cfg["batch"], local)
     stream = torch.cuda.current_stream()
     wl.step_prefix(stream)
     wl.step_calls(stream)
@@ -560,10 +568,13 @@ def run_other(args, cfg):
         raise RuntimeError("device status word set during warm-up")
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    uuid = str(torch.cuda.get_device_properties(0).uuid)
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
     clocks = Clocks(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
     clocks.start()
     time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = wl.ekv.lib.ekv_launch_count()
     t_start.record(stream)
@@ -574,9 +585,11 @@ def run_other(args, cfg):
         ends[k].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     clk = clocks.stop()
     launches = per_step * args.steps if per_step is not None else wl.ekv.lib.ekv_launch_count() - n0
-    ms = t_start.elapsed_time(t_end)
+    ms = dispatch.max_over_ranks(t_start.elapsed_time(t_end), device=f"cuda:{local}")
     call_s = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3 / wl.n_calls
     peaks = load_peaks()
     bound = "tensor" if wl.flop_per_call / (peaks["tc"] * 1e12) >= wl.bytes_per_call / (peaks["hbm"] * 1e9) else "hbm"
@@ -592,13 +605,19 @@ def run_other(args, cfg):
                  "algorithmic_per_launch": {"flop": wl.flop_per_call, "bytes": wl.bytes_per_call},
                  "timed": "CUDA events around each step's layer-calls, divided by the calls (appends included "
                           "for the LingBot chunks)"})
-    line = {"metric": METRIC, "value": wl.qtok_per_step * args.steps / (ms / 1e3), "unit": "query-tok/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+    line = {"metric": METRIC, "value": world * wl.qtok_per_step * args.steps / (ms / 1e3), "unit": "query-tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 MMA, f32 accumulate",
             "data": "synthetic", "config": {"workload": args.config, "description": cfg["desc"],
-                                            "batch_per_gpu": wl.B, "parallelism": "x1"},
+                                            "batch_per_gpu": wl.B,
+                                            "parallelism": f"{'request' if cfg['kind'] == 'groot' else 'episode'}"
+                                                           f"-sharded x{world}"},
             "roofline": roof, "clocks": clk, "gpu_launches": int(launches), "device_status": wl.pool.status()}
-    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------------------------------
@@ -652,6 +671,25 @@ def cpu_baseline(wl: Pi05Workload, n_req: int, n_layers: int, threads: int):
     return qtok / dt, dt, qtok, err
 
 
+def pi05_config(args, cfg, world) -> dict:
+    """The `config` of a pi0.5 bench line; both arms print the same one."""
+    return {"workload": args.workload, "description": cfg["desc"], "batch_per_gpu": cfg["batch"],
+            "layers": N_LAYERS, "denoise_steps": N_STEPS, "suffix_tokens": TQ, "q_heads": HQ, "kv_heads": HKV,
+            "head_dim": D, "block_tokens": BT, "parallelism": f"request-sharded x{world}",
+            "l2": "inputs > L2: every layer-call reads its own Q, suffix K/V and prefix K/V (GBs per step)"}
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 # ------------------------------------------------------------------------------------------
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -668,10 +706,11 @@ def run_reference(args, cfg):
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     rng = np.random.default_rng(1234)
-    B = min(cfg["batch"], max(8, threads))
-    n_layers = 2
+    # the sample the GPU arm's cpu_baseline times: 16 requests x the 18 layer-calls of one denoise step
+    B = min(cfg["batch"], 16)
+    n_layers = N_LAYERS
     reqs = dispatch.make_requests(B, cfg["plo"], cfg["phi"], seed=1234, padded=cfg["padded"])
     plen = np.array([r.prefix_len for r in reqs], np.int32)  # the GPU arm's first B requests
     pvalid = np.array([r.prefix_valid for r in reqs], np.int32)
@@ -707,9 +746,9 @@ def run_reference(args, cfg):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "query-tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": args.workload, "description": cfg["desc"]},
+            "data": "synthetic", "config": pi05_config(args, cfg, world),
             "cpu_baseline": {"value": value, "unit": "query-tok/s", "cores": threads, "kind": "port",
-                             "sample": sample},
+                             "sample": sample, "cpu_model": cpu_model()},
             "e2e": {"value": value, "unit": "query-tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -728,8 +767,10 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config in OTHER_CONFIGS:
-        if args.impl == "reference" or args.gpus != 1:
-            print(json.dumps({"impl": args.impl, "unavailable": f"{args.config} is measured on one GPU, ekv arm only"}))
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"{args.config}: the reference arm times the "
+                                  "default pi0.5 workload only"}))
             return
         run_other(args, OTHER_CONFIGS[args.config])
         return
@@ -750,6 +791,9 @@ def main():
 
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
+    # pinned host buffers (the end-to-end leg) local to this GPU's NUMA node
+    all_cpus = os.sched_getaffinity(0)
+    numa_cpus = dispatch.bind_to_gpu_numa_node(local)
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
@@ -845,29 +889,31 @@ def main():
     # ---- end to end through the C-ABI with host buffers (pinned), copies inside the timing ----
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(wl, args, world, barrier)
+        e2e = run_e2e(wl, args, world, rank, barrier)
+        e2e["host_cpus"] = f"{len(numa_cpus)} CPUs of the GPU's NUMA node" if numa_cpus else "unbound"
+    os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses the whole host
 
     line = {"metric": METRIC, "value": value, "unit": "query-tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16/bf16 MMA, f32 accumulate (Q8_0 cache)" if wl.dtype == wl.ekv.DTYPE_Q8_0
             else "bf16 MMA, f32 accumulate",
-            "data": "synthetic", "config": {"workload": args.workload, "description": cfg["desc"],
-                                            "batch_per_gpu": wl.B, "layers": N_LAYERS, "denoise_steps": N_STEPS,
-                                            "suffix_tokens": TQ, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
-                                            "block_tokens": BT, "parallelism": f"request-sharded x{world}",
-                                            "l2": "inputs > L2 (per step ~%.1f GB of distinct Q/KV/O)" %
-                                                  ((wl.q.numel() * 2 * 2 + wl.sk.numel() * 4 + wl.pk.numel() * 4) / 1e9)},
+            "data": "synthetic", "config": pi05_config(args, cfg, world),
             "roofline": roof, "clocks": clk, "gpu_launches": int(launches),
             "device_status": status}
     if e2e is not None:
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
+        # the reference's own thread count, min(hardware threads, 8) (models/pi05.cpp:586-587), and
+        # every host thread
+        hw = len(all_cpus)
+        threads = min(hw, 8)
         v, dt, qtok, err = cpu_baseline(wl, n_req=min(wl.B, 16), n_layers=N_LAYERS, threads=threads)
+        v_all, dt_all, _, _ = cpu_baseline(wl, n_req=min(wl.B, 16), n_layers=N_LAYERS, threads=hw)
         line["cpu_baseline"] = {"value": v, "unit": "query-tok/s", "cores": threads, "kind": "port",
                                 "sample": f"{min(wl.B, 16)} requests x {N_LAYERS} layer-calls (denoise step 0), "
                                           f"{qtok} query-tokens in {dt:.2f} s",
-                                "max_abs_err_vs_gpu": err}
+                                "all_threads": {"value": v_all, "cores": hw, "seconds": dt_all},
+                                "cpu_model": cpu_model(), "max_abs_err_vs_gpu": err}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -875,7 +921,7 @@ def main():
         print(json.dumps(line), flush=True)
 
 
-def run_e2e(wl, args, world, barrier):
+def run_e2e(wl, args, world, rank, barrier):
     """Same metric through the C-ABI with host buffers: every step copies its inputs from
     pinned host memory (prefix K/V of all layers, per-call suffix K/V and Q) and reads every
     call's output back. Per-call inputs and outputs move in chunks of one denoise step's 18
@@ -903,6 +949,12 @@ def run_e2e(wl, args, world, barrier):
     ev_out = [torch.cuda.Event() for _ in range(2)]
     h2d_bytes = (wl.pk.numel() + wl.pv.numel() + wl.sk.numel() + wl.sv.numel() + wl.q.numel()) * 2
     d2h_bytes = wl.out.numel() * 2
+    # the step's result for the serving front: the last layer-step's outputs of every request, gathered
+    # on rank 0 over NCCL (the north star's "gather action outputs") and read back there
+    h_final = torch.empty((world,) + tuple(wl.out.shape[1:]), dtype=wl.out.dtype, pin_memory=True) if rank == 0 \
+        else None
+    if rank == 0 and world > 1:
+        d2h_bytes += h_final.numel() * 2
 
     def one_step():
         with torch.cuda.stream(s_h2d):
@@ -941,6 +993,10 @@ def run_e2e(wl, args, world, barrier):
                 s_d2h.wait_event(ev_done[i])
                 h_out[k * G:(k + 1) * G].copy_(d_out[i], non_blocking=True)
                 ev_out[i].record(s_d2h)
+        if world > 1:
+            final = dispatch.gather_outputs(d_out[(n_chunks - 1) & 1, G - 1], world, rank)
+            if rank == 0:
+                h_final.copy_(final, non_blocking=True)
 
     for _ in range(args.warmup):
         one_step()
@@ -955,8 +1011,13 @@ def run_e2e(wl, args, world, barrier):
     barrier()
     # the host buffers received the same outputs the device-resident run produced
     ok = bool(torch.equal(h_out[-1].to(dev), wl.out[-1]))
+    ok_final = True
+    if world > 1 and rank == 0:
+        ok_final = bool(torch.equal(h_final[0].to(dev), wl.out[-1]))
     return {"value": world * wl.qtok_per_step * args.steps / dt, "unit": "query-tok/s",
             "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
+            "gather": "NCCL gather of every rank's last layer-step outputs to rank 0, read back there"
+                      if world > 1 else None, "gathered_outputs_match": ok_final,
             "ms_per_step": 1e3 * dt / args.steps, "outputs_match_device_run": ok,
             "timing": "host wall clock around K steps, synchronised on both sides"}
 

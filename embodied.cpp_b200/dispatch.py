@@ -120,3 +120,73 @@ def max_over_ranks(value: float, device=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_outputs(local, world: int, rank: int):
+    """Rank 0 receives every rank's device result tensor (all the same shape) over the process
+    group's backend -- NCCL on GPUs -- stacked as [world, ...]; other ranks get None."""
+    dist = _dist()
+    if world == 1 or dist is None:
+        return local[None]
+    import torch
+
+    out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device) if rank == 0 else None
+    dist.gather(local, gather_list=list(out.unbind(0)) if rank == 0 else None, dst=0)
+    return out
+
+
+def local_cpus_of_gpu(device_index: int) -> Optional[List[int]]:
+    """Host CPUs attached to the GPU's NUMA node (from its PCI device's local_cpulist), or None
+    where that cannot be read."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            bus = pynvml.nvmlDeviceGetPciInfo(pynvml.nvmlDeviceGetHandleByIndex(device_index)).busId
+        finally:
+            pynvml.nvmlShutdown()
+        if isinstance(bus, bytes):
+            bus = bus.decode()
+        # NVML reports an 8-hex-digit domain ("00000000:1B:00.0"); sysfs uses 4 and lower case
+        dom, rest = bus.split(":", 1)
+        path = f"/sys/bus/pci/devices/{int(dom, 16):04x}:{rest.lower()}/local_cpulist"
+        with open(path) as f:
+            spec = f.read().strip()
+    except Exception:
+        return None
+    cpus: List[int] = []
+    for part in spec.split(","):
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.extend(range(int(a), int(b) + 1))
+        elif part:
+            cpus.append(int(part))
+    return cpus or None
+
+
+def bind_to_gpu_numa_node(device_index: int) -> Optional[List[int]]:
+    """Restrict this process to the CPUs of its GPU's NUMA node, so that pinned host buffers
+    allocated afterwards are local to the GPU's PCIe root; returns the CPU list (None: unchanged).
+    CUDA_VISIBLE_DEVICES remapping is respected by NVML index only when it is unset or an identity
+    list; otherwise nothing is changed."""
+    import os
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if not all(x.isdigit() for x in ids) or device_index >= len(ids):
+            return None
+        device_index = int(ids[device_index])
+    cpus = local_cpus_of_gpu(device_index)
+    if not cpus:
+        return None
+    try:
+        allowed = os.sched_getaffinity(0)
+        keep = [c for c in cpus if c in allowed]
+        if not keep:
+            return None
+        os.sched_setaffinity(0, keep)
+        return keep
+    except (AttributeError, OSError):
+        return None

@@ -71,9 +71,15 @@ def main():
         raise SystemExit(3)  # leaves between steps: no collective of this rank is in flight
     merged = dispatch.gather_results(local, world, rank)
     t = dispatch.max_over_ranks(float(rank + 1))
+    import torch
+
+    # the bench's end-of-step tensor gather: every rank's [2, 3] result stacked on rank 0
+    stacked = dispatch.gather_outputs(torch.full((2, 3), float(rank + 1)), world, rank)
     if rank == 0:
-        np.savez(os.path.join(args.out, "results.npz"), max_t=t,
+        np.savez(os.path.join(args.out, "results.npz"), max_t=t, stacked=stacked.numpy(),
                  **{f"r{k}": v for k, v in merged.items()})
+    else:
+        assert stacked is None
     with open(os.path.join(args.out, f"rank{rank}.txt"), "w") as f:
         f.write(" ".join(str(r.req_id) for r in mine) + "\n")
         for k, sv in sorted(tables.items()):

@@ -71,6 +71,7 @@ def test_two_gloo_ranks_match_single_process(tmp_path, policy):
     parts = dispatch.assign_requests([r.prefix_len for r in table], 2, policy)
     res = np.load(tmp_path / "results.npz")
     assert float(res["max_t"]) == 2.0  # max over ranks of (rank + 1)
+    np.testing.assert_array_equal(res["stacked"], np.stack([np.full((2, 3), 1.0), np.full((2, 3), 2.0)]))
     for r in table:  # every request once, identical to a single-process run
         np.testing.assert_array_equal(res[f"r{r.req_id}"], W.request_output(r))
     for rank in range(2):
