@@ -600,8 +600,8 @@ def run_other(args, cfg):
         ach = wl.bytes_per_call / call_s / 1e9
         roof = {"bound": bound, "achieved": ach, "peak": peaks["hbm"], "unit": "GB/s", "frac": ach / peaks["hbm"]}
     roof.update({"traffic": None, "peak_source": peaks["source"], "avg_launch_us": call_s * 1e6,
-                 "kernel": "attn_tc_kernel (one CTA per 128 query rows" +
-                           (", packed units)" if cfg["kind"] == "groot" else ")"),
+                 "kernel": ("attn_heads_kernel (four heads of a request per unit, persistent CTAs)"
+                            if cfg["kind"] == "groot" else "attn_tc_kernel (one CTA per 128 query rows)"),
                  "algorithmic_per_launch": {"flop": wl.flop_per_call, "bytes": wl.bytes_per_call},
                  "timed": "CUDA events around each step's layer-calls, divided by the calls (appends included "
                           "for the LingBot chunks)"})

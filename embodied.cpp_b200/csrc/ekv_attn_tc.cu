@@ -1501,7 +1501,8 @@ int dispatch(const AttnArgs &a, cudaStream_t s, size_t ws) {
 extern "C" int ekv_debug_set_trace(unsigned long long *buf) {
     if (cudaMemcpyToSymbol(ekv::c_trace, &buf, sizeof(buf)) != cudaSuccess) return -2;
     if (ekv::pair_debug_set_trace(buf)) return -2;
-    return ekv::pair128_debug_set_trace(buf);
+    if (ekv::pair128_debug_set_trace(buf)) return -2;
+    return ekv::heads_debug_set_trace(buf);
 }
 namespace ekv {
 #endif
@@ -1549,6 +1550,11 @@ int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k) {
     if (a.n_splits == 0) ws = (size_t)-1;  // the C-ABI checked the size against the maximum need
     // head_dim 256: each SM of a pair copies (bf16) or dequantises (Q8_0) half of every tile, and
     // each K/V byte crosses L2 -> SM twice per request instead of four times
+    if (k == TcKernel::Heads) return launch_attention_heads(a, s, sm_count());
+    if (k == TcKernel::Auto && heads_fits(a) && heads_units(a) * 4 >= sm_count()) {
+        const int rc = launch_attention_heads(a, s, sm_count());
+        if (rc != EKV_ERR_UNSUPPORTED) return rc;  // else nothing was enqueued: the kernels below
+    }
     const bool pair = a.pool.head_dim == 256 && k != TcKernel::OneCta;
     if (pair && k == TcKernel::Pair) return launch_attention_pair128(a, s, ws, sm_count());
     // bf16 pools: the 128-key pair kernel where the shape allows it. Q8_0 pools keep the 64-key pair

@@ -143,7 +143,7 @@ int ekv_pool_create(const ekv_pool_config *cfg, ekv_pool **out) {
     v.n_layers = c.n_layers;
     v.max_seqs = c.max_seqs;
     v.max_blocks_per_seq = c.max_blocks_per_seq;
-    v.suffix_rows = (c.suffix_tokens + 7) / 8 * 8;
+    v.suffix_rows = (c.suffix_tokens + 15) / 16 * 16;
     v.swz_bytes = ekv::swizzle_bytes_for(c.head_dim);
     v.bt_shift = -1;
     for (int sh = 0; sh < 16; ++sh)
@@ -550,7 +550,8 @@ int ekv_attention_algo(ekv_pool *p, const ekv_attn_params *prm, const void *q, v
     const DeviceScope dev_scope(p);
     if (const int e = dev_scope.rc()) return e;
     if (algo == EKV_ALGO_SIMT) return ekv::launch_attention_simt(a, (cudaStream_t)stream);
-    if (algo != EKV_ALGO_TC && algo != EKV_ALGO_TC_PAIR && algo != EKV_ALGO_TC_CTA && algo != EKV_ALGO_TC_PAIR64)
+    if (algo != EKV_ALGO_TC && algo != EKV_ALGO_TC_PAIR && algo != EKV_ALGO_TC_CTA && algo != EKV_ALGO_TC_PAIR64 &&
+        algo != EKV_ALGO_TC_HEADS)
         return EKV_ERR_INVALID_ARG;
     const size_t need = ekv::attention_tc_workspace(p->view, *prm, p->cfg.max_blocks_per_seq * p->cfg.block_tokens, p->sms);
     if (workspace && ((uintptr_t)workspace & 15)) return EKV_ERR_INVALID_ARG;
@@ -562,6 +563,7 @@ int ekv_attention_algo(ekv_pool *p, const ekv_attn_params *prm, const void *q, v
     const ekv::TcKernel k = algo == EKV_ALGO_TC_PAIR     ? ekv::TcKernel::Pair
                             : algo == EKV_ALGO_TC_CTA    ? ekv::TcKernel::OneCta
                             : algo == EKV_ALGO_TC_PAIR64 ? ekv::TcKernel::Pair64
+                            : algo == EKV_ALGO_TC_HEADS  ? ekv::TcKernel::Heads
                                                          : ekv::TcKernel::Auto;
     return ekv::launch_attention_tc(a, (cudaStream_t)stream, k);
 }

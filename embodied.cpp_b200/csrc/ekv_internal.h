@@ -89,7 +89,9 @@ int launch_attention_simt(const AttnArgs &a, cudaStream_t s);
 // power-of-two blocks), else the 64-key CTA-pair kernel (ekv_attn_pair.cu); Pair = the 128-key
 // pair kernel or EKV_ERR_UNSUPPORTED; Pair64 = the 64-key pair kernel; OneCta = one CTA per 128
 // query rows. Other head dims always run one CTA per 128 query rows.
-enum class TcKernel { Auto, Pair, OneCta, Pair64 };
+// Heads = the multi-head small-query kernel (ekv_attn_heads.cu), which Auto also picks where
+// heads_fits() holds and the call has at least a quarter of the SMs' worth of units.
+enum class TcKernel { Auto, Pair, OneCta, Pair64, Heads };
 int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k);
 size_t attention_tc_workspace(const PoolView &p, const ekv_attn_params &prm, int max_prefix, int sms);
 // CTA-pair kernel (head_dim 256); n_splits == 0 in `a` = choose from the workspace at a.ws_o
@@ -99,11 +101,17 @@ int pair_choose_splits(int64_t pair_units, int max_tiles, int sms);
 // call's shape needs the 64-key pair kernel
 int launch_attention_pair128(AttnArgs a, cudaStream_t s, size_t ws_bytes, int sms);
 int pair128_choose_splits(int64_t pair_units, int max_tiles, int sms);
+// Multi-head small-query kernel: four heads of one request per unit (MHA, <= 32 query tokens,
+// head_dim 48 or 64, bf16 pool); EKV_ERR_UNSUPPORTED, with nothing enqueued, for other shapes.
+bool heads_fits(const AttnArgs &a);
+int heads_units(const AttnArgs &a);
+int launch_attention_heads(const AttnArgs &a, cudaStream_t s, int sms);
 // combine key-split partial outputs (head_dim of the pool) into a.out
 int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s);
 #ifdef EKV_TRACE
 int pair_debug_set_trace(unsigned long long *buf);
 int pair128_debug_set_trace(unsigned long long *buf);
+int heads_debug_set_trace(unsigned long long *buf);
 #endif
 
 }  // namespace ekv

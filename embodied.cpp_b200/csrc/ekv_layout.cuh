@@ -11,7 +11,8 @@
 //                 q8_qs_off) followed by fp16 scales [block_tokens][head_dim/32]; a gather
 //                 re-interleaves them into ggml's block_q8_0 {d, qs[32]} bytes.
 //   suffix arena  [n_layers][max_seqs][2][kv_heads] tiles of suffix_rows bf16 rows, in the
-//                 same swizzled bf16 tile layout (suffix_rows = suffix_tokens rounded up to 8).
+//                 same swizzled bf16 tile layout (suffix_rows = suffix_tokens rounded up to 16, so
+//                 the tiles of consecutive heads stack into one MMA operand with 16-aligned columns).
 //   seq table     int32 block_tables[max_seqs][max_blocks_per_seq], int32 seq_lens[max_seqs]
 //   status word   int32[4]: [0] first error code, [1..3] details of that error
 #pragma once
@@ -34,7 +35,7 @@ struct PoolView {
     int32_t n_layers;
     int32_t max_seqs;
     int32_t max_blocks_per_seq;
-    int32_t suffix_rows;      // rows per suffix tile (multiple of 8), 0 = none
+    int32_t suffix_rows;      // rows per suffix tile (multiple of 16), 0 = none
     int32_t swz_bytes;        // W: row bytes of one swizzle chunk (128, 64 or 32)
     int32_t bt_shift;         // log2(block_tokens) when it is a power of two, else -1
     int64_t tile_bytes;       // bytes of one (layer, block, kv, head) prefix tile

@@ -38,7 +38,7 @@ def flex_meta_word(seq: int, frame: int, clean: bool) -> int:
         return 0
     w = ((seq + 1) << 24) | ((1 if clean else 0) << 23) | (frame & 0x7FFFFF)
     return w - (1 << 32) if w >= (1 << 31) else w
-ALGO_TC, ALGO_SIMT, ALGO_TC_PAIR, ALGO_TC_CTA, ALGO_TC_PAIR64 = 0, 1, 2, 3, 4
+ALGO_TC, ALGO_SIMT, ALGO_TC_PAIR, ALGO_TC_CTA, ALGO_TC_PAIR64, ALGO_TC_HEADS = 0, 1, 2, 3, 4, 5
 
 # Device-side error codes written into the pool status word by kernels.
 DEV_ERR_BAD_BLOCK, DEV_ERR_BAD_SEQ, DEV_ERR_BAD_POS, DEV_ERR_TIMEOUT = 1, 2, 3, 4

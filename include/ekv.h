@@ -256,6 +256,13 @@ int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, const void *
 #define EKV_ALGO_TC_PAIR64 4 /* head_dim 256 on CTA pairs with 64-key tiles and Q in tensor
                               memory (what EKV_ALGO_TC runs for Q8_0 pools at head_dim 256);
                               other head dims as EKV_ALGO_TC                                  */
+#define EKV_ALGO_TC_HEADS 5 /* multi-head calls with few query tokens (GR00T's 17 x 32 heads,
+                              models/groot_n1.cpp:328-364): four heads of one request per unit,
+                              one per TMEM lane quarter, persistent CTAs streaming the four heads'
+                              K/V of a block in one copy. Needs a bf16 pool, q_heads == kv_heads
+                              (a multiple of 4), q_tokens <= 32, head_dim 48 or 64, 16/32/64-token
+                              blocks and suffix_len <= 64 (EKV_ERR_UNSUPPORTED otherwise);
+                              EKV_ALGO_TC picks it for such calls with at least 37 units    */
 int ekv_attention_algo(ekv_pool *pool, const ekv_attn_params *p, const void *q, void *out,
                        void *workspace, size_t workspace_bytes, int32_t algo,
                        ekv_stream_t stream);
