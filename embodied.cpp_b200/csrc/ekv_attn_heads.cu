@@ -31,10 +31,10 @@
 //
 // The kernel is persistent: min(units, SMs) CTAs each walk units blockIdx.x, blockIdx.x + gridDim.x,
 // ...; every role iterates the same units, so the copy engine streams the next unit's K/V while the
-// current unit's softmax and epilogue run. Warps: 0-7 softmax (warp w: head w & 3 of the unit, keys
-// [32 (w >> 2), +32) of each tile, lane = query token; the two warps of a head swap row maxima per
-// tile), 8 TMEM allocation and MMA issue (one thread), 9 K feeder, 10 V feeder, 11 planner (per unit:
-// sequence, visible key range, block ids -> shared memory) and Q loader, 12-15 epilogue (warp e: head
+// current unit's softmax and epilogue run. Warps: 0 TMEM allocation and MMA issue (one thread), 1 K
+// feeder, 2 V feeder, 3 planner (per unit: sequence, visible key range, block ids -> shared memory) and
+// Q loader, 4-11 softmax (warp w: head w & 3 of the unit, keys [32 ((w - 4) >> 2), +32) of each tile,
+// lane = query token; the two warps of a head swap row maxima per tile), 12-15 epilogue (warp e: head
 // e & 3, O / l of a unit once its last P.V is done, while the softmax warps go on to the next unit).
 //
 // Every wait is bounded; on expiry the CTA records DEV_ERR_TIMEOUT, raises its abort flag and unwinds
@@ -83,7 +83,9 @@ struct HCfg {
     static constexpr int OFF_PLAN = OFF_XCH + 8 * kBM * 4;
     static constexpr int SMEM = OFF_PLAN + 4 * (64 + kHMaxBlk * 4) + 1024;  // + alignment slack
     static constexpr int SMW = 8;                       // softmax warps
-    static constexpr int MMA_WARP = 8, KF_WARP = 9, VF_WARP = 10, Q_WARP = 11, EPI_WARP0 = 12;
+    // The MMA-issuing warp is warp 0: a sub-partition issues from its lowest-numbered ready warp first,
+    // and the issuing thread must not wait behind the softmax warps' long arithmetic runs.
+    static constexpr int MMA_WARP = 0, KF_WARP = 1, VF_WARP = 2, Q_WARP = 3, SM_WARP0 = 4, EPI_WARP0 = 12;
     static constexpr int EPW = 4;                       // epilogue warps, one per TMEM lane quarter
     static constexpr int THREADS = (EPI_WARP0 + EPW) * 32;
     static constexpr int S_COL = 0, P_COL = ROWS, O_COL = P_COL + G * BN / 2, O_STRIDE = 64;
@@ -133,8 +135,9 @@ static_assert(sizeof(HPlan) == 64 + kHMaxBlk * 4, "plan slot");
 
 // Stage row (= S column) of key k (0..63 of the tile) of head h: prefix tiles hold, for each run of
 // bt keys, the four heads' bt rows; suffix tiles the four heads' slot tiles of suffix_rows rows.
-__device__ __forceinline__ int heads_row(bool suffix, int h, int k, int bt, int suffix_rows) {
-    return suffix ? h * suffix_rows + k : (k / bt) * (kHG * bt) + h * bt + (k % bt);
+__device__ __forceinline__ int heads_row(bool suffix, int h, int k, int bt_shift, int suffix_rows) {
+    return suffix ? h * suffix_rows + k
+                  : ((k >> bt_shift) * kHG + h) * (1 << bt_shift) + (k & ((1 << bt_shift) - 1));
 }
 
 __device__ __forceinline__ void heads_fail(const AttnArgs &a, volatile int *abort, int where) {
@@ -366,8 +369,19 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
     } else if (warp == C::MMA_WARP) {
         if (lane == 0) {
             const PoolView &p = a.pool;
-            const int bt = p.block_tokens, srows = p.suffix_rows;
+            const int srows = p.suffix_rows;
             const uint32_t idO = idesc_f16(true, true, D);
+            // P.V operands of head h, key step kk (index 4h + kk): A in tensor memory; B at a fixed offset in
+            // the V stage (prefix and suffix tiles), in 16-byte units of the descriptor's address field
+            uint32_t pv_a[G * 4], pv_bp[G * 4], pv_bs[G * 4];
+#pragma unroll
+            for (int h = 0; h < G; ++h)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    pv_a[4 * h + kk] = tmem + (uint32_t)(C::P_COL + h * (BN / 2) + kk * 8);
+                    pv_bp[4 * h + kk] = (uint32_t)(heads_row(false, h, 16 * kk, p.bt_shift, srows) / 8) * (C::SBO >> 4);
+                    pv_bs[4 * h + kk] = (uint32_t)(heads_row(true, h, 16 * kk, p.bt_shift, srows) / 8) * (C::SBO >> 4);
+                }
             const uint32_t idSp = idesc_f16(true, false, C::ROWS);
             const uint32_t idSs = idesc_f16(true, false, srows > 0 ? G * srows : 16);
             const int nks = (a.suffix_len + 15) / 16;  // P.V key steps of a suffix tile, per head
@@ -424,25 +438,17 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                     return false;
                 tc_fence_after();
                 if (t < 50) TRACE(250 + t);
-                const uint32_t va = smem_addr(sV + s * C::STAGE);
+                const uint64_t vd = sdesc(smem_addr(sV + s * C::STAGE), 8 * C::W, C::SBO, C::LAYOUT);
                 const uint32_t od = tmem + (uint32_t)(C::O_COL + (u & 1) * C::O_STRIDE);
                 const bool suffix = j >= pl.np;
                 const int nk = suffix ? nks : BN / 16;
-                uint32_t av[G * 4];
                 uint64_t bv[G * 4];
 #pragma unroll
-                for (int h = 0; h < G; ++h)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const int i = h * 4 + kk;
-                        av[i] = tmem + (uint32_t)(C::P_COL + h * (BN / 2) + kk * 8);
-                        const int row = heads_row(suffix, h, 16 * kk, bt, srows);
-                        bv[i] = sdesc(va + (uint32_t)(row / 8) * C::SBO, 8 * C::W, C::SBO, C::LAYOUT);
-                    }
+                for (int i = 0; i < G * 4; ++i) bv[i] = vd + (suffix ? pv_bs[i] : pv_bp[i]);
                 if (nk == 4) {
 #pragma unroll
                     for (int h = 0; h < G; ++h)
-                        mma_ts_x4<false>(od, *reinterpret_cast<const uint32_t(*)[4]>(av + 4 * h),
+                        mma_ts_x4<false>(od, *reinterpret_cast<const uint32_t(*)[4]>(pv_a + 4 * h),
                                          *reinterpret_cast<const uint64_t(*)[4]>(bv + 4 * h), idO,
                                          (j > 0 || h > 0) ? 1u : 0u);
                 } else {  // a suffix tile of at most 48 keys: fewer key steps per head
@@ -451,7 +457,7 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
 #pragma unroll
                         for (int kk = 0; kk < 3; ++kk)
                             if (kk < nk)
-                                mma_ts(od, av[h * 4 + kk], bv[h * 4 + kk], idO, (j > 0 || h > 0 || kk > 0) ? 1u : 0u);
+                                mma_ts(od, pv_a[h * 4 + kk], bv[h * 4 + kk], idO, (j > 0 || h > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(bar(HB_VE + s));  // P.V(t) done: V stage and P buffers free, O updated
                 return true;
@@ -564,11 +570,14 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
     } else {
         // ---- softmax: warp w = head (w & 3) of the unit, keys [32 half, +32) of each tile, half = w >> 2;
         // lane = query token ----
-        const int h = warp & 3, half = warp >> 2;
+        const int h = warp & 3, half = (warp - C::SM_WARP0) >> 2;
         const uint32_t lb = ((uint32_t)(32 * h)) << 16;
         const int r = 32 * h + lane;  // TMEM lane / exchange row
         const bool row_ok = lane < a.q_tokens;
-        const int bt = a.pool.block_tokens, srows = a.pool.suffix_rows;
+        const int bs = a.pool.bt_shift, srows = a.pool.suffix_rows;
+        // S columns of this warp's two 16-key chunks in prefix and suffix tiles
+        const int row_p0 = heads_row(false, h, 32 * half, bs, srows), row_p1 = heads_row(false, h, 32 * half + 16, bs, srows);
+        const int row_s0 = heads_row(true, h, 32 * half, bs, srows), row_s1 = heads_row(true, h, 32 * half + 16, bs, srows);
         float *xmax = (float *)(smem + C::OFF_XCH);  // [2 parity][2 halves][128 rows]
         float *lsum = xmax + 4 * kBM;                 // [2 units][2 halves][128 rows]
         const uint32_t xbar = bar(HB_XCH + h);
@@ -605,16 +614,16 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                if (warp == 0 && lane == 0 && t < 50) TRACE(300 + t);
-                if (warp == 3 && lane == 0 && t < 50) TRACE(650 + t);
+                if (warp == C::SM_WARP0 && lane == 0 && t < 50) TRACE(300 + t);
+                if (warp == C::SM_WARP0 + 3 && lane == 0 && t < 50) TRACE(650 + t);
                 const bool suffix = j >= np;
                 uint32_t s0[16], s1[16];  // keys [32 half, +16), [32 half + 16, +16)
-                tmem_load16x2(tmem + lb + (uint32_t)(C::S_COL + heads_row(suffix, h, 32 * half, bt, srows)),
-                              tmem + lb + (uint32_t)(C::S_COL + heads_row(suffix, h, 32 * half + 16, bt, srows)), s0, s1);
+                tmem_load16x2(tmem + lb + (uint32_t)(C::S_COL + (suffix ? row_s0 : row_p0)),
+                              tmem + lb + (uint32_t)(C::S_COL + (suffix ? row_s1 : row_p1)), s0, s1);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(HB_SE));
-                if (warp == 0 && lane == 0 && t < 50) TRACE(850 + t);
+                if (warp == C::SM_WARP0 && lane == 0 && t < 50) TRACE(850 + t);
                 const int w0 = (suffix ? 0 : kbeg + j * BN) + 32 * half;
                 // rows past the call's tokens count as fully visible: their Q rows are zero, their
                 // scores finite, and their output rows are never stored
@@ -644,9 +653,9 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                 const float cm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                        fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
                 xmax[((t & 1) * 2 + half) * kBM + r] = cm;
-                if (warp == 0 && lane == 0 && t < 50) TRACE(900 + t);
+                if (warp == C::SM_WARP0 && lane == 0 && t < 50) TRACE(900 + t);
                 if (!(ok = heads_xsync(xbar, uses++, abort, budget))) break;
-                if (warp == 0 && lane == 0 && t < 50) TRACE(950 + t);
+                if (warp == C::SM_WARP0 && lane == 0 && t < 50) TRACE(950 + t);
                 const float rmax = fmaxf(cm, xmax[((t & 1) * 2 + (half ^ 1)) * kBM + r]);
                 bool waited = false;
                 if (__any_sync(0xffffffffu, rmax > (m_used + 8.0f) * inv_scale_log2)) {
@@ -689,26 +698,44 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                 const bool all_p = all_vis && __all_sync(0xffffffffu, m_used != -INFINITY);
                 float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 uint32_t pw[16];
+                if (all_p) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    float pr[4];
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int c = 2 * i + e;
-                        const float x0 = ex2(fmaf(__uint_as_float(s0[c]), a.scale_log2, neg_m));
-                        const float x1 = ex2(fmaf(__uint_as_float(s1[c]), a.scale_log2, neg_m));
-                        pr[e] = (all_p || ((pv >> c) & 1u)) ? x0 : 0.0f;
-                        pr[2 + e] = (all_p || ((pv >> (16 + c)) & 1u)) ? x1 : 0.0f;
-                        ps[e] += pr[e];
-                        ps[2 + e] += pr[2 + e];
+                    for (int i = 0; i < 8; ++i) {
+                        const float x0 = ex2(fmaf(__uint_as_float(s0[2 * i]), a.scale_log2, neg_m));
+                        const float x1 = ex2(fmaf(__uint_as_float(s0[2 * i + 1]), a.scale_log2, neg_m));
+                        const float y0 = ex2(fmaf(__uint_as_float(s1[2 * i]), a.scale_log2, neg_m));
+                        const float y1 = ex2(fmaf(__uint_as_float(s1[2 * i + 1]), a.scale_log2, neg_m));
+                        ps[0] += x0;
+                        ps[1] += x1;
+                        ps[2] += y0;
+                        ps[3] += y1;
+                        const __nv_bfloat162 lo = __floats2bfloat162_rn(x0, x1);
+                        const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
+                        pw[i] = *(const uint32_t *)&lo;
+                        pw[8 + i] = *(const uint32_t *)&hi;
                     }
-                    const __nv_bfloat162 lo = __floats2bfloat162_rn(pr[0], pr[1]);
-                    const __nv_bfloat162 hi = __floats2bfloat162_rn(pr[2], pr[3]);
-                    pw[i] = *(const uint32_t *)&lo;
-                    pw[8 + i] = *(const uint32_t *)&hi;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        float pr[4];
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int c = 2 * i + e;
+                            const float x0 = ex2(fmaf(__uint_as_float(s0[c]), a.scale_log2, neg_m));
+                            const float x1 = ex2(fmaf(__uint_as_float(s1[c]), a.scale_log2, neg_m));
+                            pr[e] = ((pv >> c) & 1u) ? x0 : 0.0f;
+                            pr[2 + e] = ((pv >> (16 + c)) & 1u) ? x1 : 0.0f;
+                            ps[e] += pr[e];
+                            ps[2 + e] += pr[2 + e];
+                        }
+                        const __nv_bfloat162 lo = __floats2bfloat162_rn(pr[0], pr[1]);
+                        const __nv_bfloat162 hi = __floats2bfloat162_rn(pr[2], pr[3]);
+                        pw[i] = *(const uint32_t *)&lo;
+                        pw[8 + i] = *(const uint32_t *)&hi;
+                    }
                 }
                 l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-                if (warp == 0 && lane == 0 && t < 50) TRACE(600 + t);
+                if (warp == C::SM_WARP0 && lane == 0 && t < 50) TRACE(600 + t);
                 // P(t - 1) has been consumed (P.V(t - 1) done) before P(t) overwrites it
                 if (t >= 1 && !waited) {
                     if (!mbar_wait(bar(HB_VE + (t - 1) % NS), (uint32_t)((t - 1) / NS) & 1u, abort, budget)) {
@@ -722,8 +749,8 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(HB_PF));
-                if (warp == 0 && lane == 0 && t < 50) TRACE(350 + t);
-                if (warp == 3 && lane == 0 && t < 50) TRACE(700 + t);
+                if (warp == C::SM_WARP0 && lane == 0 && t < 50) TRACE(350 + t);
+                if (warp == C::SM_WARP0 + 3 && lane == 0 && t < 50) TRACE(700 + t);
             }
             if (!ok) break;
             // ---- the unit's row sums to the epilogue warps (this unit's slot is free once the epilogue of
@@ -738,7 +765,7 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                 mbar_arrive(bar(HB_LR + (u & 1)));
                 mbar_arrive(bar(HB_LE + slot));
             }
-            if (warp == 0 && lane == 0 && u < 20) TRACE(400 + u);
+            if (warp == C::SM_WARP0 && lane == 0 && u < 20) TRACE(400 + u);
         }
         if (!ok && lane == 0) heads_fail(a, abort, 15);
     }
