@@ -219,16 +219,20 @@ __device__ __forceinline__ void pair_suffix_direct(const AttnArgs &a, const Pair
             v[i] = make_uint4(0, 0, 0, 0);
             if (u < UNITS && srow < a.suffix_len) v[i] = __ldg((const uint4 *)(src + srow * row_stride + dl));
         }
+        bool bad = false;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int u = u0 + i * nthr;
             if (u >= UNITS) break;
             const int row = u / upr, dl = (u - row * upr) * 8;
             uint4 w = v[i];
-            if (TO_F16)
+            if (TO_F16) {
                 w = make_uint4(bf16x2_to_f16x2(w.x), bf16x2_to_f16x2(w.y), bf16x2_to_f16x2(w.z), bf16x2_to_f16x2(w.w));
+                bad |= f16x8_has_inf(w);
+            }
             *(uint4 *)(sDst + tile_elem_off(row, dl, dD, W)) = w;
         }
+        if (TO_F16 && bad) report_error(a.pool.status, DEV_ERR_F16_RANGE, 2, pl.b, j);
     }
 }
 
@@ -455,14 +459,17 @@ __device__ __forceinline__ void pair_convert_suffix(const AttnArgs &a, const Pai
         v[i] = make_uint4(0, 0, 0, 0);
         if (srow < p.suffix_rows) v[i] = __ldg((const uint4 *)(src + tile_elem_off(srow, col_base + dl, D, C::W)));
     }
+    bool bad = false;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int u = dtid + i * kDq;
         const int row = u / upr, dl = (u - row * upr) * 8;
-        *(uint4 *)(sDst + tile_elem_off(row, dl, dD, C::W)) =
-            make_uint4(bf16x2_to_f16x2(v[i].x), bf16x2_to_f16x2(v[i].y), bf16x2_to_f16x2(v[i].z),
-                       bf16x2_to_f16x2(v[i].w));
+        const uint4 w = make_uint4(bf16x2_to_f16x2(v[i].x), bf16x2_to_f16x2(v[i].y), bf16x2_to_f16x2(v[i].z),
+                                   bf16x2_to_f16x2(v[i].w));
+        bad |= f16x8_has_inf(w);
+        *(uint4 *)(sDst + tile_elem_off(row, dl, dD, C::W)) = w;
     }
+    if (bad) report_error(p.status, DEV_ERR_F16_RANGE, 2, pl.b, j);
 }
 
 __device__ __forceinline__ void pair_fail(const AttnArgs &a, volatile int *abort, int where) {
@@ -772,6 +779,7 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
         // row (warp & 3) * 32 + lane; the two warps of a lane quarter take 8 of the 16 column blocks each
         const int rq = (warp & 3) * 32 + lane, hq = warp >> 2;
         const uint32_t taddr = tmem + (((uint32_t)((warp & 3) * 32)) << 16) + C::Q_COL;
+        bool q_bad = false;
 #pragma unroll 1
         for (int c = hq * 8; c < hq * 8 + 8; ++c) {
             const uint4 a0 = *(const uint4 *)(smem + rq * C::QSTR + c * 32);
@@ -780,9 +788,11 @@ __global__ void __launch_bounds__(PairCfg<Q8>::THREADS, 1)
             if (Q8) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
+                q_bad |= f16x8_has_inf(make_uint4(w[0], w[1], w[2], w[3])) | f16x8_has_inf(make_uint4(w[4], w[5], w[6], w[7]));
             }
             tmem_st8(taddr + (uint32_t)(c * 8), w);
         }
+        if (q_bad) report_error(a.pool.status, DEV_ERR_F16_RANGE, 0, pl.b, pl.qrow0);
         tmem_wait_st();
     }
     fence_proxy_async();

@@ -280,9 +280,12 @@ __device__ __forceinline__ void stage_q_store(const QStage<D, Q8> &qs, uint8_t *
     }
 }
 
+// Q row r (staged bf16) -> tensor memory; Q8_0 pools convert to f16, and the return value says whether
+// a value became inf (beyond the f16 range).
 template <int D, bool Q8>
-__device__ __forceinline__ void q_to_tmem(const uint8_t *stg, int r, uint32_t taddr, int c_lo, int c_hi) {
+__device__ __forceinline__ bool q_to_tmem(const uint8_t *stg, int r, uint32_t taddr, int c_lo, int c_hi) {
     using C = TcCfg<D, Q8>;
+    bool bad = false;
 #pragma unroll 1
     for (int c = c_lo; c < c_hi; ++c) {  // 16 elements = 8 columns per store
         const uint4 a0 = *(const uint4 *)(stg + q_stage_off(r, 2 * c, C::QSTR));
@@ -291,9 +294,11 @@ __device__ __forceinline__ void q_to_tmem(const uint8_t *stg, int r, uint32_t ta
         if (Q8) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
+            bad |= f16x8_has_inf(make_uint4(w[0], w[1], w[2], w[3])) | f16x8_has_inf(make_uint4(w[4], w[5], w[6], w[7]));
         }
         tmem_st8(taddr + (uint32_t)(c * 8), w);
     }
+    return bad;
 }
 
 // ---- bf16 feeder: one warp, one lane per segment (a block, or the suffix rows of the tile).
@@ -454,15 +459,18 @@ __device__ __forceinline__ void convert_suffix_part(const AttnArgs &a, const Pla
             v[i] = make_uint4(0, 0, 0, 0);
             if (u < UNITS && srow < p.suffix_rows) v[i] = __ldg((const uint4 *)(src + tile_elem_off(srow, d0, D, W)));
         }
+        bool bad = false;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int u = u0 + dtid + i * kDq;
             if (u >= UNITS) break;
             const int row = u / UPR, d0 = (u - row * UPR) * 8;
-            *(uint4 *)(sDst + tile_elem_off(row, d0, D, W)) =
-                make_uint4(bf16x2_to_f16x2(v[i].x), bf16x2_to_f16x2(v[i].y), bf16x2_to_f16x2(v[i].z),
-                           bf16x2_to_f16x2(v[i].w));
+            const uint4 w = make_uint4(bf16x2_to_f16x2(v[i].x), bf16x2_to_f16x2(v[i].y), bf16x2_to_f16x2(v[i].z),
+                                       bf16x2_to_f16x2(v[i].w));
+            bad |= f16x8_has_inf(w);
+            *(uint4 *)(sDst + tile_elem_off(row, d0, D, W)) = w;
         }
+        if (bad) report_error(p.status, DEV_ERR_F16_RANGE, 2, pl.b, j);
     }
 }
 
@@ -897,8 +905,9 @@ __global__ void __launch_bounds__(TcCfg<D, Q8>::THREADS, 1)
     if (warp < C::SMW) {
         // row (warp & 3) * 32 + lane; with SPLIT the H warps of a lane quarter share its column blocks
         const int h = C::SPLIT ? warp >> 2 : 0, nh = C::SPLIT_H;
-        q_to_tmem<D, Q8>(smem + C::OFF_V, (warp & 3) * 32 + lane, tmem + lane_base + C::Q_COL, h * (D / 16) / nh,
-                         (h + 1) * (D / 16) / nh);
+        if (q_to_tmem<D, Q8>(smem + C::OFF_V, (warp & 3) * 32 + lane, tmem + lane_base + C::Q_COL, h * (D / 16) / nh,
+                             (h + 1) * (D / 16) / nh))
+            report_error(a.pool.status, DEV_ERR_F16_RANGE, 0, pl.b, pl.qrow0);
         tmem_wait_st();
         fence_proxy_async();  // staging reads (generic) before the copy engine refills the V stages
         tc_fence_before();

@@ -41,7 +41,7 @@ def flex_meta_word(seq: int, frame: int, clean: bool) -> int:
 ALGO_TC, ALGO_SIMT, ALGO_TC_PAIR, ALGO_TC_CTA, ALGO_TC_PAIR64, ALGO_TC_HEADS = 0, 1, 2, 3, 4, 5
 
 # Device-side error codes written into the pool status word by kernels.
-DEV_ERR_BAD_BLOCK, DEV_ERR_BAD_SEQ, DEV_ERR_BAD_POS, DEV_ERR_TIMEOUT = 1, 2, 3, 4
+DEV_ERR_BAD_BLOCK, DEV_ERR_BAD_SEQ, DEV_ERR_BAD_POS, DEV_ERR_TIMEOUT, DEV_ERR_F16_RANGE = 1, 2, 3, 4, 5
 
 
 class PoolConfig(C.Structure):

@@ -363,3 +363,28 @@ def test_q8_0_attention_against_ggml_q8_0_path():
         v = np.concatenate([to_f32_np(f.pv[0][b, :n]), to_f32_np(f.sv[0][b, :50])])[None]
         want = oracle.attention_ggml_q8_0(to_f32_np(q[b:b + 1]), k, v, n, 1 / 16)
         check(got[b:b + 1], want, TOL[ekv.DTYPE_Q8_0])
+
+
+@pytest.mark.parametrize("algo,D", [(ekv.ALGO_TC, 256), (ekv.ALGO_TC_PAIR, 256), (ekv.ALGO_TC_CTA, 256),
+                                    (ekv.ALGO_TC, 128)])
+@pytest.mark.parametrize("where", ["q", "suffix"])
+def test_q8_0_f16_range_is_reported(algo, D, where):
+    """Q8_0 pools multiply in f16: a bf16 query or suffix value beyond the f16 range (65504) would become
+    inf there. Every tcgen05 kernel records DEV_ERR_F16_RANGE in the status word instead of returning
+    silently wrong rows; values inside the range leave the status clear."""
+    gen = torch.Generator().manual_seed(31)
+    f = Filled(dtype=ekv.DTYPE_Q8_0, B=2, prefix_lens=[90, 130], Hkv=1, D=D, suffix_len=20, seed=31)
+    q = bf16_randn(gen, (2, 20, 8, D))
+    run_attention(f, 0, q, Hq=8, scale=D ** -0.5, algo=algo)  # in range: status clear (checked inside)
+    if where == "q":
+        q[1, 3, 2, 7] = 1.0e5
+    else:
+        big = f.sk[0].clone()
+        big[0, 5, 0, 11] = -2.0e5
+        f.pool.append_suffix(0, f.seq_ids, big[:, :20].contiguous().cuda(), f.sv[0][:, :20].contiguous().cuda())
+    prm = f.pool.attention_params(layer=0, seq_ids=f.seq_ids, q_tokens=20, q_heads=8, scale=D ** -0.5,
+                                  suffix_len=20, out_dtype=ekv.DTYPE_F32)
+    out = torch.empty((2, 20, 8, D), dtype=torch.float32, device="cuda")
+    f.pool.attention(prm, q.cuda().contiguous(), out, algo=algo)
+    torch.cuda.synchronize()
+    assert f.pool.status() == ekv.DEV_ERR_F16_RANGE
