@@ -17,7 +17,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libekv.so")
 BUILD_DIR = os.path.join(HERE, "_build")
-SOURCES = ["ekv_capi.cpp", "ekv_sched.cpp", "ekv_cache_kernels.cu", "ekv_attn_simt.cu", "ekv_attn_tc.cu", "ekv_attn_pair.cu", "ekv_attn_pair128.cu", "ekv_attn_heads.cu", "ekv_noalloc.cu", "ekv_ggml_fa.cu", "ekv_ggml_tc.cu", "ekv_flow.cu"]
+SOURCES = ["ekv_capi.cpp", "ekv_sched.cpp", "ekv_cache_kernels.cu", "ekv_attn_simt.cu", "ekv_attn_tc.cu", "ekv_attn_pair.cu", "ekv_attn_pair128.cu", "ekv_attn_heads.cu", "ekv_noalloc.cu", "ekv_ggml_fa.cu", "ekv_ggml_tc.cu", "ekv_flow.cu", "ekv_project.cu"]
 HEADERS = ["ekv_internal.h", "ekv_layout.cuh", "ekv_device.cuh", "ekv_sm100.cuh", "ekv_attn_common.cuh", "ekv_ggml.h"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -573,6 +573,31 @@ int ekv_attention(ekv_pool *p, const ekv_attn_params *prm, const void *q, void *
     return ekv_attention_algo(p, prm, q, out, workspace, workspace_bytes, EKV_ALGO_TC, stream);
 }
 
+int ekv_project_qkv_rope(ekv_pool *p, int32_t layer, int32_t n_batch, const int32_t *seq_ids, int32_t tokens,
+                         int32_t q_heads, int32_t hidden, const void *x, const void *wq, const void *wk, const void *wv,
+                         const int32_t *positions, float rope_base, void *q_out, void *k_out, void *v_out,
+                         ekv_stream_t stream) {
+    if (!p || !x || !wq || !wk || !wv || !positions || !q_out) return EKV_ERR_INVALID_ARG;
+    if ((k_out == nullptr) != (v_out == nullptr)) return EKV_ERR_INVALID_ARG;
+    const ekv_pool_config &c = p->cfg;
+    if (layer < 0 || layer >= c.n_layers || n_batch <= 0 || tokens <= 0 || q_heads <= 0 || q_heads % c.kv_heads)
+        return EKV_ERR_INVALID_ARG;
+    if (hidden <= 0 || hidden % 64 || !(rope_base > 0.0f) || !std::isfinite(rope_base)) return EKV_ERR_INVALID_ARG;
+    if ((int64_t)n_batch * tokens > INT_MAX / 2) return EKV_ERR_INVALID_ARG;
+    if (((uintptr_t)x | (uintptr_t)wq | (uintptr_t)wk | (uintptr_t)wv | (uintptr_t)q_out | (uintptr_t)k_out |
+         (uintptr_t)v_out) & 15)
+        return EKV_ERR_INVALID_ARG;
+    if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return EKV_ERR_UNSUPPORTED;
+    if (!k_out) {  // into the suffix slots
+        if (!seq_ids || c.suffix_tokens == 0) return EKV_ERR_INVALID_ARG;
+        if (tokens > c.suffix_tokens) return EKV_ERR_RANGE;
+    }
+    const DeviceScope dev_scope(p);
+    if (const int e = dev_scope.rc()) return e;
+    return ekv::launch_project_qkv(p->view, layer, n_batch, seq_ids, tokens, q_heads, hidden, x, wq, wk, wv, positions,
+                                   rope_base, q_out, k_out, v_out, (cudaStream_t)stream);
+}
+
 int ekv_append_suffix_attention(ekv_pool *p, const ekv_attn_params *prm, const void *k_suffix,
                                 const void *v_suffix, const void *q, void *out, void *workspace,
                                 size_t workspace_bytes, ekv_stream_t stream) {

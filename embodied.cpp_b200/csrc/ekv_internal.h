@@ -106,6 +106,11 @@ int pair128_choose_splits(int64_t pair_units, int max_tiles, int sms);
 bool heads_fits(const AttnArgs &a);
 int heads_units(const AttnArgs &a);
 int launch_attention_heads(const AttnArgs &a, cudaStream_t s, int sms);
+// Q/K/V projection of one layer-step with RoPE NEOX (ekv_project.cu); k_out == nullptr writes K and V
+// into the suffix slots of (seq_ids[b], layer)
+int launch_project_qkv(const PoolView &p, int layer, int n_batch, const int32_t *seq_ids, int tokens, int q_heads,
+                       int hidden, const void *x, const void *wq, const void *wk, const void *wv, const int32_t *positions,
+                       float rope_base, void *q_out, void *k_out, void *v_out, cudaStream_t s);
 // combine key-split partial outputs (head_dim of the pool) into a.out
 int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s);
 #ifdef EKV_TRACE

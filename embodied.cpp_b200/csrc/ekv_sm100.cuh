@@ -441,6 +441,13 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const void *map, int c
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *map, int c0, int c1, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void *map, int c0, int c1, int c2, int c3, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "

@@ -97,7 +97,7 @@ EXPORTED = [
     "ekv_mul_mat_soft_max_mul_mat", "ekv_flash_attn_ext_workspace_size", "ekv_flash_attn_ext_ws",
     "ekv_mul_mat_soft_max_mul_mat_workspace_size", "ekv_mul_mat_soft_max_mul_mat_ws", "ekv_append_suffix_attention", "ekv_launch_count", "ekv_debug_expire_wait",
     "ekv_flow_step_f32", "ekv_guidance_f32", "ekv_sched_create", "ekv_sched_destroy", "ekv_sched_submit",
-    "ekv_sched_begin_tick", "ekv_sched_end_tick", "ekv_sched_stats",
+    "ekv_sched_begin_tick", "ekv_sched_end_tick", "ekv_sched_stats", "ekv_project_qkv_rope",
 ]
 NOALLOC_SCRATCH_BYTES = 16 << 20  # EKV_NOALLOC_SCRATCH_BYTES
 
@@ -153,6 +153,8 @@ def _load():
                                                         C.c_size_t),
         "ekv_mul_mat_soft_max_mul_mat_ws": ([C.POINTER(Tensor)] * 4 + [C.c_float] * 2 + [C.POINTER(Tensor), vp,
                                                                                          C.c_size_t, vp], C.c_int),
+        "ekv_project_qkv_rope": ([vp, i32, i32, vp, i32, i32, i32, vp, vp, vp, vp, vp, C.c_float, vp, vp, vp, vp],
+                                 C.c_int),
         "ekv_version": ([], C.c_char_p),
         "ekv_launch_count": ([], C.c_uint64),
         "ekv_strerror": ([C.c_int], C.c_char_p),
@@ -321,6 +323,18 @@ class Pool:
         check(lib.ekv_append_suffix_attention(self.h, C.byref(params), _ptr(k_suffix), _ptr(v_suffix), _ptr(q),
                                               _ptr(out), _ptr(workspace), ws_bytes, _stream(stream)),
               "ekv_append_suffix_attention")
+
+
+def project_qkv_rope(pool: "Pool", layer, seq_ids, x, wq, wk, wv, positions, rope_base, q_out, k_out=None, v_out=None,
+                     *, tokens, q_heads, stream=None):
+    """ekv_project_qkv_rope: x [n_batch * tokens, hidden] bf16, weights [out, hidden] bf16, positions int32
+    [n_batch * tokens]; q_out [n_batch, tokens, q_heads, head_dim] bf16; K/V into the pool's suffix slots
+    (k_out / v_out None) or into k_out / v_out [n_batch, tokens, kv_heads, head_dim] bf16."""
+    rows, hidden = x.shape
+    n_batch = rows // tokens
+    check(lib.ekv_project_qkv_rope(pool.h, layer, n_batch, _ptr(seq_ids), tokens, q_heads, hidden, _ptr(x), _ptr(wq),
+                                   _ptr(wk), _ptr(wv), _ptr(positions), rope_base, _ptr(q_out), _ptr(k_out),
+                                   _ptr(v_out), _stream(stream)), "ekv_project_qkv_rope")
 
 
 class DevArray:

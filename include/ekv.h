@@ -279,6 +279,22 @@ int ekv_append_suffix_attention(ekv_pool *pool, const ekv_attn_params *p, const 
                                 const void *v_suffix, const void *q, void *out, void *workspace,
                                 size_t workspace_bytes, ekv_stream_t stream);
 
+/* ---- the layer-step's Q/K/V projection with RoPE, K/V straight into the pool ----
+ * Replaces, per layer-step, models/pi05.cpp:391-407 (and :299-318 for the prefix layers' shape): q, k, v =
+ * mul_mat(Wq | Wk | Wv, x_norm) over bf16 weights in ggml's layout ([rows of hidden], q_heads * head_dim,
+ * kv_heads * head_dim and kv_heads * head_dim rows) and bf16 activations x [n_batch * tokens][hidden]
+ * (row b * tokens + t), f32 accumulation; ggml_rope_ext in NEOX mode (freq_base rope_base, no scaling) on q
+ * and k at positions[b * tokens + t]; results rounded to bf16. q goes to q_out [n_batch][tokens][q_heads]
+ * [head_dim]. With k_out and v_out NULL, K and V go into the suffix slot rows 0 .. tokens - 1 of
+ * (seq_ids[b], layer) -- the rows ekv_append_suffix writes, read by ekv_attention with suffix_len = tokens;
+ * otherwise into k_out / v_out [n_batch][tokens][kv_heads][head_dim] (the buffers of
+ * ekv_append_suffix_attention). head_dim 64, 128 or 256; hidden a multiple of 64; pointers 16-byte
+ * aligned. */
+int ekv_project_qkv_rope(ekv_pool *pool, int32_t layer, int32_t n_batch, const int32_t *seq_ids, int32_t tokens,
+                         int32_t q_heads, int32_t hidden, const void *x, const void *wq, const void *wk, const void *wv,
+                         const int32_t *positions, float rope_base, void *q_out, void *k_out, void *v_out,
+                         ekv_stream_t stream);
+
 /* ---- ggml op surface: GGML_OP_FLASH_ATTN_EXT on strided device tensors ----
  * Replaces ggml_flash_attn_ext (models/hy_vla.cpp:376-378, :439-441, :460, :492, :859 (GQA, mask);
  * models/lingbot_va.cpp:1263-1266) for a ggml backend that routes the op here: the tensors keep

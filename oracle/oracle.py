@@ -336,3 +336,44 @@ def guidance(cond, uncond, scale, use_guidance=True, bf16_round=False):
     d = (c - u).astype(np.float32)
     v = (u + (np.float32(scale) * d).astype(np.float32)).astype(np.float32)
     return rnd(v)
+
+
+def rope_neox(x: np.ndarray, pos: np.ndarray, base: float) -> np.ndarray:
+    """RoPE in ggml's NEOX mode as models/pi05.cpp:391-401 applies it (ggml_rope_ext(t, positions, n_dims =
+    head_dim, GGML_ROPE_TYPE_NEOX, n_ctx_orig 0, freq_base rope_base, freq_scale 1, ext_factor 0,
+    attn_factor 1)): ggml (llama.cpp b9016, an absent dependency) keeps theta in float32, starting at the
+    token's position and multiplied by theta_scale = base^(-2/n_dims) after every dimension pair; pair i
+    rotates dims i and i + n_dims/2 by theta: (x0 cos - x1 sin, x0 sin + x1 cos). x: [rows, ..., D] float32,
+    pos: [rows] int. Returns float32."""
+    x = np.asarray(x, np.float32)
+    d = x.shape[-1]
+    h = d // 2
+    theta_scale = np.float32(np.power(np.float32(base), np.float32(-2.0 / d), dtype=np.float32))
+    theta = np.asarray(pos, np.float32).reshape((-1,) + (1,) * (x.ndim - 2))
+    out = np.empty_like(x)
+    for i in range(h):
+        c = np.cos(theta).astype(np.float32)
+        s = np.sin(theta).astype(np.float32)
+        x0, x1 = x[..., i], x[..., i + h]
+        out[..., i] = x0 * c - x1 * s
+        out[..., i + h] = x0 * s + x1 * c
+        theta = (theta * theta_scale).astype(np.float32)
+    return out
+
+
+def project_qkv_rope(x, wq, wk, wv, pos, base, q_heads, kv_heads):
+    """The action expert's q/k/v projection of one layer-step with RoPE (models/pi05.cpp:391-401):
+    q = mul_mat(Wq, x), k = mul_mat(Wk, x), v = mul_mat(Wv, x) over bf16 weights [out][hidden] and bf16
+    activations (ggml's bf16 mul_mat rounds the f32 activations to bf16), f32 dot products; RoPE NEOX on q
+    and k at the tokens' positions; returned as float32 values of the bf16 results (q [rows, Hq, D],
+    k and v [rows, Hkv, D])."""
+    xf = np.asarray(x, np.float32)
+    d = np.asarray(wq).shape[0] // q_heads
+    rows = xf.shape[0]
+    q = (xf @ np.asarray(wq, np.float32).T).reshape(rows, q_heads, d)
+    k = (xf @ np.asarray(wk, np.float32).T).reshape(rows, kv_heads, d)
+    v = (xf @ np.asarray(wv, np.float32).T).reshape(rows, kv_heads, d)
+    q = rope_neox(q, pos, base)
+    k = rope_neox(k, pos, base)
+    r = lambda a: bf16_to_f32(f32_to_bf16(np.ascontiguousarray(a, np.float32)))
+    return r(q), r(k), r(v)

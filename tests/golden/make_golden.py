@@ -15,6 +15,10 @@ Sources of truth, none of them this repository's own code:
   * LingBot-VA flex masks: the token metadata of build_flex_mask_meta and the dense masks of
     flex_self_allowed / flex_cross_allowed (models/lingbot_va.cpp:9283-9348) restated over Python
     lists for three small layouts.
+  * Rotary position embedding in the split-halves (NEOX) convention: the installed transformers
+    package's Gemma helpers (rotate_half, apply_rotary_pos_emb) in float64, with the frequencies
+    1 / base^(2i / head_dim) of its Gemma rotary embedding -- the convention ggml_rope_ext's
+    GGML_ROPE_TYPE_NEOX mode implements (models/pi05.cpp:391-401).
 
 Usage:  python tests/golden/make_golden.py      (writes *.npz next to this file)
 """
@@ -220,6 +224,23 @@ def lingbot_flex():
     return out
 
 
+def rope_neox():
+    import torch
+    from transformers.models.gemma.modeling_gemma import apply_rotary_pos_emb
+
+    rng = np.random.default_rng(20260303)
+    base, d = 10000.0, 32
+    pos = np.array([0, 1, 7, 50, 816, 865], np.int64)
+    x = rng.standard_normal((len(pos), 3, d)).astype(np.float32)
+    inv_freq = 1.0 / (base ** (np.arange(0, d, 2, dtype=np.float64) / d))
+    ang = pos[:, None].astype(np.float64) * inv_freq[None, :]
+    emb = np.concatenate([ang, ang], axis=-1)
+    cos, sin = torch.tensor(np.cos(emb)), torch.tensor(np.sin(emb))  # [rows, d]
+    xt = torch.tensor(x.astype(np.float64))                            # [rows, heads, d]
+    out, _ = apply_rotary_pos_emb(xt, xt, cos, sin, unsqueeze_dim=1)
+    return dict(x=x, pos=pos.astype(np.int32), base=np.float64(base), out=out.numpy())
+
+
 def main():
     np.savez_compressed(os.path.join(HERE, "q8_0_gguf.npz"), **q8_0_vectors())
     np.savez_compressed(os.path.join(HERE, "bf16_gguf.npz"), **bf16_vectors())
@@ -227,6 +248,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "lingbot_smoke.npz"), **lingbot_smoke())
     np.savez_compressed(os.path.join(HERE, "mask_builders.npz"), **mask_builders())
     np.savez_compressed(os.path.join(HERE, "lingbot_flex.npz"), **lingbot_flex())
+    np.savez_compressed(os.path.join(HERE, "rope_neox.npz"), **rope_neox())
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

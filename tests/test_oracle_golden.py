@@ -160,3 +160,14 @@ def test_flex_meta_word_packing_matches_library_binding():
     import ekv
     for seq, frame, clean in [(-1, 5, 1), (0, 0, 0), (0, 7, 1), (3, 123456, 0), (254, (1 << 23) - 1, 1)]:
         assert ekv.flex_meta_word(seq, frame, clean) == oracle.flex_meta_word(seq, frame, clean)
+
+
+def test_rope_neox_matches_transformers_golden():
+    """The oracle's RoPE (ggml NEOX mode, float32 theta multiplied by base^(-2/D) per dimension pair) against
+    transformers' Gemma rotate-half rotation evaluated in float64 (tests/golden/rope_neox.npz): the same
+    convention; the float32 angle recurrence accounts for differences up to a few 1e-5 at position 865."""
+    g = np.load(os.path.join(GOLD, "rope_neox.npz"))
+    got = oracle.rope_neox(g["x"], g["pos"], float(g["base"]))
+    np.testing.assert_allclose(got, g["out"], rtol=0, atol=1e-4)
+    # position 0 is the identity; dimension pairs are (i, i + D/2)
+    np.testing.assert_array_equal(got[0], g["x"][0])
