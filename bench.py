@@ -56,6 +56,10 @@ OTHER_CONFIGS = {
                        desc="GR00T-N1.7 DiT action head: 16 layers (even: cross-attention of 17 queries to a cached "
                             "300-token backbone K/V, image span [0,256) and text [256,300) masks alternating; odd: "
                             "self-attention among the 17), 4 denoise steps, 32 heads x 48 (MHA), bf16, batch 128"),
+    "pi05_proj_b64": dict(kind="proj", batch=64,
+                          desc="pi0.5 action-expert Q/K/V projection + RoPE NEOX per layer-step, K/V into the pool's "
+                               "suffix slots: batch 64 x 50 tokens, hidden 1024, 8q/1kv x 256, 18 layers per step, "
+                               "bf16 weights and activations, f32 accumulation"),
     "lingbot_b1": dict(kind="lingbot", batch=1,
                        desc="LingBot-VA rollout: 30 layers, 24 heads x 128 (MHA), 16 chunks of 1560 video tokens "
                             "appended to a paged bf16 cache (64-token blocks, chunk stride 1600), block-causal "
@@ -363,6 +367,49 @@ class LingbotWorkload:
                 self.pool.attention(self.params[w][l], self.q[i, l], self.out[i, l], workspace=self.ws, stream=stream)
 
 
+class ProjWorkload:
+    """The expert's per-layer-step Q/K/V projection with RoPE (ekv_project_qkv_rope) on the pi0.5 shape: 64
+    requests x 50 action tokens, hidden 1024, 8 query heads and 1 KV head of 256, RoPE base 10000 at positions
+    n_prefix + i, K/V written into the pool's suffix slots. One step = one denoise step (18 layer-steps, each
+    with its own bf16 weights). Random-init weights N(0, 1/hidden), activations N(0,1) x 0.5."""
+    L, T, HID, HQ, HKV, D = 18, 50, 1024, 8, 1, 256
+    graphable = True
+
+    def __init__(self, B, device):
+        import torch
+        import ekv
+        self.ekv, self.B = ekv, B
+        L, T, HID, HQ, HKV, D = self.L, self.T, self.HID, self.HQ, self.HKV, self.D
+        self.pool = ekv.Pool(device=device, dtype=ekv.DTYPE_Q8_0, block_tokens=16, n_blocks=B, kv_heads=HKV,
+                             head_dim=D, n_layers=L, max_seqs=B, max_blocks_per_seq=1, suffix_tokens=T)
+        self.seqs = [self.pool.seq_create() for _ in range(B)]
+        self.pool.sync()
+        dev = f"cuda:{device}"
+        self.seq_ids = torch.tensor(np.asarray(self.seqs, np.int32), device=dev)
+        g = torch.Generator(device=dev).manual_seed(5)
+        rn = lambda sc, *shape: (torch.randn(shape, generator=g, device=dev) * sc).to(torch.bfloat16)
+        ws = HID ** -0.5
+        self.wq, self.wk, self.wv = rn(ws, L, HQ * D, HID), rn(ws, L, HKV * D, HID), rn(ws, L, HKV * D, HID)
+        self.x = rn(0.5, L, B * T, HID)  # > L2 together with the weights and outputs per step
+        rng = np.random.default_rng(5)
+        plens = rng.integers(700, 817, size=B)
+        self.pos = torch.tensor(np.concatenate([np.arange(T) + p for p in plens]).astype(np.int32), device=dev)
+        self.q = torch.empty((L, B, T, HQ, D), dtype=torch.bfloat16, device=dev)
+        self.n_calls = L
+        self.flop_per_call = 2.0 * B * T * (HQ + 2 * HKV) * D * HID
+        self.bytes_per_call = 2.0 * (B * T * HID + (HQ + 2 * HKV) * D * HID + B * T * (HQ + 2 * HKV) * D)
+        self.qtok_per_step = B * T * L
+        self.ws = None
+
+    def step_prefix(self, stream):
+        pass
+
+    def step_calls(self, stream):
+        for l in range(self.L):
+            self.ekv.project_qkv_rope(self.pool, l, self.seq_ids, self.x[l], self.wq[l], self.wk[l], self.wv[l],
+                                      self.pos, 10000.0, self.q[l], tokens=self.T, q_heads=self.HQ, stream=stream)
+
+
 class ServeWorkload:
     """a stream of pi0.5-shaped Q8_0 requests (prefix U[600, 1000], 50 action
     tokens, 10 denoise steps, 18 layers) served by the library's batching scheduler (ekv_sched_*)
@@ -541,7 +588,7 @@ def run_other(args, cfg):
         from datetime import timedelta
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                                 device_id=torch.device(f"cuda:{local}"))
-    cls = GrootWorkload if cfg["kind"] == "groot" else LingbotWorkload
+    cls = {"groot": GrootWorkload, "lingbot": LingbotWorkload, "proj": ProjWorkload}[cfg["kind"]]
     wl = cls(cfg["batch"], local)
     stream = torch.cuda.current_stream()
     wl.step_prefix(stream)
@@ -600,17 +647,20 @@ def run_other(args, cfg):
         ach = wl.bytes_per_call / call_s / 1e9
         roof = {"bound": bound, "achieved": ach, "peak": peaks["hbm"], "unit": "GB/s", "frac": ach / peaks["hbm"]}
     roof.update({"traffic": None, "peak_source": peaks["source"], "avg_launch_us": call_s * 1e6,
-                 "kernel": ("attn_heads_kernel (four heads of a request per unit, persistent CTAs)"
-                            if cfg["kind"] == "groot" else "attn_tc_kernel (one CTA per 128 query rows)"),
+                 "kernel": {"groot": "attn_heads_kernel (four heads of a request per unit, persistent CTAs)",
+                            "lingbot": "attn_tc_kernel (one CTA per 128 query rows)",
+                            "proj": "project_qkv_kernel<256> (tcgen05 GEMM, RoPE + slot-write epilogue)"}[cfg["kind"]],
                  "algorithmic_per_launch": {"flop": wl.flop_per_call, "bytes": wl.bytes_per_call},
                  "timed": "CUDA events around each step's layer-calls, divided by the calls (appends included "
                           "for the LingBot chunks)"})
-    line = {"metric": METRIC, "value": world * wl.qtok_per_step * args.steps / (ms / 1e3), "unit": "query-tok/s",
+    metric = "denoise qkv-projection tok/s" if cfg["kind"] == "proj" else METRIC
+    line = {"metric": metric, "value": world * wl.qtok_per_step * args.steps / (ms / 1e3),
+            "unit": "tok/s" if cfg["kind"] == "proj" else "query-tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 MMA, f32 accumulate",
             "data": "synthetic", "config": {"workload": args.config, "description": cfg["desc"],
                                             "batch_per_gpu": wl.B,
-                                            "parallelism": f"{'request' if cfg['kind'] == 'groot' else 'episode'}"
+                                            "parallelism": f"{'episode' if cfg['kind'] == 'lingbot' else 'request'}"
                                                            f"-sharded x{world}"},
             "roofline": roof, "clocks": clk, "gpu_launches": int(launches), "device_status": wl.pool.status()}
     if world > 1:

@@ -8,7 +8,9 @@
 // so that the attention that follows (ekv_attention over the slot, or ekv_append_suffix_attention over
 // the row-major K/V) reads the step's keys without a separate append.
 //
-// One CTA computes 128 token rows x one head (D columns) of [q | k | v] = x W^T: the copy engine loads
+// A tile is 128 token rows x one head (D columns) of [q | k | v] = x W^T; persistent CTAs (one per SM) walk
+// the tiles with two accumulators in tensor memory, so a tile's epilogue runs under the next tile's
+// MMAs. For each tile the copy engine loads
 // 128 x 64 tiles of x and D x 64 tiles of the head's weight rows (both K-major, 128-byte swizzled)
 // through tensor maps into a ring of stages; one thread issues tcgen05.mma (M = 128, N = D, K = 16,
 // bf16, f32 accumulation in tensor memory); eight epilogue warps (two per TMEM lane quarter, thread =
@@ -68,6 +70,7 @@ struct PCfg {
     // half of the dimension pairs)
     static constexpr int THREADS = 320;
     static_assert(NS >= 3, "stage ring");
+    static_assert((2 * NS + 7) * 8 <= 256, "barrier block");
     static_assert(SMEM <= 232448, "shared-memory budget");
 };
 
@@ -82,31 +85,40 @@ struct ProjArgs {
 
 template <int D>
 __global__ void __launch_bounds__(PCfg<D>::THREADS, 1)
-    project_qkv_kernel(const ProjArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wqmap,
-                       const __grid_constant__ CUtensorMap wkmap, const __grid_constant__ CUtensorMap wvmap) {
+    project_qkv_kernel(const ProjArgs a, int m_tiles, const __grid_constant__ CUtensorMap xmap,
+                       const __grid_constant__ CUtensorMap wqmap, const __grid_constant__ CUtensorMap wkmap,
+                       const __grid_constant__ CUtensorMap wvmap) {
     using C = PCfg<D>;
     constexpr int NS = C::NS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = (uint64_t *)(smem + C::OFF_BAR);
-    uint32_t *tmem_holder = (uint32_t *)(bars + 2 * NS + 1);
-    volatile int *abort = (volatile int *)(bars + 2 * NS + 2);
+    uint32_t *tmem_holder = (uint32_t *)(bars + 2 * NS + 5);
+    volatile int *abort = (volatile int *)(bars + 2 * NS + 6);
     const uint32_t bar0 = smem_addr(bars);
-    auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };  // full [0, NS), empty [NS, 2NS), done 2NS
+    // full [0, NS), empty [NS, 2NS), accumulator full 2NS + {0, 1}, accumulator empty 2NS + 2 + {0, 1},
+    // every MMA of the CTA finished 2NS + 4
+    auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int m0 = blockIdx.x * kPBM, hh = blockIdx.y;
     const int KT = a.hidden / kPBK;
+    const int n_tiles = m_tiles * (a.q_heads + 2 * a.kv_heads);
+    // this CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...; tile t = (token rows m, head hh) with m fastest
+    const int U = ((int)blockIdx.x < n_tiles) ? (n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(bar(s), 1);
             mbar_init(bar(NS + s), 1);
         }
-        mbar_init(bar(2 * NS), 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar(2 * NS + i), 1);
+            mbar_init(bar(2 * NS + 2 + i), 8);
+        }
+        mbar_init(bar(2 * NS + 4), 1);
         *abort = 0;
         mbar_init_fence();
     }
-    if (warp == 1) tmem_alloc(smem_addr(tmem_holder), D);
+    if (warp == 1) tmem_alloc(smem_addr(tmem_holder), 2 * D);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -114,19 +126,26 @@ __global__ void __launch_bounds__(PCfg<D>::THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            const CUtensorMap *wm = hh < a.q_heads ? &wqmap : (hh < a.q_heads + a.kv_heads ? &wkmap : &wvmap);
-            const int wrow = (hh < a.q_heads ? hh : (hh < a.q_heads + a.kv_heads ? hh - a.q_heads : hh - a.q_heads - a.kv_heads)) * D;
-            for (int k = 0; k < KT; ++k) {
-                const int s = k % NS;
-                if (k >= NS && !mbar_wait(bar(NS + s), (uint32_t)(k / NS - 1) & 1u, abort, a.wait_budget)) {
-                    *abort = 1;
-                    report_error(a.pool.status, DEV_ERR_TIMEOUT, 30, blockIdx.x, hh);
-                    break;
+            int kc = 0;
+            bool ok = true;
+            for (int i = 0; ok && i < U; ++i) {
+                const int tile = (int)blockIdx.x + i * (int)gridDim.x, m0 = (tile % m_tiles) * kPBM, hh = tile / m_tiles;
+                const CUtensorMap *wm = hh < a.q_heads ? &wqmap : (hh < a.q_heads + a.kv_heads ? &wkmap : &wvmap);
+                const int wrow =
+                    (hh < a.q_heads ? hh : (hh < a.q_heads + a.kv_heads ? hh - a.q_heads : hh - a.q_heads - a.kv_heads)) * D;
+                for (int k = 0; k < KT; ++k, ++kc) {
+                    const int s = kc % NS;
+                    if (kc >= NS && !(ok = mbar_wait(bar(NS + s), (uint32_t)(kc / NS - 1) & 1u, abort, a.wait_budget)))
+                        break;
+                    const uint32_t st = smem_addr(smem + s * C::STAGE);
+                    mbar_arrive_expect_tx(bar(s), (uint32_t)C::STAGE);
+                    tma_load_2d(st, &xmap, k * kPBK, m0, bar(s));
+                    tma_load_2d(st + C::A_BYTES, wm, k * kPBK, wrow, bar(s));
                 }
-                const uint32_t st = smem_addr(smem + s * C::STAGE);
-                mbar_arrive_expect_tx(bar(s), (uint32_t)C::STAGE);
-                tma_load_2d(st, &xmap, k * kPBK, m0, bar(s));
-                tma_load_2d(st + C::A_BYTES, wm, k * kPBK, wrow, bar(s));
+            }
+            if (!ok) {
+                *abort = 1;
+                report_error(a.pool.status, DEV_ERR_TIMEOUT, 30, blockIdx.x, 0);
             }
         }
         __syncwarp();
@@ -134,104 +153,124 @@ __global__ void __launch_bounds__(PCfg<D>::THREADS, 1)
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(true, false, D);
             bool ok = true;
-            for (int k = 0; k < KT && ok; ++k) {
-                const int s = k % NS;
-                if (!(ok = mbar_wait(bar(s), (uint32_t)(k / NS) & 1u, abort, a.wait_budget))) break;
+            int kc = 0;
+            for (int i = 0; ok && i < U; ++i) {
+                const uint32_t acc = tmem + (uint32_t)((i & 1) * D);
+                // the epilogue has read this accumulator's previous tile
+                if (i >= 2 && !(ok = mbar_wait(bar(2 * NS + 2 + (i & 1)), (uint32_t)((i - 2) >> 1) & 1u, abort, a.wait_budget)))
+                    break;
                 tc_fence_after();
-                const uint32_t st = smem_addr(smem + s * C::STAGE);
-                const uint64_t ad = sdesc(st, 16, 1024, 2u), bd = sdesc(st + C::A_BYTES, 16, 1024, 2u);
-                const uint64_t av[4] = {ad, ad + 2, ad + 4, ad + 6};  // K steps of 32 bytes in the 128-byte rows
-                const uint64_t bv[4] = {bd, bd + 2, bd + 4, bd + 6};
-                mma_ss_x4<false>(tmem, av, bv, idesc, k > 0 ? 1u : 0u);
-                mma_commit(bar(NS + s));
+                for (int k = 0; k < KT; ++k, ++kc) {
+                    const int s = kc % NS;
+                    if (!(ok = mbar_wait(bar(s), (uint32_t)(kc / NS) & 1u, abort, a.wait_budget))) break;
+                    tc_fence_after();
+                    const uint32_t st = smem_addr(smem + s * C::STAGE);
+                    const uint64_t ad = sdesc(st, 16, 1024, 2u), bd = sdesc(st + C::A_BYTES, 16, 1024, 2u);
+                    const uint64_t av[4] = {ad, ad + 2, ad + 4, ad + 6};  // K steps of 32 bytes in the 128-byte rows
+                    const uint64_t bv[4] = {bd, bd + 2, bd + 4, bd + 6};
+                    mma_ss_x4<false>(acc, av, bv, idesc, k > 0 ? 1u : 0u);
+                    mma_commit(bar(NS + s));
+                }
+                if (ok) mma_commit(bar(2 * NS + (i & 1)));  // this tile's accumulator is complete
             }
             if (!ok) {
                 *abort = 1;
-                report_error(a.pool.status, DEV_ERR_TIMEOUT, 31, blockIdx.x, hh);
+                report_error(a.pool.status, DEV_ERR_TIMEOUT, 31, blockIdx.x, 0);
             }
-            mma_commit(bar(2 * NS));
+            mma_commit(bar(2 * NS + 4));  // every MMA of the CTA finished before teardown
+            mbar_wait_drain(bar(2 * NS + 4), 0u, a.wait_budget);
         }
         __syncwarp();
     } else {
-        // ---- epilogue: thread = token row 32 (warp & 3) + lane of the tile; warps 2-5 take dimension pairs
+        // ---- epilogue: thread = token row 32 (warp & 3) + lane of a tile; warps 2-5 take dimension pairs
         // [0, D/4), warps 6-9 pairs [D/4, D/2) ----
         const int q4 = warp & 3, part = (warp - 2) >> 2;
         const uint32_t lb = ((uint32_t)(32 * q4)) << 16;
-        const int grow = m0 + 32 * q4 + lane;
-        const bool row_ok = grow < a.rows;
-        const bool done = mbar_wait(bar(2 * NS), 0u, abort, a.wait_budget);
-        if (!done && lane == 0) report_error(a.pool.status, DEV_ERR_TIMEOUT, 32, blockIdx.x, hh);
-        tc_fence_after();
-        const bool is_q = hh < a.q_heads, is_k = !is_q && hh < a.q_heads + a.kv_heads;
-        const bool rope = is_q || is_k;
-        const int g = is_q ? 0 : (is_k ? hh - a.q_heads : hh - a.q_heads - a.kv_heads);
-        const int b = row_ok ? grow / a.tokens : 0, t = row_ok ? grow - b * a.tokens : 0;
-        float theta = row_ok ? (float)a.positions[grow] : 0.0f;
-        // the angle of this warp's first pair: ggml's float32 recurrence, advanced over the other part's pairs
-        for (int i = 0; i < part * (D / 4); ++i) theta = __fmul_rn(theta, a.theta_scale);
-        // destination of this row: q_out row, a suffix-slot tile row (swizzled), or a row-major K / V row
-        uint8_t *dst = nullptr;
-        bool slot = false;
-        if (row_ok && done) {
-            if (is_q) {
-                dst = (uint8_t *)(a.q_out + ((int64_t)grow * a.q_heads + hh) * D);
-            } else if (a.to_slot) {
-                const int seq = a.seq_ids[b];
-                if (seq < 0 || seq >= a.pool.max_seqs) {
-                    report_error(a.pool.status, DEV_ERR_BAD_SEQ, b, seq, 6);
-                } else {
-                    dst = a.pool.suffix + suffix_tile_index(a.pool, a.layer, seq, is_k ? 0 : 1, g) * a.pool.suffix_tile_bytes;
-                    slot = true;
-                }
-            } else {
-                dst = (uint8_t *)((is_k ? a.k_out : a.v_out) + ((int64_t)grow * a.kv_heads + g) * D);
-            }
-        }
         const int W = a.pool.swz_bytes;
-#pragma unroll 1
-        for (int c0 = part * (D / 4); c0 < (part + 1) * (D / 4); c0 += 16) {
-            uint32_t lo[16], hi[16];
-            tmem_load16x2(tmem + lb + (uint32_t)c0, tmem + lb + (uint32_t)(c0 + D / 2), lo, hi);
-            float o0[16], o1[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const float x0 = __uint_as_float(lo[i]), x1 = __uint_as_float(hi[i]);
-                if (rope) {
-                    float sn, cs;
-                    rope_sincos(theta, sn, cs);
-                    o0[i] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-                    o1[i] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-                    theta = __fmul_rn(theta, a.theta_scale);
+        for (int i = 0; i < U; ++i) {
+            const int tile = (int)blockIdx.x + i * (int)gridDim.x, m0 = (tile % m_tiles) * kPBM, hh = tile / m_tiles;
+            const bool done = mbar_wait(bar(2 * NS + (i & 1)), (uint32_t)(i >> 1) & 1u, abort, a.wait_budget);
+            if (!done) {
+                if (lane == 0) report_error(a.pool.status, DEV_ERR_TIMEOUT, 32, blockIdx.x, hh);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t acc = tmem + lb + (uint32_t)((i & 1) * D);
+            const int grow = m0 + 32 * q4 + lane;
+            const bool row_ok = grow < a.rows;
+            const bool is_q = hh < a.q_heads, is_k = !is_q && hh < a.q_heads + a.kv_heads;
+            const bool rope = is_q || is_k;
+            const int g = is_q ? 0 : (is_k ? hh - a.q_heads : hh - a.q_heads - a.kv_heads);
+            const int b = row_ok ? grow / a.tokens : 0, t = row_ok ? grow - b * a.tokens : 0;
+            float theta = row_ok ? (float)a.positions[grow] : 0.0f;
+            // the angle of this warp's first pair: ggml's float32 recurrence, advanced over the other part's pairs
+            for (int j = 0; j < part * (D / 4); ++j) theta = __fmul_rn(theta, a.theta_scale);
+            // destination of this row: q_out row, a suffix-slot tile row (swizzled), or a row-major K / V row
+            uint8_t *dst = nullptr;
+            bool slot = false;
+            if (row_ok) {
+                if (is_q) {
+                    dst = (uint8_t *)(a.q_out + ((int64_t)grow * a.q_heads + hh) * D);
+                } else if (a.to_slot) {
+                    const int seq = a.seq_ids[b];
+                    if (seq < 0 || seq >= a.pool.max_seqs) {
+                        report_error(a.pool.status, DEV_ERR_BAD_SEQ, b, seq, 6);
+                    } else {
+                        dst = a.pool.suffix + suffix_tile_index(a.pool, a.layer, seq, is_k ? 0 : 1, g) * a.pool.suffix_tile_bytes;
+                        slot = true;
+                    }
                 } else {
-                    o0[i] = x0;
-                    o1[i] = x1;
+                    dst = (uint8_t *)((is_k ? a.k_out : a.v_out) + ((int64_t)grow * a.kv_heads + g) * D);
                 }
             }
-            if (dst) {
+#pragma unroll 1
+            for (int c0 = part * (D / 4); c0 < (part + 1) * (D / 4); c0 += 16) {
+                uint32_t lo[16], hi[16];
+                tmem_load16x2(acc + (uint32_t)c0, acc + (uint32_t)(c0 + D / 2), lo, hi);
+                float o0[16], o1[16];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const float *o = half ? o1 : o0;
-                    const int c = c0 + half * (D / 2);
+                for (int j = 0; j < 16; ++j) {
+                    const float x0 = __uint_as_float(lo[j]), x1 = __uint_as_float(hi[j]);
+                    if (rope) {
+                        float sn, cs;
+                        rope_sincos(theta, sn, cs);
+                        o0[j] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+                        o1[j] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+                        theta = __fmul_rn(theta, a.theta_scale);
+                    } else {
+                        o0[j] = x0;
+                        o1[j] = x1;
+                    }
+                }
+                if (dst) {
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {  // 8 values = one 16-byte unit
-                        uint32_t w[4];
+                    for (int half = 0; half < 2; ++half) {
+                        const float *o = half ? o1 : o0;
+                        const int c = c0 + half * (D / 2);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * u + 2 * e], o[8 * u + 2 * e + 1]);
-                            w[e] = *(const uint32_t *)&b2;
+                        for (int u = 0; u < 2; ++u) {  // 8 values = one 16-byte unit
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * u + 2 * e], o[8 * u + 2 * e + 1]);
+                                w[e] = *(const uint32_t *)&b2;
+                            }
+                            const uint32_t off = slot ? tile_elem_off(t, c + 8 * u, D, W) : (uint32_t)(c + 8 * u) * 2u;
+                            *(uint4 *)(dst + off) = make_uint4(w[0], w[1], w[2], w[3]);
                         }
-                        const uint32_t off = slot ? tile_elem_off(t, c + 8 * u, D, W) : (uint32_t)(c + 8 * u) * 2u;
-                        *(uint4 *)(dst + off) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(2 * NS + 2 + (i & 1)));  // the accumulator may take the next tile
         }
     }
     __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, D);
+    if (warp == 1) tmem_dealloc(tmem, 2 * D);
 }
 
 // 2-D tensor map of a row-major bf16 matrix [rows][cols] with boxes of 64 columns x box_rows rows, 128-byte
@@ -265,8 +304,11 @@ int launch_project(const ProjArgs &a, const void *x, const void *wq, const void 
             return EKV_ERR_CUDA;
         attr_done[dev] = 1;
     }
-    const dim3 grid((unsigned)((a.rows + kPBM - 1) / kPBM), (unsigned)(a.q_heads + 2 * a.kv_heads));
-    project_qkv_kernel<D><<<grid, C::THREADS, C::SMEM, s>>>(a, xm, qm, km, vm);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int m_tiles = (a.rows + kPBM - 1) / kPBM;
+    const int n_tiles = m_tiles * (a.q_heads + 2 * a.kv_heads);
+    project_qkv_kernel<D><<<std::min(n_tiles, sms), C::THREADS, C::SMEM, s>>>(a, m_tiles, xm, qm, km, vm);
     if (cudaGetLastError() != cudaSuccess) return EKV_ERR_CUDA;
     note_launches(1);
     return EKV_OK;
