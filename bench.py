@@ -658,7 +658,8 @@ def run_other(args, cfg):
             "unit": "tok/s" if cfg["kind"] == "proj" else "query-tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 MMA, f32 accumulate",
-            "data": "synthetic", "config": {"workload": args.config, "description": cfg["desc"],
+            "data": "synthetic", "config": {"workload": args.config if not args.batch else f"{args.config}@batch{args.batch}",
+                                            "description": cfg["desc"],
                                             "batch_per_gpu": wl.B,
                                             "parallelism": f"{'episode' if cfg['kind'] == 'lingbot' else 'request'}"
                                                            f"-sharded x{world}"},
@@ -822,7 +823,10 @@ def main():
                 print(json.dumps({"impl": "reference", "unavailable": f"{args.config}: the reference arm times the "
                                   "default pi0.5 workload only"}))
             return
-        run_other(args, OTHER_CONFIGS[args.config])
+        cfg = dict(OTHER_CONFIGS[args.config])
+        if args.batch:
+            cfg["batch"] = args.batch  # a profiling case, not the headline config
+        run_other(args, cfg)
         return
     cfg = dict(CONFIGS[args.config])
     args.workload = args.config

@@ -35,27 +35,61 @@ __device__ __forceinline__ bool prefix_dest(const PoolView &p, int layer, int se
     return blk >= 0;
 }
 
-// bf16 append: one thread moves 8 elements (16 bytes) of one (row, kv, head).
+// Rows per CTA of the bf16 append kernels, and 16-byte loads a lane keeps in flight before its stores.
+constexpr int kRowsPerCta = 16;
+constexpr int kUnitsPerLane = 8;
+
+// Move one (row, K|V) of kv_heads x head_dim bf16 elements from a packed source row to the swizzled
+// tiles at row `rib` (tile of head h at tile0 + h * tile_bytes), by one warp: consecutive lanes take
+// consecutive 16-byte units of the source row, up to kUnitsPerLane loads in flight per lane.
+__device__ __forceinline__ void move_row_bf16(const uint4 *__restrict__ src, uint8_t *tile0, int64_t tile_bytes,
+                                              int rib, const PoolView &p, int lane) {
+    const int dh8 = p.head_dim / 8, upk = p.kv_heads * dh8;
+    for (int u0 = lane; u0 < upk; u0 += 32 * kUnitsPerLane) {
+        uint4 val[kUnitsPerLane];
+#pragma unroll
+        for (int j = 0; j < kUnitsPerLane; ++j)
+            if (u0 + 32 * j < upk) val[j] = __ldg(src + u0 + 32 * j);
+#pragma unroll
+        for (int j = 0; j < kUnitsPerLane; ++j) {
+            const int u = u0 + 32 * j;
+            if (u < upk) {
+                const int h = u / dh8, d0 = (u - h * dh8) * 8;
+                *(uint4 *)(tile0 + h * tile_bytes + tile_elem_off(rib, d0, p.head_dim, p.swz_bytes)) = val[j];
+            }
+        }
+    }
+}
+
+// bf16 append: a CTA moves kRowsPerCta rows of one batch element. One thread per row resolves the
+// row's destination block (sequence length and block-table reads) into shared memory; then each warp
+// takes (row, K|V) pairs and moves them with move_row_bf16.
 __global__ void append_bf16_kernel(PoolView p, int layer, const int32_t *__restrict__ seq_ids,
                                    const int32_t *__restrict__ dst_pos, const int32_t *__restrict__ n_rows,
                                    const int32_t *__restrict__ src_row, int max_rows,
                                    const uint4 *__restrict__ k, const uint4 *__restrict__ v) {
+    __shared__ int s_blk[kRowsPerCta], s_rib[kRowsPerCta];
     const int b = blockIdx.y;
-    const int units_per_row = 2 * p.kv_heads * (p.head_dim / 8);
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int r = (int)(idx / units_per_row);
-    if (r >= max_rows || r >= n_rows[b]) return;
-    const int u = (int)(idx - (int64_t)r * units_per_row);
-    const int kv = u / (p.kv_heads * (p.head_dim / 8));
-    const int rem = u - kv * (p.kv_heads * (p.head_dim / 8));
-    const int h = rem / (p.head_dim / 8);
-    const int d0 = (rem - h * (p.head_dim / 8)) * 8;
-    int blk, rib;
-    if (!prefix_dest(p, layer, seq_ids[b], dst_pos[b] + r, blk, rib)) return;
-    const int64_t src = (((int64_t)src_row[b] + r) * p.kv_heads + h) * p.head_dim + d0;
-    const uint4 val = (kv ? v : k)[src / 8];
-    uint8_t *tile = p.prefix + prefix_tile_index(p, layer, blk, kv, h) * p.tile_bytes;
-    *(uint4 *)(tile + tile_elem_off(rib, d0, p.head_dim, p.swz_bytes)) = val;
+    const int r0 = blockIdx.x * kRowsPerCta;
+    const int nr = min(kRowsPerCta, min(max_rows, n_rows[b]) - r0);
+    if (nr <= 0) return;
+    if ((int)threadIdx.x < nr) {
+        int blk, rib = 0;
+        if (!prefix_dest(p, layer, seq_ids[b], dst_pos[b] + r0 + (int)threadIdx.x, blk, rib)) blk = -1;
+        s_blk[threadIdx.x] = blk;
+        s_rib[threadIdx.x] = rib;
+    }
+    __syncthreads();
+    const int upk = p.kv_heads * (p.head_dim / 8);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int64_t row0 = (int64_t)src_row[b] + r0;
+    for (int pr = warp; pr < 2 * nr; pr += blockDim.x / 32) {
+        const int r = pr >> 1, kv = pr & 1;
+        const int blk = s_blk[r];
+        if (blk < 0) continue;
+        move_row_bf16((kv ? v : k) + (row0 + r) * upk, p.prefix + prefix_tile_index(p, layer, blk, kv, 0) * p.tile_bytes,
+                      p.tile_bytes, s_rib[r], p, lane);
+    }
 }
 
 // Q8_0 append: one thread quantises one 32-element group of one (row, kv, head).
@@ -117,29 +151,26 @@ __global__ void append_q8_kernel(PoolView p, int layer, const int32_t *__restric
     *sdst = __half_as_ushort(__float2half_rn(d));
 }
 
-// Suffix slot write (bf16, swizzled tile of suffix_rows rows).
+// Suffix slot write (bf16, swizzled tile of suffix_rows rows): a CTA moves kRowsPerCta rows of one
+// batch element, one warp per (row, K|V) pair at a time.
 __global__ void append_suffix_kernel(PoolView p, int layer, const int32_t *__restrict__ seq_ids, int n_rows,
                                      const uint4 *__restrict__ k, const uint4 *__restrict__ v) {
     const int b = blockIdx.y;
-    const int per_head = p.head_dim / 8;
-    const int units_per_row = 2 * p.kv_heads * per_head;
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int r = (int)(idx / units_per_row);
-    if (r >= n_rows) return;
-    const int u = (int)(idx - (int64_t)r * units_per_row);
-    const int kv = u / (p.kv_heads * per_head);
-    const int rem = u - kv * (p.kv_heads * per_head);
-    const int h = rem / per_head;
-    const int d0 = (rem - h * per_head) * 8;
+    const int r0 = blockIdx.x * kRowsPerCta;
+    const int nr = min(kRowsPerCta, n_rows - r0);
     const int seq = seq_ids[b];
     if (seq < 0 || seq >= p.max_seqs) {
-        report_error(p.status, DEV_ERR_BAD_SEQ, seq, r, 1);
+        if (threadIdx.x == 0) report_error(p.status, DEV_ERR_BAD_SEQ, seq, r0, 1);
         return;
     }
-    const int64_t src = (((int64_t)b * n_rows + r) * p.kv_heads + h) * p.head_dim + d0;
-    const uint4 val = (kv ? v : k)[src / 8];
-    uint8_t *tile = p.suffix + suffix_tile_index(p, layer, seq, kv, h) * p.suffix_tile_bytes;
-    *(uint4 *)(tile + tile_elem_off(r, d0, p.head_dim, p.swz_bytes)) = val;
+    const int upk = p.kv_heads * (p.head_dim / 8);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    for (int pr = warp; pr < 2 * nr; pr += blockDim.x / 32) {
+        const int r = pr >> 1, kv = pr & 1;
+        move_row_bf16((kv ? v : k) + ((int64_t)b * n_rows + r0 + r) * upk,
+                      p.suffix + suffix_tile_index(p, layer, seq, kv, 0) * p.suffix_tile_bytes, p.suffix_tile_bytes,
+                      r0 + r, p, lane);
+    }
 }
 
 // Gather of bf16 tiles (prefix or suffix) back to [rows][kv_heads][head_dim].
@@ -243,8 +274,7 @@ int launch_append(const PoolView &p, int layer, int n_batch, const int32_t *seq_
     if (((uintptr_t)k | (uintptr_t)v) & 15) return EKV_ERR_INVALID_ARG;
     if (n_batch > 65535) return EKV_ERR_INVALID_ARG;
     if (p.dtype == EKV_DTYPE_BF16) {
-        const int64_t units = (int64_t)max_rows * 2 * p.kv_heads * (p.head_dim / 8);
-        append_bf16_kernel<<<dim3(grid_for(units), n_batch), kThreads, 0, s>>>(
+        append_bf16_kernel<<<dim3((max_rows + kRowsPerCta - 1) / kRowsPerCta, n_batch), kThreads, 0, s>>>(
             p, layer, seq_ids, dst_pos, n_rows, src_row, max_rows, (const uint4 *)k, (const uint4 *)v);
     } else {
         const int64_t units = (int64_t)max_rows * 2 * p.kv_heads * (p.head_dim / 32);
@@ -259,9 +289,8 @@ int launch_append_suffix(const PoolView &p, int layer, int n_batch, const int32_
                          const void *k, const void *v, cudaStream_t s) {
     if (((uintptr_t)k | (uintptr_t)v) & 15) return EKV_ERR_INVALID_ARG;
     if (n_batch > 65535 || p.suffix_rows == 0) return EKV_ERR_INVALID_ARG;
-    const int64_t units = (int64_t)n_rows * 2 * p.kv_heads * (p.head_dim / 8);
-    append_suffix_kernel<<<dim3(grid_for(units), n_batch), kThreads, 0, s>>>(p, layer, seq_ids, n_rows,
-                                                                             (const uint4 *)k, (const uint4 *)v);
+    append_suffix_kernel<<<dim3((n_rows + kRowsPerCta - 1) / kRowsPerCta, n_batch), kThreads, 0, s>>>(
+        p, layer, seq_ids, n_rows, (const uint4 *)k, (const uint4 *)v);
     note_launches(1);
     return launch_status();
 }
