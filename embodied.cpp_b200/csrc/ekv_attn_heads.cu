@@ -451,15 +451,28 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                         mma_ts_x4<false>(od, *reinterpret_cast<const uint32_t(*)[4]>(pv_a + 4 * h),
                                          *reinterpret_cast<const uint64_t(*)[4]>(bv + 4 * h), idO,
                                          (j > 0 || h > 0) ? 1u : 0u);
-                } else {  // a suffix tile of at most 48 keys: fewer key steps per head
-#pragma unroll
-                    for (int h = 0; h < G; ++h)
-#pragma unroll
-                        for (int kk = 0; kk < 3; ++kk)
-                            if (kk < nk)
-                                mma_ts(od, pv_a[h * 4 + kk], bv[h * 4 + kk], idO, (j > 0 || h > 0 || kk > 0) ? 1u : 0u);
+                } else {  // a suffix tile of at most 48 keys: nk key steps per head, all heads back to back
+                    static_assert(G == 4, "four heads per unit");
+                    const uint32_t acc0 = j > 0 ? 1u : 0u;
+                    if (nk == 1) {
+                        const uint32_t a4[4] = {pv_a[0], pv_a[4], pv_a[8], pv_a[12]};
+                        const uint64_t b4[4] = {bv[0], bv[4], bv[8], bv[12]};
+                        mma_ts_x4<false>(od, a4, b4, idO, acc0);
+                    } else if (nk == 2) {
+                        const uint32_t a8[8] = {pv_a[0], pv_a[1], pv_a[4], pv_a[5], pv_a[8], pv_a[9], pv_a[12], pv_a[13]};
+                        const uint64_t b8[8] = {bv[0], bv[1], bv[4], bv[5], bv[8], bv[9], bv[12], bv[13]};
+                        mma_ts_x8(od, a8, b8, idO, acc0);
+                    } else {
+                        const uint32_t a4[4] = {pv_a[0], pv_a[1], pv_a[2], pv_a[4]};
+                        const uint64_t b4[4] = {bv[0], bv[1], bv[2], bv[4]};
+                        const uint32_t a8[8] = {pv_a[5], pv_a[6], pv_a[8], pv_a[9], pv_a[10], pv_a[12], pv_a[13], pv_a[14]};
+                        const uint64_t b8[8] = {bv[5], bv[6], bv[8], bv[9], bv[10], bv[12], bv[13], bv[14]};
+                        mma_ts_x4<false>(od, a4, b4, idO, acc0);
+                        mma_ts_x8(od, a8, b8, idO, 1u);
+                    }
                 }
                 mma_commit(bar(HB_VE + s));  // P.V(t) done: V stage and P buffers free, O updated
+                if (t < 50) TRACE(150 + t);
                 return true;
             };
             int t = 0;
@@ -468,6 +481,7 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                     ok = false;
                     break;
                 }
+                if (u < 50) TRACE(550 + u);
                 const HPlan &pl = plans[u & 3];
                 const int n = pl.np + pl.ns;
                 if (n == 0) {  // no tiles: the epilogue writes zeros once the unit's O buffer is free

@@ -35,8 +35,11 @@ __device__ __forceinline__ bool prefix_dest(const PoolView &p, int layer, int se
     return blk >= 0;
 }
 
-// Rows per CTA of the bf16 append kernels, and 16-byte loads a lane keeps in flight before its stores.
+// Rows per CTA of the bf16 prefix append and of the suffix append (a suffix is a few dozen rows per
+// request, so its CTAs take fewer rows: one warp per (row, K|V) pair keeps enough CTAs in flight), and
+// 16-byte loads a lane keeps in flight before its stores.
 constexpr int kRowsPerCta = 16;
+constexpr int kSuffixRowsPerCta = 4;
 constexpr int kUnitsPerLane = 8;
 
 // Move one (row, K|V) of kv_heads x head_dim bf16 elements from a packed source row to the swizzled
@@ -151,13 +154,13 @@ __global__ void append_q8_kernel(PoolView p, int layer, const int32_t *__restric
     *sdst = __half_as_ushort(__float2half_rn(d));
 }
 
-// Suffix slot write (bf16, swizzled tile of suffix_rows rows): a CTA moves kRowsPerCta rows of one
-// batch element, one warp per (row, K|V) pair at a time.
+// Suffix slot write (bf16, swizzled tile of suffix_rows rows): a CTA moves kSuffixRowsPerCta rows of one
+// batch element, one warp per (row, K|V) pair.
 __global__ void append_suffix_kernel(PoolView p, int layer, const int32_t *__restrict__ seq_ids, int n_rows,
                                      const uint4 *__restrict__ k, const uint4 *__restrict__ v) {
     const int b = blockIdx.y;
-    const int r0 = blockIdx.x * kRowsPerCta;
-    const int nr = min(kRowsPerCta, n_rows - r0);
+    const int r0 = blockIdx.x * kSuffixRowsPerCta;
+    const int nr = min(kSuffixRowsPerCta, n_rows - r0);
     const int seq = seq_ids[b];
     if (seq < 0 || seq >= p.max_seqs) {
         if (threadIdx.x == 0) report_error(p.status, DEV_ERR_BAD_SEQ, seq, r0, 1);
@@ -289,7 +292,7 @@ int launch_append_suffix(const PoolView &p, int layer, int n_batch, const int32_
                          const void *k, const void *v, cudaStream_t s) {
     if (((uintptr_t)k | (uintptr_t)v) & 15) return EKV_ERR_INVALID_ARG;
     if (n_batch > 65535 || p.suffix_rows == 0) return EKV_ERR_INVALID_ARG;
-    append_suffix_kernel<<<dim3((n_rows + kRowsPerCta - 1) / kRowsPerCta, n_batch), kThreads, 0, s>>>(
+    append_suffix_kernel<<<dim3((n_rows + kSuffixRowsPerCta - 1) / kSuffixRowsPerCta, n_batch), kThreads, 0, s>>>(
         p, layer, seq_ids, n_rows, (const uint4 *)k, (const uint4 *)v);
     note_launches(1);
     return launch_status();

@@ -399,6 +399,27 @@ __device__ __forceinline__ void mma_ts_x4(uint32_t d_tmem, const uint32_t (&a)[4
     }
 }
 
+// Eight tcgen05.mma (cta_group::1) back to back with A in tensor memory (a[0..7]) and B in shared memory
+// (descriptors b[0..7]); the first accumulates into D only when acc0 != 0, the others always.
+__device__ __forceinline__ void mma_ts_x8(uint32_t d_tmem, const uint32_t (&a)[8], const uint64_t (&b)[8], uint32_t idesc,
+                                          uint32_t acc0) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t"
+        "setp.ne.b32 p, %18, 0;\n\t"
+        "setp.eq.b32 t, %18, %18;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %9, %17, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %10, %17, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %11, %17, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %12, %17, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %13, %17, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %14, %17, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %15, %17, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %16, %17, t;\n\t}" ::"r"(d_tmem),
+        "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]), "l"(b[0]), "l"(b[1]),
+        "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "r"(idesc), "r"(acc0)
+        : "memory");
+}
+
 // Four tcgen05.mma back to back with both operands in shared memory (descriptors a[0..3], b[0..3]);
 // the first accumulates into D only when acc0 != 0, the others always.
 template <bool PAIR>
