@@ -87,7 +87,10 @@ typedef struct ekv_pool_info {
 int ekv_pool_create(const ekv_pool_config *cfg, ekv_pool **out);
 int ekv_pool_destroy(ekv_pool *pool);
 int ekv_pool_get_info(const ekv_pool *pool, ekv_pool_info *info);
-/* Read (and clear) the device status word: *code receives EKV_OK or the first kernel error. */
+/* Read (and clear) the device status word: *code receives EKV_OK or the first kernel error:
+ * 1 block-table entry outside the pool, 2 sequence id outside [0, max_seqs), 3 position outside the
+ * sequence's blocks, 4 a bounded internal wait ran out, 5 a bf16 query or suffix value beyond the f16
+ * range met an f16 operand (Q8_0 pools compute in f16). */
 int ekv_pool_status(ekv_pool *pool, int32_t *code, ekv_stream_t stream);
 /* Upload host-side block tables / lengths changed since the last sync (stream-ordered). */
 int ekv_pool_sync(ekv_pool *pool, ekv_stream_t stream);
