@@ -648,10 +648,14 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                 else
                     vb = vis_word(m, suffix, w0, lane, pvalid, sb, se, a.suffix_len, n_prefix);
                 const bool all_vis = __all_sync(0xffffffffu, vb == 0xffffffffu);
+                // no key of this warp's 32 visible to any of its rows (a short suffix tile, the end of a
+                // span): no maximum, and P is zero without exponentials
+                const bool none_vis = __all_sync(0xffffffffu, vb == 0u);
                 float mx[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-                if (all_vis) {
+                if (none_vis) {
+                } else if (all_vis) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(s0[i]));
@@ -712,7 +716,10 @@ __global__ void __launch_bounds__(HCfg<D>::THREADS, 1)
                 const bool all_p = all_vis && __all_sync(0xffffffffu, m_used != -INFINITY);
                 float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 uint32_t pw[16];
-                if (all_p) {
+                if (none_vis) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) pw[i] = 0u;
+                } else if (all_p) {
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float x0 = ex2(fmaf(__uint_as_float(s0[2 * i]), a.scale_log2, neg_m));
