@@ -1511,7 +1511,8 @@ extern "C" int ekv_debug_set_trace(unsigned long long *buf) {
     if (cudaMemcpyToSymbol(ekv::c_trace, &buf, sizeof(buf)) != cudaSuccess) return -2;
     if (ekv::pair_debug_set_trace(buf)) return -2;
     if (ekv::pair128_debug_set_trace(buf)) return -2;
-    return ekv::heads_debug_set_trace(buf);
+    if (ekv::heads_debug_set_trace(buf)) return -2;
+    return ekv::project_debug_set_trace(buf);
 }
 namespace ekv {
 #endif

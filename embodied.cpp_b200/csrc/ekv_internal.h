@@ -117,6 +117,7 @@ int launch_merge_splits(const AttnArgs &a, int n_qtiles, cudaStream_t s);
 int pair_debug_set_trace(unsigned long long *buf);
 int pair128_debug_set_trace(unsigned long long *buf);
 int heads_debug_set_trace(unsigned long long *buf);
+int project_debug_set_trace(unsigned long long *buf);
 #endif
 
 }  // namespace ekv

@@ -102,6 +102,23 @@ def test_row_major_outputs_and_ragged_rows(D, Hq, Hkv, B, T, p0):
     agree(v, ev.reshape(B, T, Hkv, D))
 
 
+def test_outputs_16_byte_aligned_only():
+    """q_out / k_out / v_out that are 16-byte but not 32-byte aligned (views 8 elements into larger buffers)
+    take the 16-byte store path and give the same bits as 32-byte aligned outputs."""
+    B, T, hidden, Hq, Hkv, D = 2, 40, 256, 4, 2, 128
+    f, x, wq, wk, wv, pos = setup(B, T, hidden, Hq, Hkv, D, [20, 30], 77)
+    q_a, k_a, v_a = run(f, x, wq, wk, wv, pos, T=T, Hq=Hq, row_major=True)
+    bufs = [torch.full((B * T * h * D + 8,), float("nan"), dtype=torch.bfloat16, device="cuda") for h in (Hq, Hkv, Hkv)]
+    q_u, k_u, v_u = (b_[8:].view(B, T, h, D) for b_, h in zip(bufs, (Hq, Hkv, Hkv)))
+    assert q_u.data_ptr() % 32 == 16
+    ekv.project_qkv_rope(f.pool, 0, f.seq_ids, x.cuda(), wq.cuda(), wk.cuda(), wv.cuda(), torch.tensor(pos, device="cuda"),
+                         10000.0, q_u, k_u, v_u, tokens=T, q_heads=Hq)
+    torch.cuda.synchronize()
+    assert f.pool.status() == 0
+    for got, want in ((q_u, q_a), (k_u, k_a), (v_u, v_a)):
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
 @pytest.mark.parametrize("case", ["hidden", "tokens", "align", "one_of_kv"])
 def test_rejects_bad_arguments(case):
     B, T, hidden, Hq, Hkv, D = 2, 8, 128, 2, 1, 64
