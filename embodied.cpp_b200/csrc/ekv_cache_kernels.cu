@@ -64,17 +64,17 @@ __device__ __forceinline__ void move_row_bf16(const uint4 *__restrict__ src, uin
     }
 }
 
-// bf16 append: a CTA moves kRowsPerCta rows of one batch element. One thread per row resolves the
-// row's destination block (sequence length and block-table reads) into shared memory; then each warp
-// takes (row, K|V) pairs and moves them with move_row_bf16.
+// bf16 append: a CTA moves `rows` (at most kRowsPerCta) rows of one batch element. One thread per row
+// resolves the row's destination block (sequence length and block-table reads) into shared memory; then
+// each warp takes (row, K|V) pairs and moves them with move_row_bf16.
 __global__ void append_bf16_kernel(PoolView p, int layer, const int32_t *__restrict__ seq_ids,
                                    const int32_t *__restrict__ dst_pos, const int32_t *__restrict__ n_rows,
-                                   const int32_t *__restrict__ src_row, int max_rows,
+                                   const int32_t *__restrict__ src_row, int max_rows, int rows,
                                    const uint4 *__restrict__ k, const uint4 *__restrict__ v) {
     __shared__ int s_blk[kRowsPerCta], s_rib[kRowsPerCta];
     const int b = blockIdx.y;
-    const int r0 = blockIdx.x * kRowsPerCta;
-    const int nr = min(kRowsPerCta, min(max_rows, n_rows[b]) - r0);
+    const int r0 = blockIdx.x * rows;
+    const int nr = min(rows, min(max_rows, n_rows[b]) - r0);
     if (nr <= 0) return;
     if ((int)threadIdx.x < nr) {
         int blk, rib = 0;
@@ -277,8 +277,14 @@ int launch_append(const PoolView &p, int layer, int n_batch, const int32_t *seq_
     if (((uintptr_t)k | (uintptr_t)v) & 15) return EKV_ERR_INVALID_ARG;
     if (n_batch > 65535) return EKV_ERR_INVALID_ARG;
     if (p.dtype == EKV_DTYPE_BF16) {
-        append_bf16_kernel<<<dim3((max_rows + kRowsPerCta - 1) / kRowsPerCta, n_batch), kThreads, 0, s>>>(
-            p, layer, seq_ids, dst_pos, n_rows, src_row, max_rows, (const uint4 *)k, (const uint4 *)v);
+        // rows per CTA: 16, or fewer where that leaves under two CTAs per SM (a long chunk of one request)
+        int sms = 148, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        int rows = kRowsPerCta;
+        while (rows > 4 && (int64_t)((max_rows + rows - 1) / rows) * n_batch < 2 * sms) rows /= 2;
+        append_bf16_kernel<<<dim3((max_rows + rows - 1) / rows, n_batch), kThreads, 0, s>>>(
+            p, layer, seq_ids, dst_pos, n_rows, src_row, max_rows, rows, (const uint4 *)k, (const uint4 *)v);
     } else {
         const int64_t units = (int64_t)max_rows * 2 * p.kv_heads * (p.head_dim / 32);
         append_q8_kernel<<<dim3(grid_for(units), n_batch), kThreads, 0, s>>>(
