@@ -1567,10 +1567,13 @@ int launch_attention_tc(const AttnArgs &a, cudaStream_t s, TcKernel k) {
     }
     const bool pair = a.pool.head_dim == 256 && k != TcKernel::OneCta;
     if (pair && k == TcKernel::Pair) return launch_attention_pair128(a, s, ws, sm_count());
-    // bf16 pools: the 128-key pair kernel where the shape allows it. Q8_0 pools keep the 64-key pair
-    // kernel: with Q in shared memory, the N = 128 MMAs' operand reads leave too little shared-memory
-    // bandwidth for the in-place dequantisation of every tile.
-    if (pair && k == TcKernel::Auto && a.pool.dtype == EKV_DTYPE_BF16) {
+    // bf16 pools: the 128-key pair kernel for calls of at most 8 (request, 256-row tile) pair units, where
+    // its fewer, larger MMA groups shorten a latency-bound call (batch 1: 14.8 against 15.3 us); from 16
+    // units on the 64-key kernel is ahead (2-4% at batch 16-256). Q8_0 pools keep the 64-key pair kernel:
+    // with Q in shared memory, the N = 128 MMAs' operand reads leave too little shared-memory bandwidth
+    // for the in-place dequantisation of every tile.
+    const int64_t pair_units = (int64_t)a.n_batch * a.pool.kv_heads * ((a.q_tokens * a.group + 255) / 256);
+    if (pair && k == TcKernel::Auto && a.pool.dtype == EKV_DTYPE_BF16 && pair_units <= 8) {
         const int rc = launch_attention_pair128(a, s, ws, sm_count());
         if (rc != EKV_ERR_UNSUPPORTED) return rc;
     }

@@ -246,8 +246,9 @@ int ekv_attention_noalloc(ekv_pool *pool, const ekv_attn_params *p, const void *
                           ekv_stream_t stream);
 
 #define EKV_ALGO_TC 0      /* tcgen05 tensor cores (default): CTA pairs for head_dim 256 (128-key
-                              tiles for bf16 pools where EKV_ALGO_TC_PAIR supports the shape,
-                              64-key tiles otherwise), the one-CTA kernel for other head dims  */
+                              tiles for bf16 calls of at most 8 pairs of 256 query rows where
+                              EKV_ALGO_TC_PAIR supports the shape, 64-key tiles otherwise), the
+                              one-CTA kernel for other head dims                              */
 #define EKV_ALGO_SIMT 1    /* one-warp-per-row CUDA-core kernel, kept as a GPU cross-check   */
 #define EKV_ALGO_TC_PAIR 2 /* head_dim 256 on CTA pairs (tcgen05 cta_group::2, 256 query rows
                               per pair, each K/V tile split between the two CTAs) with 128-key
