@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(PCfg<D>::THREADS, 1)
         // 128 h + 32 (warp & 3) + lane; dimension pairs [0, D/4) for (e >> 2) even, [D/4, D/2) for odd ----
         const int q4 = warp & 3, part = ((warp - 2) >> 2) & 1, mh = (warp - 2) >> 3;
         const uint32_t lb = ((uint32_t)(32 * q4)) << 16;
-        const int W = a.pool.swz_bytes;
+        constexpr int W = 128;  // the pool's swizzle width at head_dim 64 / 128 / 256 (checked at launch)
         for (int i = 0; i < U; ++i) {
             const int tile = (int)blockIdx.x + i * (int)gridDim.x, m0 = (tile % m_tiles) * TROWS, hh = tile / m_tiles;
             const int bsel = i % NB;
@@ -294,12 +294,18 @@ __global__ void __launch_bounds__(PCfg<D>::THREADS, 1)
                         } else if (slot) {
                             // the swizzle keeps the two 16-byte units of an aligned 32-byte group together, in
                             // either order: one 32-byte store, halves swapped where the row's swizzle swaps them
+                            // (a select, not a branch: odd and even rows of a warp take the same path)
                             const uint32_t off0 = tile_elem_off(t, c, D, W), off1 = tile_elem_off(t, c + 8, D, W);
-                            if (off1 == off0 + 16u && ((uintptr_t)(dst + off0) & 31u) == 0u) {
-                                st_global_32B(dst + off0, w);
-                            } else if (off0 == off1 + 16u && ((uintptr_t)(dst + off1) & 31u) == 0u) {
-                                const uint32_t sw[8] = {w[4], w[5], w[6], w[7], w[0], w[1], w[2], w[3]};
-                                st_global_32B(dst + off1, sw);
+                            const uint32_t lo_off = min(off0, off1);
+                            if (max(off0, off1) == lo_off + 16u && ((uintptr_t)(dst + lo_off) & 31u) == 0u) {
+                                const bool sw = off0 > off1;
+                                uint32_t x[8];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    x[e] = sw ? w[4 + e] : w[e];
+                                    x[4 + e] = sw ? w[e] : w[4 + e];
+                                }
+                                st_global_32B(dst + lo_off, x);
                             } else {
                                 *(uint4 *)(dst + off0) = make_uint4(w[0], w[1], w[2], w[3]);
                                 *(uint4 *)(dst + off1) = make_uint4(w[4], w[5], w[6], w[7]);
@@ -346,6 +352,7 @@ bool make_rows_map(const void *base, int64_t rows, int64_t cols, int box_rows, C
 template <int D>
 int launch_project(const ProjArgs &a, const void *x, const void *wq, const void *wk, const void *wv, cudaStream_t s) {
     using C = PCfg<D>;
+    if (a.pool.swz_bytes != 128) return EKV_ERR_UNSUPPORTED;
     CUtensorMap xm, qm, km, vm;
     if (!make_rows_map(x, a.rows, a.hidden, C::MH * kPBM, &xm) || !make_rows_map(wq, (int64_t)a.q_heads * D, a.hidden, D, &qm) ||
         !make_rows_map(wk, (int64_t)a.kv_heads * D, a.hidden, D, &km) ||
